@@ -1,0 +1,185 @@
+// C-ABI layer (include/axq.h): argument validation, status/message
+// handling in the reference's Expected<void>/Error style, and dispatch to the
+// kernels.  Nothing here allocates device memory.
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "axq_common.cuh"
+#include "axq_internal.h"
+
+namespace axq {
+
+namespace {
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+    g_last_error = msg;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+    return fail(AXQ_ERR_CUDA, std::string(where) + ": " + cudaGetErrorString(e));
+}
+
+const char* fmt_name(int f) {
+    switch (f) {
+        case F_Q8_0: return "Q8_0";
+        case F_Q4_0: return "Q4_0";
+        case F_Q2_K: return "Q2_K";
+        case F_Q3_K: return "Q3_K";
+        case F_Q4_K: return "Q4_K";
+        case F_Q5_K: return "Q5_K";
+        case F_Q6_K: return "Q6_K";
+        default: return "?";
+    }
+}
+
+bool known_fmt(int f) { return host_block_elems(f) != 0; }
+
+// A kernel handed a pageable host pointer or another device's memory would
+// fault; reject those here instead.
+int check_ptr(const void* p, const char* what, const char* fn) {
+    if (!p) return fail(AXQ_ERR_INVALID, std::string(fn) + ": " + what + " is NULL");
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, fn);
+    cudaPointerAttributes at{};
+    e = cudaPointerGetAttributes(&at, p);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(AXQ_ERR_INVALID, std::string(fn) + ": " + what + " is not a CUDA-accessible pointer");
+    }
+    if (at.type == cudaMemoryTypeDevice) {
+        if (at.device != dev)
+            return fail(AXQ_ERR_INVALID, std::string(fn) + ": " + what + " lives on device " +
+                                             std::to_string(at.device) + " but the current device is " +
+                                             std::to_string(dev));
+        return AXQ_OK;
+    }
+    if (at.type == cudaMemoryTypeManaged || (at.type == cudaMemoryTypeHost && at.devicePointer != nullptr)) return AXQ_OK;
+    return fail(AXQ_ERR_INVALID, std::string(fn) + ": " + what + " is host memory that the device cannot access");
+}
+
+constexpr size_t kStatusBytes = 256;  // status words at the front of a workspace
+
+}  // namespace
+
+int device_sm_count() {
+    static int cache[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (cache[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        cache[dev] = n;
+    }
+    return cache[dev];
+}
+
+}  // namespace axq
+
+using namespace axq;
+
+extern "C" {
+
+const char* axq_last_error(void) { return g_last_error.c_str(); }
+
+int axq_version(void) { return 100; }
+
+size_t axq_quantized_size(size_t numel, int fmt) {
+    int be = host_block_elems(fmt);
+    if (!be) return 0;
+    return (numel + be - 1) / be * static_cast<size_t>(host_block_bytes(fmt));
+}
+
+size_t axq_quantized_size_2d(int64_t rows, int64_t cols, int fmt) {
+    int be = host_block_elems(fmt);
+    if (!be || rows < 0 || cols < 0) return 0;
+    return static_cast<size_t>(rows) * static_cast<size_t>((cols + be - 1) / be) * host_block_bytes(fmt);
+}
+
+int axq_quantize(int fmt, const float* src, void* dst, int64_t rows, int64_t cols, axq_stream_t stream) {
+    const char* fn = "axq_quantize";
+    if (!known_fmt(fmt)) return fail(AXQ_ERR_UNSUPPORTED, std::string(fn) + ": unsupported format " + std::to_string(fmt));
+    if (rows < 0 || cols < 0) return fail(AXQ_ERR_INVALID, std::string(fn) + ": negative shape");
+    if (rows == 0 || cols == 0) return AXQ_OK;
+    if (int r = check_ptr(src, "src", fn)) return r;
+    if (int r = check_ptr(dst, "dst", fn)) return r;
+    if (reinterpret_cast<uintptr_t>(src) % 4) return fail(AXQ_ERR_INVALID, std::string(fn) + ": src must be 4-byte aligned");
+    cudaError_t e = pack_dispatch(fmt, src, dst, rows, cols, reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, fn);
+    return AXQ_OK;
+}
+
+int axq_dequantize(int fmt, const void* src, float* dst, int64_t rows, int64_t cols, axq_stream_t stream) {
+    const char* fn = "axq_dequantize";
+    if (!known_fmt(fmt)) return fail(AXQ_ERR_UNSUPPORTED, std::string(fn) + ": unsupported format " + std::to_string(fmt));
+    if (rows < 0 || cols < 0) return fail(AXQ_ERR_INVALID, std::string(fn) + ": negative shape");
+    if (rows == 0 || cols == 0) return AXQ_OK;
+    if (int r = check_ptr(src, "src", fn)) return r;
+    if (int r = check_ptr(dst, "dst", fn)) return r;
+    if (reinterpret_cast<uintptr_t>(dst) % 4) return fail(AXQ_ERR_INVALID, std::string(fn) + ": dst must be 4-byte aligned");
+    cudaError_t e = dequant_dispatch(fmt, src, dst, rows, cols, reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, fn);
+    return AXQ_OK;
+}
+
+size_t axq_matmul_workspace_size(int fmt, int64_t M, int64_t K, int64_t N) {
+    (void)M;
+    int be = host_block_elems(fmt);
+    if (!be || K < 0 || N < 0) return 0;
+    const int64_t Kp = (K + be - 1) / be * be;
+    return kStatusBytes + gemv_workspace_layout(Kp, N).total;
+}
+
+int axq_matmul(int fmt, const void* a_q, const float* b, float* out, int64_t M, int64_t K, int64_t N, unsigned flags,
+               void* workspace, size_t workspace_bytes, axq_stream_t stream) {
+    const char* fn = "axq_matmul";
+    if (!known_fmt(fmt)) return fail(AXQ_ERR_UNSUPPORTED, std::string(fn) + ": unsupported format " + std::to_string(fmt));
+    if (M < 0 || K < 0 || N < 0) return fail(AXQ_ERR_INVALID, std::string(fn) + ": negative shape");
+    if (flags & ~(AXQ_FLAG_B_TOKMAJOR | AXQ_FLAG_OUT_TOKMAJOR))
+        return fail(AXQ_ERR_INVALID, std::string(fn) + ": unknown flag bits");
+    if (M == 0 || N == 0) return AXQ_OK;
+    if (N > (int64_t(1) << 24) || M > (int64_t(1) << 31) || K > (int64_t(1) << 30))
+        return fail(AXQ_ERR_INVALID, std::string(fn) + ": shape too large");
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (K == 0) {
+        if (int r = check_ptr(out, "out", fn)) return r;
+        cudaError_t e = cudaMemsetAsync(out, 0, static_cast<size_t>(M * N) * 4, s);
+        return e == cudaSuccess ? AXQ_OK : cuda_fail(e, fn);
+    }
+    if (int r = check_ptr(a_q, "a_q", fn)) return r;
+    if (int r = check_ptr(b, "b", fn)) return r;
+    if (int r = check_ptr(out, "out", fn)) return r;
+    if (reinterpret_cast<uintptr_t>(b) % 4 || reinterpret_cast<uintptr_t>(out) % 4)
+        return fail(AXQ_ERR_INVALID, std::string(fn) + ": b and out must be 4-byte aligned");
+    const size_t need = axq_matmul_workspace_size(fmt, M, K, N);
+    if (!workspace || workspace_bytes < need)
+        return fail(AXQ_ERR_WORKSPACE, std::string(fn) + ": workspace of " + std::to_string(need) +
+                                           " bytes required (" + fmt_name(fmt) + ")");
+    if (int r = check_ptr(workspace, "workspace", fn)) return r;
+    if (reinterpret_cast<uintptr_t>(workspace) % 256)
+        return fail(AXQ_ERR_INVALID, std::string(fn) + ": workspace must be 256-byte aligned");
+    auto* ws = static_cast<uint8_t*>(workspace);
+    int* err = reinterpret_cast<int*>(ws);  // zeroed by the first kernel of the call
+    cudaError_t e = gemv_dispatch(fmt, a_q, b, out, M, K, N, static_cast<int>(flags), ws + kStatusBytes,
+                      workspace_bytes - kStatusBytes, err, s);
+    if (e != cudaSuccess) return cuda_fail(e, fn);
+    return AXQ_OK;
+}
+
+int axq_workspace_status(const void* workspace, axq_stream_t stream) {
+    const char* fn = "axq_workspace_status";
+    if (int r = check_ptr(workspace, "workspace", fn)) return r;
+    int flag = 0;
+    cudaError_t e = cudaMemcpyAsync(&flag, workspace, sizeof(int), cudaMemcpyDeviceToHost,
+                                    reinterpret_cast<cudaStream_t>(stream));
+    if (e == cudaSuccess) e = cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, fn);
+    if (flag) return fail(AXQ_ERR_TIMEOUT, std::string(fn) + ": a kernel gave up waiting on its copy pipeline");
+    return AXQ_OK;
+}
+
+}  // extern "C"

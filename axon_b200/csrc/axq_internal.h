@@ -1,0 +1,28 @@
+// Internal launch interfaces shared by the kernel translation units and the
+// C-ABI layer (axq_capi.cu).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "../../include/axq.h"
+
+namespace axq {
+
+// Multiprocessor count of the current device (cached per device).
+int device_sm_count();
+
+cudaError_t pack_dispatch(int fmt, const float* src, void* dst, int64_t rows, int64_t cols, cudaStream_t s);
+cudaError_t dequant_dispatch(int fmt, const void* src, float* dst, int64_t rows, int64_t cols, cudaStream_t s);
+
+// Workspace for the block-quantized activations of a GEMV-class matmul.
+struct GemvWorkspace {
+    size_t off_hi, off_lo, off_u, off_s8, total;
+};
+GemvWorkspace gemv_workspace_layout(int64_t Kp, int64_t ntok);
+
+cudaError_t gemv_dispatch(int fmt, const void* w, const float* x, float* out, int64_t M, int64_t K, int64_t N, int flags,
+                          void* ws, size_t ws_bytes, int* err, cudaStream_t s);
+
+}  // namespace axq

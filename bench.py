@@ -1,0 +1,400 @@
+"""Benchmark of the quantized GEMV path on B200.
+
+Workload (the largest configuration, the one sharded across GPUs): per GPU,
+y = x . W^T for W[28672 x 8192] packed in Q2_K, Q3_K and Q5_K (one matmul
+each per step; weights ~ N(0, 0.02^2) plus 0.1% outliers ~ N(0, 0.5^2)),
+x[1 x 8192] ~ N(0,1).  One step = the three GEMVs.  With N GPUs each rank
+holds its own 28672-row shard of a [28672*N x 8192] weight (weak scaling)
+and the outputs are all-gathered over NCCL.  The three packed matrices
+(340 MB per GPU) exceed the 126 MB L2, so no flush is needed between steps.
+
+Metric: packed-weight GB/s over all ranks (higher is better).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Under torchrun (N > 1) every rank runs; rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+ROWS, K_DIM, M_TOK = 28672, 8192, 1
+FORMATS = ("Q2_K", "Q3_K", "Q5_K")
+DOMINANT = "Q5_K"
+METRIC = "Quant matmul weight GB/s (GEMV), TOPS (GEMM) at 1/2/4/8 B200 vs AVX2 host"
+WORKLOAD = "low-bit large GEMV: y = x.W^T, W[28672x8192] in Q2_K, Q3_K, Q5_K per GPU, x[1x8192]"
+
+
+def packed_bytes(fmt: str, rows: int = ROWS, cols: int = K_DIM) -> int:
+    be = 256
+    bb = {"Q2_K": 84, "Q3_K": 110, "Q4_K": 144, "Q5_K": 176, "Q6_K": 210}[fmt]
+    return rows * ((cols + be - 1) // be) * bb
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d.get("hbm_gbs", 6650.0)), "measured"
+    return 6650.0, "fallback"
+
+
+def load_traffic():
+    """dram bytes per launch of the dominant kernel from the committed ncu
+    summary (profiles/traffic.json), or None."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        try:
+            with open(p) as f:
+                return json.load(f).get(f"gemv_{DOMINANT}")
+        except Exception:
+            return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples taken during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for n, v in zip(names, r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+# ------------------------------------------------------------------ CPU arms
+
+def cpu_pack_reference(fmt, W, threads):
+    import oracle
+    ref = oracle.ref()
+    out = np.empty(packed_bytes(fmt, W.shape[0], W.shape[1]), dtype=np.uint8)
+    if ref is not None:
+        rc = ref.lib.ref_quantize_threads(oracle.FORMATS[fmt], W.ctypes.data, W.shape[0], W.shape[1],
+                                          out.ctypes.data, threads)
+        if rc != 0:
+            raise RuntimeError("reference quantize failed")
+        return out
+    return oracle.orc().quantize(fmt, W)
+
+
+def make_weights_np(fmt_index, rows, cols, seed):
+    rng = np.random.default_rng(seed + fmt_index)
+    W = (rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(0.02))
+    m = rng.random((rows, cols), dtype=np.float32) < 0.001
+    W[m] = rng.standard_normal(int(m.sum()), dtype=np.float32) * np.float32(0.5)
+    return W
+
+
+class CpuArm:
+    """The reference's CPU matmul on the host cores: its own kernels compiled
+    from its sources (oracle/_ref, kind "reference"), or the C restatement
+    (kind "port") where that library is absent.  Rows are split across all
+    host threads (the reference kernels are single-threaded)."""
+
+    def __init__(self, packed, x, threads):
+        import oracle
+        self.threads = threads
+        self.ref = oracle.ref()
+        self.kind = "reference" if self.ref is not None else "port"
+        self.jobs = []
+        self.bytes = 0
+        for fmt, q, rows in packed:
+            self.bytes += q.size
+            if self.ref is not None:
+                self.jobs.append(oracle.MatmulJob(self.ref, fmt, q, x, rows, K_DIM, threads))
+            else:
+                self.jobs.append((fmt, q, rows))
+        self.x = x
+
+    def step(self):
+        import concurrent.futures as cf
+        import oracle
+        if self.ref is not None:
+            for j in self.jobs:
+                j.run()
+            return
+        orc = oracle.orc()
+        for fmt, q, rows in self.jobs:
+            out = np.empty((rows, self.x.shape[1]), dtype=np.float32)
+            with cf.ThreadPoolExecutor(self.threads) as ex:
+                chunks = [(rows * t // self.threads, rows * (t + 1) // self.threads) for t in range(self.threads)]
+                list(ex.map(lambda c: orc.matmul_rows(fmt, q, self.x, out, rows, K_DIM, c[0], c[1]), chunks))
+
+    def close(self):
+        if self.ref is not None:
+            for j in self.jobs:
+                j.close()
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    rows = ROWS
+    x = np.random.default_rng(2).standard_normal((K_DIM, M_TOK), dtype=np.float32)
+    packed = []
+    for i, fmt in enumerate(FORMATS):
+        W = make_weights_np(i, rows, K_DIM, 9)
+        packed.append((fmt, cpu_pack_reference(fmt, W, threads), rows))
+        del W
+    arm = CpuArm(packed, x, threads)
+    for _ in range(args.warmup):
+        arm.step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        arm.step()
+    dt = (time.perf_counter() - t0) / args.steps
+    arm.close()
+    gbs = arm.bytes / dt / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 4), "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD + " (rank 0's shard)", "rows": rows, "K": K_DIM, "M": M_TOK,
+                   "formats": list(FORMATS), "l2": "inputs larger than L2"},
+        "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": arm.kind,
+                         "sample": f"full step: {len(FORMATS)} GEMVs over {rows} rows"},
+        "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------ GPU arm
+
+def run_gpu(args):
+    import torch
+    import torch.distributed as dist
+    import axon_b200 as ax
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    # Seeded synthetic weights, packed on the device by our quantize kernel.
+    g = torch.Generator(device=dev).manual_seed(1000 * rank + 9)
+    qs = {}
+    for fmt in FORMATS:
+        W = torch.randn(ROWS, K_DIM, device=dev, generator=g) * 0.02
+        m = torch.rand(ROWS, K_DIM, device=dev, generator=g) < 0.001
+        W[m] = torch.randn(int(m.sum().item()), device=dev, generator=g) * 0.5
+        qt = ax.QTensor.empty(ROWS, K_DIM, ax.QuantFormat[fmt], device=dev)
+        ax.quantize(qt, W, ax.QuantFormat[fmt])
+        del W, m
+        qs[fmt] = qt
+    torch.cuda.synchronize()
+    xg = torch.Generator(device=dev).manual_seed(2)
+    x = torch.randn(M_TOK, K_DIM, device=dev, generator=xg)
+    ys = {f: torch.empty(M_TOK, ROWS, device=dev) for f in FORMATS}
+    yfull = {f: torch.empty(world * M_TOK * ROWS, device=dev) for f in FORMATS}
+    ws = ax.Workspace()
+    stream = torch.cuda.current_stream()
+    ev_dom = []
+
+    def step(record=False):
+        for fmt in FORMATS:
+            if record and fmt == DOMINANT:
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+            ax.linear_q(x, qs[fmt], out=ys[fmt], workspace=ws)
+            if record and fmt == DOMINANT:
+                e1.record(stream)
+                ev_dom.append((e0, e1))
+            if world > 1:
+                dist.all_gather_into_tensor(yfull[fmt], ys[fmt].view(-1))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    barrier()
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    t0.record(stream)
+    for _ in range(args.steps):
+        step(record=True)
+    t1.record(stream)
+    barrier()
+    ms = t0.elapsed_time(t1) / args.steps
+    dom_ms = sum(a.elapsed_time(b) for a, b in ev_dom) / max(1, len(ev_dom))
+    clocks = sampler.stop() if sampler else None
+    if world > 1:
+        t = torch.tensor([ms, dom_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, dom_ms = float(t[0]), float(t[1])
+
+    # End to end through the public API with host buffers: pinned x -> device,
+    # the three matmuls (+ all-gathers), full outputs -> pinned host.
+    xh = torch.randn(M_TOK, K_DIM).pin_memory()
+    yh = {f: torch.empty(world * M_TOK * ROWS).pin_memory() for f in FORMATS}
+    xd = torch.empty_like(x)
+
+    def e2e_step():
+        xd.copy_(xh, non_blocking=True)
+        for fmt in FORMATS:
+            ax.linear_q(xd, qs[fmt], out=ys[fmt], workspace=ws)
+            if world > 1:
+                dist.all_gather_into_tensor(yfull[fmt], ys[fmt].view(-1))
+                yh[fmt].copy_(yfull[fmt], non_blocking=True)
+            else:
+                yh[fmt].copy_(ys[fmt].view(-1), non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t[0])
+
+    total_w = world * sum(packed_bytes(f) for f in FORMATS)
+    value = total_w / (ms / 1e3) / 1e9
+    e2e_val = total_w / (e2e_ms / 1e3) / 1e9
+    peak, peak_kind = load_peaks()
+    dom_bytes = packed_bytes(DOMINANT) + 4 * K_DIM * M_TOK + 4 * ROWS * M_TOK
+    achieved = dom_bytes / (dom_ms / 1e3) / 1e9
+    line = None
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = cpu_baseline(qs, x)
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8-dp4a/f32-acc", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "rows_per_gpu": ROWS, "K": K_DIM, "M": M_TOK,
+                       "formats": list(FORMATS), "parallelism": f"row-shard x{world} + NCCL all-gather",
+                       "l2": "inputs larger than L2 (340 MB of packed weights per GPU)"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                         "kernel": f"matmul {DOMINANT} (act prep + gemv)", "ms_per_launch": round(dom_ms, 5),
+                         "traffic": load_traffic()},
+            "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * K_DIM * M_TOK,
+                    "d2h_bytes_per_step": 4 * world * M_TOK * ROWS * len(FORMATS)},
+            "gpu_launches": 2 * len(FORMATS) * args.steps,
+            "clocks": clocks,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def cpu_baseline(qs, x):
+    """Reference CPU path (rank 0, N=1) on a bounded sample: the full step's
+    three GEMVs over 1/4 of the rows, with all host threads, ~10 s."""
+    rows = ROWS // 4
+    threads = os.cpu_count() or 1
+    xn = x.t().contiguous().cpu().numpy()  # reference B layout [K x N]
+    packed = []
+    for fmt in FORMATS:
+        rb = packed_bytes(fmt, 1)
+        packed.append((fmt, qs[fmt].data[: rows * rb].cpu().numpy(), rows))
+    arm = CpuArm(packed, xn, threads)
+    arm.step()
+    n, t0 = 0, time.perf_counter()
+    while True:
+        arm.step()
+        n += 1
+        dt = time.perf_counter() - t0
+        if dt > 10.0 or n >= 50:
+            break
+    arm.close()
+    return {"value": round(arm.bytes * n / dt / 1e9, 4), "unit": "GB/s", "cores": threads, "kind": arm.kind,
+            "sample": f"{n} steps of {len(FORMATS)} GEMVs over {rows} of {ROWS} rows"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="axon_b200", choices=["axon_b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    return run_gpu(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,101 @@
+/*
+ * axq.h — C ABI of the B200 (sm_100a) block-quantized matmul path.
+ *
+ * Drop-in device implementation of the reference's (ruwwww/Axon) GGML-style
+ * quantize / dequantize / quantized-matmul CPU path.  Plain pointers and
+ * sizes only: every pointer argument except host-side results is device
+ * memory on the current CUDA device; every call is asynchronous on `stream`
+ * (NULL = legacy default stream) and allocates nothing.
+ *
+ * Errors follow the reference's Expected<void>/Error{message} convention
+ * (include/axon/core/expected.h:9-62): 0 is success, a non-zero AXQ_ERR_*
+ * code is failure and axq_last_error() returns the message (thread-local).
+ *
+ * Orientation is the reference's: the quantized operand is the LEFT matrix,
+ * out[M x N] = A_q[M x K] . B[K x N] (src/backend/cpu_backend.cpp:1699-1720).
+ * For y = x . W^T with W[M x K] quantized and x[N x K], pass
+ * AXQ_FLAG_B_TOKMAJOR (B stored as x, [N x K]) and AXQ_FLAG_OUT_TOKMAJOR
+ * (out stored as y, [N x M]).
+ */
+#ifndef AXQ_H
+#define AXQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Format ids: the reference's QuantFormat ordinals
+ * (include/axon/core/types.h:36-45). */
+enum axq_format {
+    AXQ_NONE = 0,
+    AXQ_Q8_0 = 1,
+    AXQ_Q6_K = 2,
+    AXQ_Q5_K = 3,
+    AXQ_Q4_0 = 4,
+    AXQ_Q4_K = 5,
+    AXQ_Q3_K = 6,
+    AXQ_Q2_K = 7
+};
+
+enum axq_status {
+    AXQ_OK = 0,
+    AXQ_ERR_INVALID = 1,     /* bad shape, pointer, format or flags */
+    AXQ_ERR_UNSUPPORTED = 2, /* format / option not implemented on this path */
+    AXQ_ERR_CUDA = 3,        /* a CUDA runtime call failed */
+    AXQ_ERR_WORKSPACE = 4,   /* workspace missing or too small */
+    AXQ_ERR_TIMEOUT = 5,     /* a kernel's bounded wait gave up */
+    AXQ_ERR_COMM = 6         /* a collective failed */
+};
+
+#define AXQ_FLAG_B_TOKMAJOR 1u   /* B is [N x K] (token-major) instead of [K x N] */
+#define AXQ_FLAG_OUT_TOKMAJOR 2u /* out is [N x M] instead of [M x N] */
+
+typedef struct CUstream_st* axq_stream_t; /* == cudaStream_t */
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* axq_last_error(void);
+
+/* Library version, major*10000 + minor*100 + patch. */
+int axq_version(void);
+
+/* Bytes of `numel` elements packed as one flat run of blocks.
+ * Replaces cpu::quantized_size (src/backend/cpu_backend.cpp:693-711). */
+size_t axq_quantized_size(size_t numel, int fmt);
+
+/* Bytes of a [rows x cols] matrix packed row by row (each row padded to
+ * whole blocks).  Replaces cpu::quantized_size_2d (cpu_backend.cpp:713-735). */
+size_t axq_quantized_size_2d(int64_t rows, int64_t cols, int fmt);
+
+/* Pack src[rows x cols] (fp32, row-major) into dst (axq_quantized_size_2d
+ * bytes), byte-identical to the reference.  A 1-D tensor of n elements is
+ * rows = 1, cols = n.  Replaces cpu::quantize (cpu_backend.cpp:1160-1330). */
+int axq_quantize(int fmt, const float* src, void* dst, int64_t rows, int64_t cols, axq_stream_t stream);
+
+/* Decode packed src into dst[rows x cols] (fp32), bit-identical to the
+ * reference.  Replaces cpu::dequantize (cpu_backend.cpp:1334-1670). */
+int axq_dequantize(int fmt, const void* src, float* dst, int64_t rows, int64_t cols, axq_stream_t stream);
+
+/* Device scratch bytes axq_matmul needs for these sizes (activation
+ * block-quantization and status words). */
+size_t axq_matmul_workspace_size(int fmt, int64_t M, int64_t K, int64_t N);
+
+/* out = A_q . B, fp32 out.  a_q holds M packed rows of K elements.
+ * Replaces cpu::matmul_q4 / matmul_q2_K / _q3_K / _q4_K / _q5_K / _q6_K
+ * (cpu_backend.cpp:1674, 1862, 1924, 1727, 1999, 1805) and the Q8_0 route of
+ * cpu::matmul (cpu_backend.cpp:116-173), which the reference names but never
+ * registers.  Results match the reference within 1e-3 * max|out_ref|. */
+int axq_matmul(int fmt, const void* a_q, const float* b, float* out, int64_t M, int64_t K, int64_t N,
+               unsigned flags, void* workspace, size_t workspace_bytes, axq_stream_t stream);
+
+/* Synchronizes `stream` and reports whether a kernel that used `workspace`
+ * gave up a bounded wait (AXQ_ERR_TIMEOUT) — 0 otherwise. */
+int axq_workspace_status(const void* workspace, axq_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AXQ_H */
