@@ -94,6 +94,19 @@ __device__ __forceinline__ void scale_min_k4(int j, const uint8_t* q, int& d, in
     }
 }
 
+// x86 SSE NaN results: an invalid operation (0*inf, inf-inf) yields the
+// "default NaN" 0xFFC00000; a NaN operand propagates quieted.  The GPU
+// returns its canonical 0x7FFFFFFF instead, so the decode ops below restore
+// the x86 bit pattern (only ever taken when the result is NaN).
+__device__ __forceinline__ float x86_nan(float r, float a, float b) {
+    if (!isnan(r)) return r;
+    if (isnan(a)) return __uint_as_float(__float_as_uint(a) | 0x400000u);
+    if (isnan(b)) return __uint_as_float(__float_as_uint(b) | 0x400000u);
+    return __uint_as_float(0xFFC00000u);
+}
+__device__ __forceinline__ float xmul(float a, float b) { return x86_nan(__fmul_rn(a, b), a, b); }
+__device__ __forceinline__ float xsub(float a, float b) { return x86_nan(__fsub_rn(a, b), a, b); }
+
 // Little-endian 16-bit read from a byte pointer with any alignment.
 __device__ __forceinline__ uint32_t ld_u16(const uint8_t* p) { return p[0] | (static_cast<uint32_t>(p[1]) << 8); }
 

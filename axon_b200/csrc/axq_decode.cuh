@@ -18,7 +18,7 @@ template <> struct Decode<F_Q8_0> {
     __device__ __forceinline__ static void run(const uint8_t* blk, int e0, float* out) {
         float d = h2f_ref(ld_u16(blk));
 #pragma unroll
-        for (int u = 0; u < 8; ++u) out[u] = __fmul_rn(static_cast<float>(static_cast<int8_t>(blk[2 + e0 + u])), d);
+        for (int u = 0; u < 8; ++u) out[u] = xmul(static_cast<float>(static_cast<int8_t>(blk[2 + e0 + u])), d);
     }
 };
 
@@ -30,8 +30,8 @@ template <> struct Decode<F_Q4_0> {
 #pragma unroll
         for (int u = 0; u < 8; u += 2) {
             uint32_t b = blk[2 + (e0 + u) / 2];
-            out[u] = __fmul_rn(static_cast<float>(static_cast<int>(b & 0xF) - 8), d);
-            out[u + 1] = __fmul_rn(static_cast<float>(static_cast<int>(b >> 4) - 8), d);
+            out[u] = xmul(static_cast<float>(static_cast<int>(b & 0xF) - 8), d);
+            out[u + 1] = xmul(static_cast<float>(static_cast<int>(b >> 4) - 8), d);
         }
     }
 };
@@ -43,12 +43,12 @@ template <> struct Decode<F_Q2_K> {
         int n = e0 >> 7, j = (e0 >> 5) & 3, l0 = e0 & 31;
         float d = h2f_ref(ld_u16(blk)), mn = h2f_ref(ld_u16(blk + 2));
         uint32_t sc = blk[4 + 8 * n + 2 * j + (l0 >= 16)];
-        float dl = __fmul_rn(d, static_cast<float>(sc & 0xF));
-        float ml = __fmul_rn(mn, static_cast<float>(sc >> 4));
+        float dl = xmul(d, static_cast<float>(sc & 0xF));
+        float ml = xmul(mn, static_cast<float>(sc >> 4));
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
             int q = (blk[20 + 32 * n + l0 + u] >> (2 * j)) & 3;
-            out[u] = __fsub_rn(__fmul_rn(dl, static_cast<float>(q)), ml);
+            out[u] = xsub(xmul(dl, static_cast<float>(q)), ml);
         }
     }
 };
@@ -65,12 +65,12 @@ template <> struct Decode<F_Q3_K> {
         int n = e0 >> 7, j = (e0 >> 5) & 3, l0 = e0 & 31;
         float d_all = h2f_ref(ld_u16(blk + 108));
         int sc = subscale(blk + 96, 8 * n + 2 * j + (l0 >= 16));
-        float dl = __fmul_rn(d_all, static_cast<float>(sc));
+        float dl = xmul(d_all, static_cast<float>(sc));
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
             int qv = (blk[32 + 32 * n + l0 + u] >> (2 * j)) & 3;
             int h = (blk[l0 + u] >> (4 * n + j)) & 1;
-            out[u] = __fmul_rn(dl, static_cast<float>(qv - (h ? 0 : 4)));
+            out[u] = xmul(dl, static_cast<float>(qv - (h ? 0 : 4)));
         }
     }
 };
@@ -83,12 +83,12 @@ template <> struct Decode<F_Q4_K> {
         float d = h2f_ref(ld_u16(blk)), mn = h2f_ref(ld_u16(blk + 2));
         int sc, m;
         scale_min_k4(g, blk + 4, sc, m);
-        float d1 = __fmul_rn(d, static_cast<float>(sc)), m1 = __fmul_rn(mn, static_cast<float>(m));
+        float d1 = xmul(d, static_cast<float>(sc)), m1 = xmul(mn, static_cast<float>(m));
         int sh = (g & 1) * 4;
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
             int q = (blk[16 + 32 * c + l0 + u] >> sh) & 0xF;
-            out[u] = __fsub_rn(__fmul_rn(d1, static_cast<float>(q)), m1);
+            out[u] = xsub(xmul(d1, static_cast<float>(q)), m1);
         }
     }
 };
@@ -100,12 +100,12 @@ template <> struct Decode<F_Q5_K> {
         float d = h2f_ref(ld_u16(blk)), mn = h2f_ref(ld_u16(blk + 2));
         int sc, m;
         scale_min_k4(g, blk + 4, sc, m);
-        float d1 = __fmul_rn(d, static_cast<float>(sc)), m1 = __fmul_rn(mn, static_cast<float>(m));
+        float d1 = xmul(d, static_cast<float>(sc)), m1 = xmul(mn, static_cast<float>(m));
         int sh = (g & 1) * 4;
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
             int q = ((blk[48 + 32 * c + l0 + u] >> sh) & 0xF) + (((blk[16 + l0 + u] >> g) & 1) << 4);
-            out[u] = __fsub_rn(__fmul_rn(d1, static_cast<float>(q)), m1);
+            out[u] = xsub(xmul(d1, static_cast<float>(q)), m1);
         }
     }
 };
@@ -117,14 +117,14 @@ template <> struct Decode<F_Q6_K> {
         int n = e0 >> 7, t = (e0 >> 5) & 3, l0 = e0 & 31;
         float d = h2f_ref(ld_u16(blk + 208));
         int sc = static_cast<int8_t>(blk[192 + 8 * n + (l0 >> 4) + 2 * t]);
-        float dsc = __fmul_rn(d, static_cast<float>(sc));
+        float dsc = xmul(d, static_cast<float>(sc));
         const uint8_t* ql = blk + 64 * n + ((t & 1) ? 32 : 0);
         const uint8_t* qh = blk + 128 + 32 * n;
         int sh = (t & 2) ? 4 : 0;
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
             int q = (((ql[l0 + u] >> sh) & 0xF) | (((qh[l0 + u] >> (2 * t)) & 3) << 4)) - 32;
-            out[u] = __fmul_rn(dsc, static_cast<float>(q));
+            out[u] = xmul(dsc, static_cast<float>(q));
         }
     }
 };

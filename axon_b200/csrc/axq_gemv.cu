@@ -497,15 +497,16 @@ GemvPlan plan_gemv(int64_t rows, int64_t K, int mg) {
 template <int F, int MG>
 cudaError_t launch_gemv_mg(const GemvPlan& p, GemvArgs a, cudaStream_t s) {
     auto kern = gemv_kernel<F, MG>;
-    // Opt in to large dynamic shared memory once per device.
+    // Opt in to the dynamic shared memory this launch needs (largest value
+    // seen so far, per device).
     static int configured[64] = {0};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (p.smem > 227 * 1024) return cudaErrorInvalidConfiguration;
-    if (dev < 0 || dev >= 64 || !configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (p.smem > configured[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, p.smem);
         if (e != cudaSuccess) return e;
-        if (dev >= 0 && dev < 64) configured[dev] = 1;
+        configured[dev] = p.smem;
     }
     kern<<<p.grid, p.threads, p.smem, s>>>(a);
     return cudaGetLastError();
