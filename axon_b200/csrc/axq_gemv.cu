@@ -1,24 +1,34 @@
 // Quantized GEMV / small-batch matmul: out[M x N] = W_q[M x K] . X[K x N]
-// for N (activation columns, "tokens") up to a few, HBM-bound on the packed
+// for N (activation columns, "tokens") of 1..8, HBM-bound on the packed
 // weights.
 //
 // Design (B200-first):
-//  * Weights stream through shared memory in row tiles (R whole rows, any
-//    byte alignment) with 1-D bulk async copies (TMA engine) into a
-//    4-stage mbarrier pipeline; odd head/tail bytes of a tile are copied by
-//    one thread, so no alignment is required of the packed rows (Q6_K rows
-//    of K=11008 are 9030 bytes).
+//  * Warp specialisation: one producer warp streams weight tiles into a ring
+//    of shared-memory stages with 1-D bulk async copies (TMA engine,
+//    cp.async.bulk + mbarrier complete_tx); eight consumer warps decode and
+//    multiply.  full/empty mbarriers pace the ring; every wait is bounded.
+//  * A stage holds 16 weight rows x 8 column groups (CG = 256 elements: one
+//    K-quant block or eight Q8_0/Q4_0 blocks).  Consumer warp w takes CG w of
+//    the stage; lane l handles row l%16 and half l/16 of that CG (128
+//    elements), so a block's scales are decoded once per 128 elements and no
+//    per-row shuffle reduction is needed.  Per-row partials are combined
+//    across warps once per 16-row unit.
+//  * Packed rows keep the reference's layout and any byte alignment: each
+//    row segment is copied from its 16-byte-rounded range (bytes of the
+//    neighbouring segments ride along), except where that range would leave
+//    the weight buffer, where the producer warp copies bytes itself.
 //  * Activations are block-quantized once per call (act_prep_kernel): each
 //    32-element block is split into two int8 terms, x ~ u*(254*hi + lo),
-//    plus exact fp32 sums per 8-element run.  The reference's fp32 dot
-//    (cpu_backend.cpp:1699-2060) is then sum_runs D*u*S - Mo*sum(x) with
-//    S = 254*dp4a(q,hi) + dp4a(q,lo), where D is the run's weight scale and
-//    Mo folds the format's code offset and K-quant min.  The relative error
-//    of the split is ~1e-5 of the block maximum, well inside the 1e-3 of
-//    max|y| tolerance.
-//  * Each thread owns fixed 32-element chunks of every row, so its
-//    activation words sit in registers for the R rows of a tile; per-row
-//    partials reduce with warp shuffles and a small shared-memory pass.
+//    with exact fp32 sums per 16-element run.  Every format decodes into
+//    eight 16-element runs of (code words, D, Mo) with value = D*code - Mo,
+//    so the reference's fp32 dot (cpu_backend.cpp:1699-2060) becomes
+//    sum_runs (D*u)*S - Mo*sum(x), S = 254*dp4a(q,hi) + dp4a(q,lo).
+//    Nibbles and 2-bit fields are masked in place (not shifted) and the
+//    power-of-two factor is folded into D, using unsigned x signed dp4a.
+//    The split's error is ~1.5e-5 of each block's max |x|, far inside the
+//    1e-3 * max|y| tolerance.
+#include <algorithm>
+
 #include "axq_common.cuh"
 #include "axq_internal.h"
 #include "axq_ptx.cuh"
@@ -26,179 +36,322 @@
 namespace axq {
 namespace {
 
-constexpr int kStages = 4;
-constexpr int kMaxRows = 8;  // rows per tile
-constexpr int kMaxThreads = 512;
+constexpr int kConsumerWarps = 8;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kUnitRows = 16;
+constexpr int kMaxStages = 8;
+constexpr int kStageCG = 2 * kConsumerWarps;  // column groups per stage (two per warp)
+// Shared-memory header: full[kMaxStages], empty[kMaxStages] mbarriers, abort flag.
+constexpr int kHeaderBytes = ((2 * kMaxStages * 8 + 4 + 127) / 128) * 128;
 
-// Per-format chunk geometry and decode into dp4a operands.
-//   CPB: 32-element chunks per block; NR: runs per chunk (run = 32/NR
-//   elements sharing one weight scale and one activation block);
-//   k0(c, r): first element (within the block) of run r of chunk c;
-//   load(): 8 code words (4 codes each, in the activation order of the run)
-//   plus the run scales D and offsets Mo (value = D*code - Mo).
-template <int F> struct Gv;
-
-template <> struct Gv<F_Q8_0> {
-    static constexpr int CPB = 1, NR = 1;
-    __device__ static int k0(int, int) { return 0; }
-    __device__ static void load(const uint8_t* blk, int, uint32_t* q, float* D, float* Mo) {
-        uint32_t h[1];
-        ld_words<1>(blk, h);
-        D[0] = h2f_ref(h[0] & 0xFFFFu);
-        Mo[0] = 0.0f;
-        ld_words<8>(blk + 2, q);
-    }
-};
-
-// Q4_0 codes come out as even elements then odd elements of each 8-run; the
-// activation prep writes the same order (kPermQ4_0).
-template <> struct Gv<F_Q4_0> {
-    static constexpr int CPB = 1, NR = 1;
-    __device__ static int k0(int, int) { return 0; }
-    __device__ static void load(const uint8_t* blk, int, uint32_t* q, float* D, float* Mo) {
-        uint32_t h[1], w[4];
-        ld_words<1>(blk, h);
-        float d = h2f_ref(h[0] & 0xFFFFu);
-        D[0] = d;
-        Mo[0] = 8.0f * d;
-        ld_words<4>(blk + 2, w);
+// n 32-bit words from shared address p with static alignment A (16, 4, or 1
+// for "any").  The generic form reads one extra word past the data.
+template <int N, int A>
+__device__ __forceinline__ void ldw(const uint8_t* p, uint32_t* out) {
+    if constexpr (A >= 16 && N % 4 == 0) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            q[2 * i] = w[i] & 0x0F0F0F0Fu;
-            q[2 * i + 1] = (w[i] >> 4) & 0x0F0F0F0Fu;
+        for (int i = 0; i < N / 4; ++i) {
+            uint4 v = reinterpret_cast<const uint4*>(p)[i];
+            out[4 * i] = v.x; out[4 * i + 1] = v.y; out[4 * i + 2] = v.z; out[4 * i + 3] = v.w;
         }
-    }
-};
-
-template <> struct Gv<F_Q2_K> {
-    static constexpr int CPB = 8, NR = 4;
-    __device__ static int k0(int c, int r) { return 128 * (c >> 2) + 32 * r + 8 * (c & 3); }
-    __device__ static void load(const uint8_t* blk, int c, uint32_t* q, float* D, float* Mo) {
-        const int n = c >> 2, l0 = 8 * (c & 3);
-        uint32_t h[1], s[2], w[2];
-        ld_words<1>(blk, h);
-        float d = h2f_ref(h[0] & 0xFFFFu), mn = h2f_ref(h[0] >> 16);
-        ld_words<2>(blk + 4 + 8 * n, s);
-        ld_words<2>(blk + 20 + 32 * n + l0, w);
+    } else if constexpr (A >= 4) {
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            uint32_t sc = byte_of(s, (l0 >= 16) + 2 * r);
-            D[r] = d * static_cast<float>(sc & 0xF);
-            Mo[r] = mn * static_cast<float>(sc >> 4);
-            q[2 * r] = (w[0] >> (2 * r)) & 0x03030303u;
-            q[2 * r + 1] = (w[1] >> (2 * r)) & 0x03030303u;
-        }
-    }
-};
-
-template <> struct Gv<F_Q3_K> {
-    static constexpr int CPB = 8, NR = 4;
-    __device__ static int k0(int c, int r) { return 128 * (c >> 2) + 32 * r + 8 * (c & 3); }
-    __device__ static void load(const uint8_t* blk, int c, uint32_t* q, float* D, float* Mo) {
-        const int n = c >> 2, l0 = 8 * (c & 3);
-        uint32_t hd[1], s[3], w[2], hm[2];
-        ld_words<1>(blk + 108, hd);
-        float d = h2f_ref(hd[0] & 0xFFFFu);
-        ld_words<3>(blk + 96, s);
-        ld_words<2>(blk + 32 + 32 * n + l0, w);
-        ld_words<2>(blk + l0, hm);
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            const int is = 8 * n + 2 * r + (l0 >= 16);
-            int lo4 = (is < 8) ? (byte_of(s, is) & 0xF) : (byte_of(s, is - 8) >> 4);
-            int hi2 = (byte_of(s, 8 + (is & 3)) >> (2 * (is >> 2))) & 3;
-            float Dr = d * static_cast<float>((lo4 | (hi2 << 4)) - 32);
-            D[r] = Dr;
-            Mo[r] = 4.0f * Dr;
-            const int hb = 4 * n + r;
-#pragma unroll
-            for (int i = 0; i < 2; ++i)
-                q[2 * r + i] = ((w[i] >> (2 * r)) & 0x03030303u) | (((hm[i] >> hb) & 0x01010101u) << 2);
-        }
-    }
-};
-
-__device__ __forceinline__ void k4_scale_min(const uint32_t* hw, int g, int& sc, int& m) {
-    // 12 scale bytes are bytes 4..15 of the 16-byte header words.
-    if (g < 4) {
-        sc = byte_of(hw, 4 + g) & 63;
-        m = byte_of(hw, 8 + g) & 63;
+        for (int i = 0; i < N; ++i) out[i] = reinterpret_cast<const uint32_t*>(p)[i];
     } else {
-        sc = (byte_of(hw, 8 + g) & 0xF) | ((byte_of(hw, g) >> 6) << 4);
-        m = (byte_of(hw, 8 + g) >> 4) | ((byte_of(hw, 4 + g) >> 6) << 4);
+        ld_words<N>(p, out);
     }
 }
 
-template <> struct Gv<F_Q4_K> {
-    static constexpr int CPB = 8, NR = 2;
-    __device__ static int k0(int c, int r) { return 64 * (c >> 1) + 32 * r + 16 * (c & 1); }
-    __device__ static void load(const uint8_t* blk, int c, uint32_t* q, float* D, float* Mo) {
-        const int cc = c >> 1, l0 = 16 * (c & 1);
-        uint32_t hw[4], w[4];
-        ld_words<4>(blk, hw);
-        float d = h2f_ref(hw[0] & 0xFFFFu), mn = h2f_ref(hw[0] >> 16);
+template <bool SIGNED>
+__device__ __forceinline__ int dp4(uint32_t a, uint32_t b, int c) {
+    int d;
+    if constexpr (SIGNED) asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    else asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// Per-token activation pointers for one column group (256 elements).
+template <int NT> struct ActCG {
+    const int8_t* hi[NT];
+    const int8_t* lo[NT];
+    const float* u[NT];
+    const float* s16[NT];
+};
+
+// One run of NW code words (4*NW elements starting at element k of the
+// column group) sharing weight scale D and offset Mo: acc += D*u*S - Mo*sum(x).
+template <bool SG, int NW, int NT>
+__device__ __forceinline__ void run_dot(const uint32_t* q, float D, float Mo, const ActCG<NT>& A, int k, float* acc,
+                                        int ntok) {
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            int sc, m;
-            k4_scale_min(hw, 2 * cc + r, sc, m);
-            D[r] = d * static_cast<float>(sc);
-            Mo[r] = mn * static_cast<float>(m);
+    for (int t = 0; t < NT; ++t) {
+        if (t < ntok) {
+            uint32_t h[NW], l[NW];
+#pragma unroll
+            for (int v = 0; v < NW / 4; ++v) {
+                const uint4 hv = __ldg(reinterpret_cast<const uint4*>(A.hi[t] + k) + v);
+                const uint4 lv = __ldg(reinterpret_cast<const uint4*>(A.lo[t] + k) + v);
+                h[4 * v] = hv.x; h[4 * v + 1] = hv.y; h[4 * v + 2] = hv.z; h[4 * v + 3] = hv.w;
+                l[4 * v] = lv.x; l[4 * v + 1] = lv.y; l[4 * v + 2] = lv.z; l[4 * v + 3] = lv.w;
+            }
+            const float uu = __ldg(A.u[t] + k / 32);
+            float sx;
+            if constexpr (NW == 8) {
+                const float2 s2 = __ldg(reinterpret_cast<const float2*>(A.s16[t] + k / 16));
+                sx = s2.x + s2.y;
+            } else {
+                sx = __ldg(A.s16[t] + k / 16);
+            }
+            int sh = 0;
+#pragma unroll
+            for (int v = 0; v < NW; ++v) sh = dp4<SG>(q[v], h[v], sh);
+            int S = sh * 254;
+#pragma unroll
+            for (int v = 0; v < NW; ++v) S = dp4<SG>(q[v], l[v], S);
+            acc[t] = fmaf(D * uu, static_cast<float>(S), acc[t]);
+            acc[t] = fmaf(-Mo, sx, acc[t]);
         }
-        ld_words<4>(blk + 16 + 32 * cc + l0, w);
+    }
+}
+
+// Byte i (compile-time) of a little-endian word array.
+template <int I>
+__device__ __forceinline__ uint32_t bt(const uint32_t* w) { return (w[I >> 2] >> (8 * (I & 3))) & 0xFFu; }
+
+// get_scale_min_k4 for a compile-time group G on the 16-byte header words
+// (bytes 4..15 are the 12 scale bytes).
+template <int G>
+__device__ __forceinline__ void k4sm(const uint32_t* hw, int& sc, int& m) {
+    if constexpr (G < 4) {
+        sc = bt<4 + G>(hw) & 63;
+        m = bt<8 + G>(hw) & 63;
+    } else {
+        sc = (bt<8 + G>(hw) & 0xF) | ((bt<G>(hw) >> 6) << 4);
+        m = (bt<8 + G>(hw) >> 4) | ((bt<4 + G>(hw) >> 6) << 4);
+    }
+}
+
+// Per-format processing of one full column group (256 elements) of one
+// row: decode (bit-level layouts of cpu_backend.cpp:1340-1504) into
+// 16- or 32-element runs and accumulate their dot products.
+template <int F> struct Lane;
+
+// Q8_0: CG = 8 blocks {u16 d; i8 qs[32]}; one signed 32-element run each.
+template <> struct Lane<F_Q8_0> {
+    static constexpr int CGB = 8 * 34, A = 1, PERM = 0;
+    template <int AL, int NT>
+    __device__ static void process(const uint8_t* cg, int nblk_valid, const ActCG<NT>& X, float* acc, int ntok) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            q[i] = w[i] & 0x0F0F0F0Fu;
-            q[4 + i] = (w[i] >> 4) & 0x0F0F0F0Fu;
+        for (int b = 0; b < 8; ++b) {
+            if (b < nblk_valid) {
+                uint32_t hd[1], w[8];
+                ld_words<1>(cg + 34 * b, hd);
+                ld_words<8>(cg + 34 * b + 2, w);
+                run_dot<true, 8, NT>(w, h2f_ref(hd[0] & 0xFFFFu), 0.0f, X, 32 * b, acc, ntok);
+            }
         }
     }
 };
 
-template <> struct Gv<F_Q5_K> {
-    static constexpr int CPB = 8, NR = 2;
-    __device__ static int k0(int c, int r) { return 64 * (c >> 1) + 32 * r + 16 * (c & 1); }
-    __device__ static void load(const uint8_t* blk, int c, uint32_t* q, float* D, float* Mo) {
-        const int cc = c >> 1, l0 = 16 * (c & 1);
-        uint32_t hw[4], w[4], h[4];
-        ld_words<4>(blk, hw);
-        float d = h2f_ref(hw[0] & 0xFFFFu), mn = h2f_ref(hw[0] >> 16);
+// Q4_0: CG = 8 blocks {u16 d; u8 qs[16]}; low nibbles = even elements, high
+// nibbles (kept in place, x16 folded into D) = odd elements; the activation
+// prep orders each 32-block as evens then odds.
+template <> struct Lane<F_Q4_0> {
+    static constexpr int CGB = 8 * 18, A = 1, PERM = 1;
+    template <int AL, int NT>
+    __device__ static void process(const uint8_t* cg, int nblk_valid, const ActCG<NT>& X, float* acc, int ntok) {
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            int sc, m;
-            k4_scale_min(hw, 2 * cc + r, sc, m);
-            D[r] = d * static_cast<float>(sc);
-            Mo[r] = mn * static_cast<float>(m);
-        }
-        ld_words<4>(blk + 48 + 32 * cc + l0, w);
-        ld_words<4>(blk + 16 + l0, h);
+        for (int b = 0; b < 8; ++b) {
+            if (b < nblk_valid) {
+                uint32_t hd[1], w[4], q[4];
+                ld_words<1>(cg + 18 * b, hd);
+                ld_words<4>(cg + 18 * b + 2, w);
+                const float d = h2f_ref(hd[0] & 0xFFFFu);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            q[i] = (w[i] & 0x0F0F0F0Fu) | (((h[i] >> (2 * cc)) & 0x01010101u) << 4);
-            q[4 + i] = ((w[i] >> 4) & 0x0F0F0F0Fu) | (((h[i] >> (2 * cc + 1)) & 0x01010101u) << 4);
+                for (int j = 0; j < 4; ++j) q[j] = w[j] & 0x0F0F0F0Fu;
+                run_dot<false, 4, NT>(q, d, 8.0f * d, X, 32 * b, acc, ntok);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) q[j] = w[j] & 0xF0F0F0F0u;
+                run_dot<false, 4, NT>(q, d * 0.0625f, 8.0f * d, X, 32 * b + 16, acc, ntok);
+            }
         }
     }
 };
 
-template <> struct Gv<F_Q6_K> {
-    static constexpr int CPB = 8, NR = 4;
-    __device__ static int k0(int c, int r) { return 128 * (c >> 2) + 32 * r + 8 * (c & 3); }
-    __device__ static void load(const uint8_t* blk, int c, uint32_t* q, float* D, float* Mo) {
-        const int n = c >> 2, l0 = 8 * (c & 3);
-        uint32_t hd[1], s[2], a[2], b[2], h[2];
-        ld_words<1>(blk + 208, hd);
-        float d = h2f_ref(hd[0] & 0xFFFFu);
-        ld_words<2>(blk + 192 + 8 * n, s);
-        ld_words<2>(blk + 64 * n + l0, a);
-        ld_words<2>(blk + 64 * n + 32 + l0, b);
-        ld_words<2>(blk + 128 + 32 * n + l0, h);
+// Q2_K {d, dmin, scales[16], qs[64]}: sub-block j = 8n + 2s + lh holds the
+// 2-bit field at shift 2s of qs[32n + 16lh + l]; masked in place, 4^-s in D.
+template <> struct Lane<F_Q2_K> {
+    static constexpr int CGB = 84, A = 4, PERM = 0;
+    template <int AL, int NT>
+    __device__ static void process(const uint8_t* cg, int, const ActCG<NT>& X, float* acc, int ntok) {
+        uint32_t hd[1], sc[4];
+        ldw<1, AL>(cg, hd);
+        ldw<4, AL>(cg + 4, sc);
+        const float d = h2f_ref(hd[0] & 0xFFFFu), mn = h2f_ref(hd[0] >> 16);
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-            float Dt = d * static_cast<float>(static_cast<int8_t>(byte_of(s, (l0 >> 4) + 2 * t)));
-            D[t] = Dt;
-            Mo[t] = 32.0f * Dt;
+        for (int n = 0; n < 2; ++n) {
+            uint32_t w[8];
+            ldw<8, AL>(cg + 20 + 32 * n, w);
 #pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                uint32_t src = (t & 1) ? b[i] : a[i];
-                q[2 * t + i] = ((src >> ((t & 2) ? 4 : 0)) & 0x0F0F0F0Fu) | (((h[i] >> (2 * t)) & 0x03030303u) << 4);
+            for (int s = 0; s < 4; ++s) {
+#pragma unroll
+                for (int lh = 0; lh < 2; ++lh) {
+                    const int j = 8 * n + 2 * s + lh;
+                    const uint32_t scb = (sc[j >> 2] >> (8 * (j & 3))) & 0xFFu;
+                    uint32_t q[4];
+#pragma unroll
+                    for (int v = 0; v < 4; ++v) q[v] = w[4 * lh + v] & (0x03030303u << (2 * s));
+                    const float D = d * static_cast<float>(scb & 0xF) * (1.0f / static_cast<float>(1 << (2 * s)));
+                    run_dot<false, 4, NT>(q, D, mn * static_cast<float>(scb >> 4), X, 128 * n + 32 * s + 16 * lh, acc,
+                                          ntok);
+                }
+            }
+        }
+    }
+};
+
+// Q3_K {hmask[32], qs[64], scales[12], d}: code = 2-bit field + 4*hmask bit,
+// value = D*(code - 4), D = d * (6-bit scale - 32).
+template <> struct Lane<F_Q3_K> {
+    static constexpr int CGB = 110, A = 1, PERM = 0;
+    template <int AL, int NT>
+    __device__ static void process(const uint8_t* cg, int, const ActCG<NT>& X, float* acc, int ntok) {
+        uint32_t hd[1], s12[3], hm[8];
+        ld_words<1>(cg + 108, hd);
+        ld_words<3>(cg + 96, s12);
+        ld_words<8>(cg, hm);
+        const float d = h2f_ref(hd[0] & 0xFFFFu);
+#pragma unroll
+        for (int n = 0; n < 2; ++n) {
+            uint32_t w[8];
+            ld_words<8>(cg + 32 + 32 * n, w);
+#pragma unroll
+            for (int s = 0; s < 4; ++s) {
+#pragma unroll
+                for (int lh = 0; lh < 2; ++lh) {
+                    const int is = 8 * n + 2 * s + lh;
+                    const int lo4 = (is < 8) ? ((s12[is >> 2] >> (8 * (is & 3))) & 0xF)
+                                             : ((s12[(is - 8) >> 2] >> (8 * ((is - 8) & 3) + 4)) & 0xF);
+                    const int hi2 = (s12[2] >> (8 * (is & 3) + 2 * (is >> 2))) & 3;
+                    const float D = d * static_cast<float>((lo4 | (hi2 << 4)) - 32);
+                    uint32_t q[4];
+#pragma unroll
+                    for (int v = 0; v < 4; ++v)
+                        q[v] = ((w[4 * lh + v] >> (2 * s)) & 0x03030303u) |
+                               (((hm[4 * lh + v] >> (4 * n + s)) & 0x01010101u) << 2);
+                    run_dot<false, 4, NT>(q, D, 4.0f * D, X, 128 * n + 32 * s + 16 * lh, acc, ntok);
+                }
+            }
+        }
+    }
+};
+
+// Q4_K {d, dmin, scales[12], qs[128]}: group g = 2c + nib covers nibble nib
+// of qs[32c + l]; high nibbles masked in place (1/16 in D).
+template <> struct Lane<F_Q4_K> {
+    static constexpr int CGB = 144, A = 16, PERM = 0;
+    template <int G, int AL, int NT>
+    __device__ static void group(const uint32_t* hw, const uint32_t* w, float d, float mn, const ActCG<NT>& X,
+                                 float* acc, int ntok) {
+        int sc, m;
+        k4sm<G>(hw, sc, m);
+        uint32_t q[8];
+#pragma unroll
+        for (int v = 0; v < 8; ++v) q[v] = w[v] & ((G & 1) ? 0xF0F0F0F0u : 0x0F0F0F0Fu);
+        const float D = d * static_cast<float>(sc) * ((G & 1) ? 0.0625f : 1.0f);
+        run_dot<false, 8, NT>(q, D, mn * static_cast<float>(m), X, 32 * G, acc, ntok);
+    }
+    template <int AL, int NT>
+    __device__ static void process(const uint8_t* cg, int, const ActCG<NT>& X, float* acc, int ntok) {
+        uint32_t hw[4];
+        ldw<4, AL>(cg, hw);
+        const float d = h2f_ref(hw[0] & 0xFFFFu), mn = h2f_ref(hw[0] >> 16);
+        uint32_t w[8];
+        ldw<8, AL>(cg + 16, w);
+        group<0, AL, NT>(hw, w, d, mn, X, acc, ntok);
+        group<1, AL, NT>(hw, w, d, mn, X, acc, ntok);
+        ldw<8, AL>(cg + 48, w);
+        group<2, AL, NT>(hw, w, d, mn, X, acc, ntok);
+        group<3, AL, NT>(hw, w, d, mn, X, acc, ntok);
+        ldw<8, AL>(cg + 80, w);
+        group<4, AL, NT>(hw, w, d, mn, X, acc, ntok);
+        group<5, AL, NT>(hw, w, d, mn, X, acc, ntok);
+        ldw<8, AL>(cg + 112, w);
+        group<6, AL, NT>(hw, w, d, mn, X, acc, ntok);
+        group<7, AL, NT>(hw, w, d, mn, X, acc, ntok);
+    }
+};
+
+// Q5_K {d, dmin, scales[12], qh[32], qs[128]}: as Q4_K plus bit g of qh[l].
+template <> struct Lane<F_Q5_K> {
+    static constexpr int CGB = 176, A = 16, PERM = 0;
+    template <int G, int AL, int NT>
+    __device__ static void group(const uint32_t* hw, const uint32_t* qh, const uint32_t* w, float d, float mn,
+                                 const ActCG<NT>& X, float* acc, int ntok) {
+        int sc, m;
+        k4sm<G>(hw, sc, m);
+        uint32_t q[8];
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+            const uint32_t nib = (G & 1) ? ((w[v] >> 4) & 0x0F0F0F0Fu) : (w[v] & 0x0F0F0F0Fu);
+            const uint32_t hb = (G <= 4) ? ((qh[v] << (4 - G)) & 0x10101010u) : ((qh[v] >> (G - 4)) & 0x10101010u);
+            q[v] = nib | hb;
+        }
+        run_dot<false, 8, NT>(q, d * static_cast<float>(sc), mn * static_cast<float>(m), X, 32 * G, acc, ntok);
+    }
+    template <int AL, int NT>
+    __device__ static void process(const uint8_t* cg, int, const ActCG<NT>& X, float* acc, int ntok) {
+        uint32_t hw[4], qh[8];
+        ldw<4, AL>(cg, hw);
+        ldw<8, AL>(cg + 16, qh);
+        const float d = h2f_ref(hw[0] & 0xFFFFu), mn = h2f_ref(hw[0] >> 16);
+        uint32_t w[8];
+        ldw<8, AL>(cg + 48, w);
+        group<0, AL, NT>(hw, qh, w, d, mn, X, acc, ntok);
+        group<1, AL, NT>(hw, qh, w, d, mn, X, acc, ntok);
+        ldw<8, AL>(cg + 80, w);
+        group<2, AL, NT>(hw, qh, w, d, mn, X, acc, ntok);
+        group<3, AL, NT>(hw, qh, w, d, mn, X, acc, ntok);
+        ldw<8, AL>(cg + 112, w);
+        group<4, AL, NT>(hw, qh, w, d, mn, X, acc, ntok);
+        group<5, AL, NT>(hw, qh, w, d, mn, X, acc, ntok);
+        ldw<8, AL>(cg + 144, w);
+        group<6, AL, NT>(hw, qh, w, d, mn, X, acc, ntok);
+        group<7, AL, NT>(hw, qh, w, d, mn, X, acc, ntok);
+    }
+};
+
+// Q6_K {ql[128], qh[64], scales[16], d}: sub-block j = 8n + 2t + lh; low 4
+// bits from ql (half t&1, nibble t>>1), high 2 bits from qh at shift 2t.
+template <> struct Lane<F_Q6_K> {
+    static constexpr int CGB = 210, A = 1, PERM = 0;
+    template <int AL, int NT>
+    __device__ static void process(const uint8_t* cg, int, const ActCG<NT>& X, float* acc, int ntok) {
+        uint32_t hd[1], sc[4];
+        ld_words<1>(cg + 208, hd);
+        ld_words<4>(cg + 192, sc);
+        const float d = h2f_ref(hd[0] & 0xFFFFu);
+#pragma unroll
+        for (int n = 0; n < 2; ++n) {
+            uint32_t qa[8], qb[8], qh[8];
+            ld_words<8>(cg + 64 * n, qa);
+            ld_words<8>(cg + 64 * n + 32, qb);
+            ld_words<8>(cg + 128 + 32 * n, qh);
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+#pragma unroll
+                for (int lh = 0; lh < 2; ++lh) {
+                    const int j = 8 * n + 2 * t + lh;
+                    const float D = d * static_cast<float>(static_cast<int8_t>((sc[j >> 2] >> (8 * (j & 3))) & 0xFFu));
+                    uint32_t q[4];
+#pragma unroll
+                    for (int v = 0; v < 4; ++v) {
+                        const uint32_t src = (t & 1) ? qb[4 * lh + v] : qa[4 * lh + v];
+                        const uint32_t nib = (t & 2) ? ((src >> 4) & 0x0F0F0F0Fu) : (src & 0x0F0F0F0Fu);
+                        q[v] = nib | (((qh[4 * lh + v] >> (2 * t)) & 0x03030303u) << 4);
+                    }
+                    run_dot<false, 4, NT>(q, D, 32.0f * D, X, 128 * n + 32 * t + 16 * lh, acc, ntok);
+                }
             }
         }
     }
@@ -206,23 +359,18 @@ template <> struct Gv<F_Q6_K> {
 
 // ------------------------------------------------------ activation prep
 
-// One warp per (token, 32-element block).  Output position p of a block
-// holds element perm(p): identity, or for Q4_0 the even elements of each
-// 8-run followed by its odd elements.
-__global__ void act_prep_kernel(const float* __restrict__ x, int64_t K, int64_t ntok, int x_tokmajor, int perm_q4_0,
+// One warp per (token, 32-element block).  Position p of a block holds
+// element perm(p): identity, or (Q4_0) the 16 even elements then the 16 odd.
+__global__ void act_prep_kernel(const float* __restrict__ x, int64_t K, int64_t ntok, int x_tokmajor, int perm,
                                 int64_t Kp, int8_t* __restrict__ xhi, int8_t* __restrict__ xlo,
-                                float* __restrict__ xu, float* __restrict__ xs8, int* __restrict__ err) {
+                                float* __restrict__ xu, float* __restrict__ xs16, int* __restrict__ err) {
     const int lane = threadIdx.x & 31;
     if (blockIdx.x == 0 && threadIdx.x == 0) *err = 0;  // status word of this call
     const int64_t wid = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int64_t nblk = Kp / 32;
     if (wid >= nblk * ntok) return;
     const int64_t tok = wid / nblk, cb = wid - tok * nblk;
-    int e = lane;
-    if (perm_q4_0) {
-        int p = lane & 7;
-        e = (lane & ~7) + ((p < 4) ? 2 * p : 2 * (p - 4) + 1);
-    }
+    const int e = perm ? ((lane < 16) ? 2 * lane : 2 * (lane - 16) + 1) : lane;
     const int64_t k = cb * 32 + e;
     float v = 0.0f;
     if (k < K) v = x_tokmajor ? x[tok * K + k] : x[k * ntok + tok];
@@ -233,272 +381,208 @@ __global__ void act_prep_kernel(const float* __restrict__ x, int64_t K, int64_t 
     int hi = 0, lo = 0;
     if (amax > 0.0f && amax <= 3.0e38f) {
         u = amax * (1.0f / 32258.0f);  // 127 * 254
-        float shi = u * 254.0f;
+        const float shi = u * 254.0f;
         hi = max(-127, min(127, __float2int_rn(v / shi)));
-        float r = fmaf(-static_cast<float>(hi), shi, v);
+        const float r = fmaf(-static_cast<float>(hi), shi, v);
         lo = max(-127, min(127, __float2int_rn(r / u)));
     }
     float s = v;
 #pragma unroll
-    for (int o = 1; o < 8; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    for (int o = 1; o < 16; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     const int64_t base = tok * Kp + cb * 32 + lane;
     xhi[base] = static_cast<int8_t>(hi);
     xlo[base] = static_cast<int8_t>(lo);
     if (lane == 0) xu[tok * nblk + cb] = u;
-    if ((lane & 7) == 0) xs8[tok * (Kp / 8) + cb * 4 + (lane >> 3)] = s;
+    if ((lane & 15) == 0) xs16[tok * (Kp / 16) + cb * 2 + (lane >> 4)] = s;
 }
 
 // ------------------------------------------------------------- the GEMV
 
 struct GemvArgs {
     const uint8_t* w;
-    int64_t rows, row_bytes;
-    int64_t Kp;              // padded activation length (blocks per row * block elems)
+    int64_t rows, rb;        // rows and bytes per packed row
+    int nblk_row;            // blocks per row
+    int ncg;                 // column groups per row
+    int nks;                 // K-steps per 16-row unit (8 CGs each)
+    int64_t units;
+    int rs;                  // shared-memory row stride of a stage
+    int stage_bytes, nstages;
     const int8_t* xhi;
     const int8_t* xlo;
     const float* xu;
-    const float* xs8;
+    const float* xs16;
+    int64_t Kp;
     int ntok;
     float* out;
-    int out_tokmajor;        // 0: out[row*ntok + tok]; 1: out[tok*rows + row]
-    int R;                   // rows per tile
-    int64_t ntiles;
-    int stage_bytes;
-    int nchunks;             // chunks per row
+    int64_t out_ld;          // row stride of out ([M x ld] or [ntok x ld] when token-major)
+    int out_tokmajor;
     int* err;
 };
 
-template <int MG> struct ActRegs {
-    uint32_t hi[MG][8], lo[MG][8];
-    float u[MG][4], sx[MG][4];
-};
-
-template <int F, int MG>
-__device__ __forceinline__ void load_act(const GemvArgs& a, int tok0, int b, int c, ActRegs<MG>& A) {
-    using G = Gv<F>;
-    constexpr int RL = 32 / G::NR;  // elements per run
-    constexpr int WPR = RL / 4;     // words per run
-#pragma unroll
-    for (int m = 0; m < MG; ++m) {
-        const int tok = min(tok0 + m, a.ntok - 1);
-        const int8_t* hi = a.xhi + static_cast<int64_t>(tok) * a.Kp;
-        const int8_t* lo = a.xlo + static_cast<int64_t>(tok) * a.Kp;
-#pragma unroll
-        for (int r = 0; r < G::NR; ++r) {
-            const int64_t k = static_cast<int64_t>(b) * Traits<F>::BE + G::k0(c, r);
-            if (WPR == 2) {
-                uint2 h = __ldg(reinterpret_cast<const uint2*>(hi + k));
-                uint2 l = __ldg(reinterpret_cast<const uint2*>(lo + k));
-                A.hi[m][r * 2] = h.x; A.hi[m][r * 2 + 1] = h.y;
-                A.lo[m][r * 2] = l.x; A.lo[m][r * 2 + 1] = l.y;
-            } else {
-#pragma unroll
-                for (int v = 0; v < WPR / 4; ++v) {
-                    uint4 h = __ldg(reinterpret_cast<const uint4*>(hi + k) + v);
-                    uint4 l = __ldg(reinterpret_cast<const uint4*>(lo + k) + v);
-                    A.hi[m][r * WPR + 4 * v] = h.x; A.hi[m][r * WPR + 4 * v + 1] = h.y;
-                    A.hi[m][r * WPR + 4 * v + 2] = h.z; A.hi[m][r * WPR + 4 * v + 3] = h.w;
-                    A.lo[m][r * WPR + 4 * v] = l.x; A.lo[m][r * WPR + 4 * v + 1] = l.y;
-                    A.lo[m][r * WPR + 4 * v + 2] = l.z; A.lo[m][r * WPR + 4 * v + 3] = l.w;
-                }
-            }
-            A.u[m][r] = __ldg(a.xu + static_cast<int64_t>(tok) * (a.Kp / 32) + k / 32);
-            float s = 0.0f;
-#pragma unroll
-            for (int v = 0; v < RL / 8; ++v) s += __ldg(a.xs8 + static_cast<int64_t>(tok) * (a.Kp / 8) + k / 8 + v);
-            A.sx[m][r] = s;
-        }
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
     }
+    return false;
 }
 
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
-
-// Issues the copy of tile `t` into stage buffer `buf` (thread 0 only).
-__device__ __forceinline__ void issue_tile(const GemvArgs& a, int64_t t, uint8_t* buf, uint64_t* bar) {
-    const int64_t row0 = t * a.R;
-    const int64_t nr = min64(a.R, a.rows - row0);
-    const uintptr_t gs = reinterpret_cast<uintptr_t>(a.w) + static_cast<uintptr_t>(row0 * a.row_bytes);
-    const uintptr_t ge = gs + static_cast<uintptr_t>(nr * a.row_bytes);
-    const uintptr_t base = gs & ~static_cast<uintptr_t>(15);
-    uintptr_t A16 = (gs + 15) & ~static_cast<uintptr_t>(15);
-    uintptr_t E16 = ge & ~static_cast<uintptr_t>(15);
-    if (A16 >= E16) {
-        A16 = ge;  // no aligned body: everything is head bytes
-        E16 = ge;
-    }
-    for (uintptr_t g = gs; g < A16; ++g) buf[g - base] = *reinterpret_cast<const uint8_t*>(g);
-    for (uintptr_t g = E16; g < ge; ++g) buf[g - base] = *reinterpret_cast<const uint8_t*>(g);
-    const uint32_t body = static_cast<uint32_t>(E16 - A16);
-    if (body) {
-        mbar_arrive_expect_tx(bar, body);
-        bulk_g2s(buf + (A16 - base), reinterpret_cast<const void*>(A16), body, bar);
-    } else {
-        mbar_arrive(bar);
-    }
-}
-
-template <int F, int MG>
-__global__ void __launch_bounds__(kMaxThreads) gemv_kernel(GemvArgs a) {
-    using G = Gv<F>;
+template <int F, int NT, int AL>
+__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvArgs a) {
+    using L = Lane<F>;
     extern __shared__ __align__(128) uint8_t smem[];
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
-    float* red = reinterpret_cast<float*>(smem + 64);  // [warps][kMaxRows*MG]
-    uint8_t* stages = smem + 64 + (kMaxThreads / 32) * kMaxRows * MG * 4;
-    __shared__ int s_abort;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + kMaxStages;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kMaxStages);
+    float* red = reinterpret_cast<float*>(smem + kHeaderBytes);  // [2][warps][16][NT]
+    uint8_t* stages = smem + kHeaderBytes + ((2 * kConsumerWarps * kUnitRows * NT * 4 + 127) / 128) * 128;
 
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
-        for (int s = 0; s < kStages; ++s) mbar_init(&bars[s], 1);
+        for (int s = 0; s < kMaxStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
+        *abort_flag = 0;
         fence_mbar_init();
-        s_abort = 0;
     }
     __syncthreads();
 
-    const int64_t first = blockIdx.x, stride = gridDim.x;
-    // Thread 0 tracks, per stage, the iteration whose copy is in flight.
-    int pending[kStages];
-#pragma unroll
-    for (int s = 0; s < kStages; ++s) pending[s] = -1;
-    if (tid == 0) {
-        for (int s = 0; s < kStages; ++s) {
-            int64_t t = first + s * stride;
-            if (t < a.ntiles) {
-                issue_tile(a, t, stages + s * a.stage_bytes, &bars[s]);
-                pending[s] = s;
-            }
-        }
-    }
+    const uintptr_t wbase = reinterpret_cast<uintptr_t>(a.w);
+    const uintptr_t wend = wbase + static_cast<uintptr_t>(a.rows * a.rb);
+    const int64_t step_bytes = static_cast<int64_t>(kStageCG) * L::CGB;
 
-    const int cpt = (a.nchunks + blockDim.x - 1) / blockDim.x;
-    int it = 0;
-    for (int64_t t = first; t < a.ntiles; t += stride, ++it) {
-        const int s = it % kStages;
-        const uint32_t parity = (it / kStages) & 1;
-        if (!mbar_wait_bounded(&bars[s], parity)) {
-            s_abort = 1;
-            atomicExch(a.err, 1);
-        }
-        if (tid == 0) pending[s] = -1;
-        const int64_t row0 = t * a.R;
-        const int nr = static_cast<int>(min64(a.R, a.rows - row0));
-        const uintptr_t gs = reinterpret_cast<uintptr_t>(a.w) + static_cast<uintptr_t>(row0 * a.row_bytes);
-        const uint8_t* tile = stages + s * a.stage_bytes + (gs & 15);
-
-        for (int tok0 = 0; tok0 < a.ntok; tok0 += MG) {
-            float acc[kMaxRows][MG];
-#pragma unroll
-            for (int r = 0; r < kMaxRows; ++r)
-#pragma unroll
-                for (int m = 0; m < MG; ++m) acc[r][m] = 0.0f;
-
-            for (int ci = 0; ci < cpt; ++ci) {
-                const int ch = tid + ci * blockDim.x;
-                if (ch >= a.nchunks) break;
-                const int b = ch / G::CPB, c = ch - b * G::CPB;
-                ActRegs<MG> A;
-                load_act<F, MG>(a, tok0, b, c, A);
-#pragma unroll
-                for (int r = 0; r < kMaxRows; ++r) {
-                    if (r < nr) {
-                        uint32_t q[8];
-                        float D[4], Mo[4];
-                        G::load(tile + static_cast<int64_t>(r) * a.row_bytes + static_cast<int64_t>(b) * Traits<F>::BB,
-                                c, q, D, Mo);
-#pragma unroll
-                        for (int m = 0; m < MG; ++m) {
-#pragma unroll
-                            for (int rr = 0; rr < G::NR; ++rr) {
-                                constexpr int WPR = 8 / G::NR;
-                                int sh = 0, sl = 0;
-#pragma unroll
-                                for (int v = 0; v < WPR; ++v) {
-                                    sh = dp4a_s8(q[rr * WPR + v], A.hi[m][rr * WPR + v], sh);
-                                    sl = dp4a_s8(q[rr * WPR + v], A.lo[m][rr * WPR + v], sl);
-                                }
-                                const int S = sh * 254 + sl;
-                                acc[r][m] = fmaf(D[rr] * A.u[m][rr], static_cast<float>(S), acc[r][m]);
-                                acc[r][m] = fmaf(-Mo[rr], A.sx[m][rr], acc[r][m]);
-                            }
+    if (warp == kConsumerWarps) {
+        // ---------------- producer warp: lane r copies row r of each stage ----
+        int it = 0;
+        for (int64_t u = blockIdx.x; u < a.units; u += gridDim.x) {
+            for (int ks = 0; ks < a.nks; ++ks, ++it) {
+                const int s = it % a.nstages;
+                if (it >= a.nstages) {
+                    if (!wait_or_abort(&empty[s], ((it / a.nstages) - 1) & 1, abort_flag)) {
+                        if (lane == 0) {
+                            *abort_flag = 1;
+                            atomicExch(a.err, 1);
                         }
+                        return;
                     }
                 }
-            }
-            // CTA reduction of the nr x MG partial sums.
-#pragma unroll
-            for (int r = 0; r < kMaxRows; ++r) {
-                if (r < nr) {
-#pragma unroll
-                    for (int m = 0; m < MG; ++m) {
-                        float v = warp_sum(acc[r][m]);
-                        if (lane == 0) red[warp * (kMaxRows * MG) + r * MG + m] = v;
+                uint8_t* st = stages + s * a.stage_bytes;
+                const int64_t off = static_cast<int64_t>(ks) * step_bytes;
+                const int64_t seg = min64(step_bytes, a.rb - off);
+                const int64_t row = u * kUnitRows + lane;
+                uint32_t my_tx = 0;
+                bool bulk = false;
+                uintptr_t lo = 0;
+                if (lane < kUnitRows && row < a.rows) {
+                    const uintptr_t ga = wbase + static_cast<uintptr_t>(row * a.rb + off);
+                    const uintptr_t gb = ga + static_cast<uintptr_t>(seg);
+                    lo = ga & ~static_cast<uintptr_t>(15);
+                    const uintptr_t hi = (gb + 15) & ~static_cast<uintptr_t>(15);
+                    if (lo >= wbase && hi <= wend) {
+                        bulk = true;
+                        my_tx = static_cast<uint32_t>(hi - lo);
+                    } else {
+                        // the 16-byte-rounded range would leave the buffer
+                        uint8_t* dst = st + lane * a.rs + (ga & 15);
+                        for (uintptr_t g = ga; g < gb; ++g) dst[g - ga] = *reinterpret_cast<const uint8_t*>(g);
                     }
                 }
-            }
-            __syncthreads();
-            if (tid < nr * MG) {
-                const int r = tid / MG, m = tid - r * MG;
-                float v = 0.0f;
-                for (int w2 = 0; w2 < nwarps; ++w2) v += red[w2 * (kMaxRows * MG) + tid];
-                const int tok = tok0 + m;
-                const int64_t row = row0 + r;
-                if (tok < a.ntok) {
-                    if (a.out_tokmajor) a.out[static_cast<int64_t>(tok) * a.rows + row] = v;
-                    else a.out[row * a.ntok + tok] = v;
+                const uint32_t tx = __reduce_add_sync(0xffffffffu, my_tx);
+                __syncwarp();
+                if (lane == 0) {
+                    if (tx) mbar_arrive_expect_tx(&full[s], tx);
+                    else mbar_arrive(&full[s]);
                 }
-            }
-            __syncthreads();
-        }
-        if (s_abort) break;
-        if (tid == 0) {
-            const int64_t nt = t + kStages * stride;
-            if (nt < a.ntiles) {
-                issue_tile(a, nt, stages + s * a.stage_bytes, &bars[s]);
-                pending[s] = it + kStages;
+                __syncwarp();
+                if (bulk) bulk_g2s(st + lane * a.rs, reinterpret_cast<const void*>(lo), my_tx, &full[s]);
             }
         }
+        return;
     }
-    if (s_abort && tid == 0) {
-        // Let copies already in flight land before the CTA exits (bounded).
-        for (int s = 0; s < kStages; ++s)
-            if (pending[s] >= 0) mbar_wait_bounded(&bars[s], (pending[s] / kStages) & 1);
+
+    // ---------------- consumer warps ----------------
+    const int r = lane & 15, cgl = 2 * warp + (lane >> 4);  // row in unit, CG in stage
+    float acc[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
+    int it = 0, unit_par = 0;
+    for (int64_t u = blockIdx.x; u < a.units; u += gridDim.x, unit_par ^= 1) {
+        const int64_t row = u * kUnitRows + r;
+        const bool row_ok = row < a.rows;
+        for (int ks = 0; ks < a.nks; ++ks, ++it) {
+            const int s = it % a.nstages;
+            if (!wait_or_abort(&full[s], (it / a.nstages) & 1, abort_flag)) {
+                if (lane == 0) {
+                    *abort_flag = 1;
+                    atomicExch(a.err, 1);
+                }
+            }
+            const int cg = ks * kStageCG + cgl;
+            if (row_ok && cg < a.ncg && !*abort_flag) {
+                const uintptr_t ga = wbase + static_cast<uintptr_t>(row * a.rb + static_cast<int64_t>(ks) * step_bytes);
+                const uint8_t* cgp = stages + s * a.stage_bytes + r * a.rs + (ga & 15) + cgl * L::CGB;
+                ActCG<NT> X;
+                const int64_t k0 = static_cast<int64_t>(cg) * 256;
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    const int tt = min(t, a.ntok - 1);
+                    X.hi[t] = a.xhi + tt * a.Kp + k0;
+                    X.lo[t] = a.xlo + tt * a.Kp + k0;
+                    X.u[t] = a.xu + tt * (a.Kp / 32) + k0 / 32;
+                    X.s16[t] = a.xs16 + tt * (a.Kp / 16) + k0 / 16;
+                }
+                L::template process<AL, NT>(cgp, a.nblk_row - cg * 8, X, acc, a.ntok);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        // combine the two column groups of each lane pair, then the warps
+        float* rp = red + unit_par * (kConsumerWarps * kUnitRows * NT);
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            const float v = acc[t] + __shfl_xor_sync(0xffffffffu, acc[t], 16);
+            if (lane < 16) rp[(warp * kUnitRows + lane) * NT + t] = v;
+            acc[t] = 0.0f;
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+        if (warp == 0 && lane < 16 && row_ok) {
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                if (t < a.ntok) {
+                    float v = 0.0f;
+#pragma unroll
+                    for (int w2 = 0; w2 < kConsumerWarps; ++w2) v += rp[(w2 * kUnitRows + lane) * NT + t];
+                    if (a.out_tokmajor) a.out[t * a.out_ld + row] = v;
+                    else a.out[row * a.out_ld + t] = v;
+                }
+            }
+        }
     }
 }
 
 struct GemvPlan {
-    int threads, R, stage_bytes, smem, grid;
-    int64_t ntiles;
-    int nchunks;
+    int rs, stage_bytes, nstages, smem, grid;
 };
 
 template <int F>
-GemvPlan plan_gemv(int64_t rows, int64_t K, int mg) {
+GemvPlan plan_gemv(int nt) {
+    using L = Lane<F>;
     GemvPlan p{};
-    const int64_t bpr = (K + Traits<F>::BE - 1) / Traits<F>::BE;
-    const int64_t rb = bpr * Traits<F>::BB;
-    p.nchunks = static_cast<int>(bpr * Gv<F>::CPB);
-    p.threads = static_cast<int>(std::min<int64_t>(kMaxThreads, ((p.nchunks + 31) / 32) * 32));
-    if (p.threads < 64) p.threads = 64;
-    const int sms = device_sm_count();
-    int R = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(kMaxRows, (24 * 1024) / rb)));
-    while (R > 1 && (rows + R - 1) / R < 8 * sms) --R;
-    p.R = R;
-    p.ntiles = (rows + R - 1) / R;
-    p.stage_bytes = static_cast<int>(((R * rb + 16 + 16) + 127) / 128 * 128);
-    p.smem = 64 + (kMaxThreads / 32) * kMaxRows * mg * 4 + kStages * p.stage_bytes;
-    int per_sm = std::max(1, std::min(4, (220 * 1024) / std::max(1, p.smem)));
-    p.grid = static_cast<int>(std::min<int64_t>(p.ntiles, static_cast<int64_t>(sms) * per_sm));
+    // Row stride: the segment, 16 bytes of alignment slack, 4 bytes of
+    // over-read slack; then padded to 16 mod 128 to spread smem banks.
+    p.rs = ((kStageCG * L::CGB + 32 + 127) / 128) * 128 + 16;
+    p.stage_bytes = kUnitRows * p.rs;
+    const int red_bytes = ((2 * kConsumerWarps * kUnitRows * nt * 4 + 127) / 128) * 128;
+    const int budget = 200 * 1024 - kHeaderBytes - red_bytes;
+    p.nstages = std::max(2, std::min(kMaxStages, budget / p.stage_bytes));
+    p.smem = kHeaderBytes + red_bytes + p.nstages * p.stage_bytes;
     return p;
 }
 
-template <int F, int MG>
-cudaError_t launch_gemv_mg(const GemvPlan& p, GemvArgs a, cudaStream_t s) {
-    auto kern = gemv_kernel<F, MG>;
-    // Opt in to the dynamic shared memory this launch needs (largest value
-    // seen so far, per device).
+template <int F, int NT, int AL>
+cudaError_t launch_nt(const GemvPlan& p, const GemvArgs& a, cudaStream_t s) {
+    auto kern = gemv_kernel<F, NT, AL>;
     static int configured[64] = {0};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -508,52 +592,76 @@ cudaError_t launch_gemv_mg(const GemvPlan& p, GemvArgs a, cudaStream_t s) {
         if (e != cudaSuccess) return e;
         configured[dev] = p.smem;
     }
-    kern<<<p.grid, p.threads, p.smem, s>>>(a);
+    kern<<<p.grid, kThreads, p.smem, s>>>(a);
     return cudaGetLastError();
+}
+
+template <int F, int AL>
+cudaError_t launch_al(const GemvPlan& p, const GemvArgs& a, int nt, cudaStream_t s) {
+    switch (nt) {
+        case 1: return launch_nt<F, 1, AL>(p, a, s);
+        case 2: return launch_nt<F, 2, AL>(p, a, s);
+        case 4: return launch_nt<F, 4, AL>(p, a, s);
+        default: return launch_nt<F, 8, AL>(p, a, s);
+    }
 }
 
 template <int F>
 cudaError_t launch_gemv(const void* w, const float* x, float* out, int64_t M, int64_t K, int64_t N, int flags,
                         void* ws, size_t ws_bytes, int* err, cudaStream_t s) {
-    const int64_t bpr = (K + Traits<F>::BE - 1) / Traits<F>::BE;
-    const int64_t Kp = bpr * Traits<F>::BE;
+    using L = Lane<F>;
+    constexpr int BE = Traits<F>::BE, BB = Traits<F>::BB;
+    const int64_t bpr = (K + BE - 1) / BE;
+    const int64_t Kp = bpr * BE;
     GemvWorkspace wl = gemv_workspace_layout(Kp, N);
     if (ws_bytes < wl.total) return cudaErrorInvalidValue;
     auto* base = static_cast<uint8_t*>(ws);
     int8_t* xhi = reinterpret_cast<int8_t*>(base + wl.off_hi);
     int8_t* xlo = reinterpret_cast<int8_t*>(base + wl.off_lo);
     float* xu = reinterpret_cast<float*>(base + wl.off_u);
-    float* xs8 = reinterpret_cast<float*>(base + wl.off_s8);
+    float* xs16 = reinterpret_cast<float*>(base + wl.off_s16);
     {
         const int64_t warps = (Kp / 32) * N;
-        const int per_cta = 8;
-        const int64_t grid = (warps + per_cta - 1) / per_cta;
-        act_prep_kernel<<<static_cast<unsigned>(grid), per_cta * 32, 0, s>>>(
-            x, K, N, (flags & AXQ_FLAG_B_TOKMAJOR) ? 1 : 0, F == F_Q4_0 ? 1 : 0, Kp, xhi, xlo, xu, xs8, err);
+        const int64_t grid = (warps + 7) / 8;
+        act_prep_kernel<<<static_cast<unsigned>(grid), 256, 0, s>>>(x, K, N, (flags & AXQ_FLAG_B_TOKMAJOR) ? 1 : 0,
+                                                                    L::PERM, Kp, xhi, xlo, xu, xs16, err);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
-    const int mg = (N >= 2) ? 2 : 1;
-    GemvPlan p = plan_gemv<F>(M, K, mg);
     GemvArgs a{};
     a.w = static_cast<const uint8_t*>(w);
     a.rows = M;
-    a.row_bytes = bpr * Traits<F>::BB;
+    a.rb = bpr * BB;
+    a.nblk_row = static_cast<int>(bpr);
+    a.ncg = static_cast<int>((bpr * BB + L::CGB - 1) / L::CGB);
+    a.nks = (a.ncg + kStageCG - 1) / kStageCG;
+    a.units = (M + kUnitRows - 1) / kUnitRows;
     a.Kp = Kp;
-    a.xhi = xhi;
-    a.xlo = xlo;
-    a.xu = xu;
-    a.xs8 = xs8;
-    a.ntok = static_cast<int>(N);
-    a.out = out;
     a.out_tokmajor = (flags & AXQ_FLAG_OUT_TOKMAJOR) ? 1 : 0;
-    a.R = p.R;
-    a.ntiles = p.ntiles;
-    a.stage_bytes = p.stage_bytes;
-    a.nchunks = p.nchunks;
+    a.out_ld = a.out_tokmajor ? M : N;
     a.err = err;
-    if (mg == 2) return launch_gemv_mg<F, 2>(p, a, s);
-    return launch_gemv_mg<F, 1>(p, a, s);
+    // Natural alignment holds when the buffer and every row start are
+    // 16-byte aligned; otherwise every format takes the any-alignment loads.
+    const bool aligned = (reinterpret_cast<uintptr_t>(w) % 16 == 0) && (a.rb % 16 == 0);
+    const int sms = device_sm_count();
+    for (int64_t t0 = 0; t0 < N; t0 += 8) {
+        const int nt_run = static_cast<int>(std::min<int64_t>(8, N - t0));
+        const int nt = nt_run == 1 ? 1 : nt_run == 2 ? 2 : nt_run <= 4 ? 4 : 8;
+        GemvPlan p = plan_gemv<F>(nt);
+        p.grid = static_cast<int>(std::min<int64_t>(a.units, static_cast<int64_t>(sms)));
+        a.rs = p.rs;
+        a.stage_bytes = p.stage_bytes;
+        a.nstages = p.nstages;
+        a.xhi = xhi + t0 * Kp;
+        a.xlo = xlo + t0 * Kp;
+        a.xu = xu + t0 * (Kp / 32);
+        a.xs16 = xs16 + t0 * (Kp / 16);
+        a.ntok = nt_run;
+        a.out = a.out_tokmajor ? out + t0 * M : out + t0;
+        cudaError_t e = (aligned && L::A > 1) ? launch_al<F, L::A>(p, a, nt, s) : launch_al<F, 1>(p, a, nt, s);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 }  // namespace
@@ -564,8 +672,8 @@ GemvWorkspace gemv_workspace_layout(int64_t Kp, int64_t ntok) {
     w.off_hi = 0;
     w.off_lo = up(static_cast<size_t>(Kp * ntok));
     w.off_u = w.off_lo + up(static_cast<size_t>(Kp * ntok));
-    w.off_s8 = w.off_u + up(static_cast<size_t>((Kp / 32) * ntok * 4));
-    w.total = w.off_s8 + up(static_cast<size_t>((Kp / 8) * ntok * 4));
+    w.off_s16 = w.off_u + up(static_cast<size_t>((Kp / 32) * ntok * 4));
+    w.total = w.off_s16 + up(static_cast<size_t>((Kp / 16) * ntok * 4));
     return w;
 }
 

@@ -18,7 +18,7 @@ cudaError_t dequant_dispatch(int fmt, const void* src, float* dst, int64_t rows,
 
 // Workspace for the block-quantized activations of a GEMV-class matmul.
 struct GemvWorkspace {
-    size_t off_hi, off_lo, off_u, off_s8, total;
+    size_t off_hi, off_lo, off_u, off_s16, total;
 };
 GemvWorkspace gemv_workspace_layout(int64_t Kp, int64_t ntok);
 

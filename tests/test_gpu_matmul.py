@@ -116,3 +116,21 @@ def test_matmul_full_size_rows_sampled(cuda, orc, fmt):
         ax.matmul_q(out, q, B, F, rows, K)
         y_ref = orc.matmul(fmt, qs, B.cpu().numpy(), 64, K)
         assert rel_err(out[torch.from_numpy(sel).cuda()].cpu().numpy(), y_ref) <= TOL
+
+
+@pytest.mark.parametrize("fmt", FORMATS)
+@pytest.mark.parametrize("offset", [2, 6, 16])
+def test_matmul_unaligned_weight_buffer(cuda, orc, fmt, offset):
+    """Packed weights starting at an odd 2-byte offset inside their buffer
+    (the copy pipeline then takes its byte-copy and any-alignment paths)."""
+    import torch
+    import axon_b200 as ax
+    rng = np.random.default_rng(offset)
+    for M, K in ((33, 4096), (20, 11008), (7, 700)):
+        q = orc.quantize(fmt, gen(rng, (M, K), "randn"))
+        buf = torch.zeros(q.size + offset, dtype=torch.uint8, device="cuda")
+        buf[offset:].copy_(torch.from_numpy(q))
+        B = rng.standard_normal((K, 3)).astype(np.float32)
+        out = torch.empty(M, 3, device="cuda")
+        ax.matmul_q(out, buf[offset:], torch.from_numpy(B).cuda(), ax.QuantFormat[fmt], M, K)
+        assert rel_err(out.cpu().numpy(), orc.matmul(fmt, q, B, M, K)) <= TOL, (fmt, offset, M, K)
