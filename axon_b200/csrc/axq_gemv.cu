@@ -78,41 +78,65 @@ template <int NT> struct ActCG {
     const float* s16[NT];
 };
 
-// One run of NW code words (4*NW elements starting at element k of the
-// column group) sharing weight scale D and offset Mo: acc += D*u*S - Mo*sum(x).
-template <bool SG, int NW, int NT>
-__device__ __forceinline__ void run_dot(const uint32_t* q, float D, float Mo, const ActCG<NT>& A, int k, float* acc,
-                                        int ntok) {
+// One 32-element activation block of one token: both int8 terms, the unit
+// scale and the two 16-element sums.
+struct ActBlk {
+    uint32_t h[8], l[8];
+    float u, s[2];
+};
+
+template <int NT>
+__device__ __forceinline__ void load_blk(const ActCG<NT>& A, int t, int k, ActBlk& B) {
 #pragma unroll
-    for (int t = 0; t < NT; ++t) {
-        if (t < ntok) {
-            uint32_t h[NW], l[NW];
-#pragma unroll
-            for (int v = 0; v < NW / 4; ++v) {
-                const uint4 hv = __ldg(reinterpret_cast<const uint4*>(A.hi[t] + k) + v);
-                const uint4 lv = __ldg(reinterpret_cast<const uint4*>(A.lo[t] + k) + v);
-                h[4 * v] = hv.x; h[4 * v + 1] = hv.y; h[4 * v + 2] = hv.z; h[4 * v + 3] = hv.w;
-                l[4 * v] = lv.x; l[4 * v + 1] = lv.y; l[4 * v + 2] = lv.z; l[4 * v + 3] = lv.w;
-            }
-            const float uu = __ldg(A.u[t] + k / 32);
-            float sx;
-            if constexpr (NW == 8) {
-                const float2 s2 = __ldg(reinterpret_cast<const float2*>(A.s16[t] + k / 16));
-                sx = s2.x + s2.y;
-            } else {
-                sx = __ldg(A.s16[t] + k / 16);
-            }
-            int sh = 0;
-#pragma unroll
-            for (int v = 0; v < NW; ++v) sh = dp4<SG>(q[v], h[v], sh);
-            int S = sh * 254;
-#pragma unroll
-            for (int v = 0; v < NW; ++v) S = dp4<SG>(q[v], l[v], S);
-            acc[t] = fmaf(D * uu, static_cast<float>(S), acc[t]);
-            acc[t] = fmaf(-Mo, sx, acc[t]);
-        }
+    for (int v = 0; v < 2; ++v) {
+        const uint4 hv = __ldg(reinterpret_cast<const uint4*>(A.hi[t] + k) + v);
+        const uint4 lv = __ldg(reinterpret_cast<const uint4*>(A.lo[t] + k) + v);
+        B.h[4 * v] = hv.x; B.h[4 * v + 1] = hv.y; B.h[4 * v + 2] = hv.z; B.h[4 * v + 3] = hv.w;
+        B.l[4 * v] = lv.x; B.l[4 * v + 1] = lv.y; B.l[4 * v + 2] = lv.z; B.l[4 * v + 3] = lv.w;
     }
+    B.u = __ldg(A.u[t] + k / 32);
+    const float2 s2 = __ldg(reinterpret_cast<const float2*>(A.s16[t] + k / 16));
+    B.s[0] = s2.x;
+    B.s[1] = s2.y;
 }
+
+// Accumulators: two parities (alternating runs) x {scale terms, offset terms}
+// so consecutive runs do not serialize on one register.
+template <int NT> struct Acc {
+    float d[2][NT], m[2][NT];
+};
+
+// Dot of NW code words (NW = 4: half HALF of the block; NW = 8: all of it)
+// with the block, weight scale D and offset Mo:
+//   acc += D*u*(254*dot(q,hi) + dot(q,lo)) - Mo*sum(x).
+// The four dp4a chains are independent to keep the pipes busy.
+template <bool SG, int NW, int HALF, int P, int NT>
+__device__ __forceinline__ void dot_run(const uint32_t* q, float D, float Mo, const ActBlk& B, Acc<NT>& acc, int t) {
+    constexpr int o = (NW == 8) ? 0 : 4 * HALF;
+    int h0 = 0, h1 = 0, l0 = 0, l1 = 0;
+#pragma unroll
+    for (int v = 0; v < NW; v += 2) {
+        h0 = dp4<SG>(q[v], B.h[o + v], h0);
+        h1 = dp4<SG>(q[v + 1], B.h[o + v + 1], h1);
+        l0 = dp4<SG>(q[v], B.l[o + v], l0);
+        l1 = dp4<SG>(q[v + 1], B.l[o + v + 1], l1);
+    }
+    const int S = (h0 + h1) * 254 + (l0 + l1);
+    const float sx = (NW == 8) ? (B.s[0] + B.s[1]) : B.s[HALF];
+    acc.d[P][t] = fmaf(D * B.u, static_cast<float>(S), acc.d[P][t]);
+    acc.m[P][t] = fmaf(Mo, sx, acc.m[P][t]);
+}
+
+// For every token t < ntok: load the activation block at element k and run
+// the body (which calls dot_run with token t).
+#define AXQ_FOR_TOKENS(k, xb, ...)                   \
+    _Pragma("unroll") for (int t = 0; t < NT; ++t) { \
+        if (t < ntok) {                              \
+            ActBlk xb;                               \
+            load_blk<NT>(X, t, (k), xb);             \
+            __VA_ARGS__                              \
+        }                                            \
+    }
 
 // Byte i (compile-time) of a little-endian word array.
 template <int I>
@@ -139,16 +163,27 @@ template <int F> struct Lane;
 // Q8_0: CG = 8 blocks {u16 d; i8 qs[32]}; one signed 32-element run each.
 template <> struct Lane<F_Q8_0> {
     static constexpr int CGB = 8 * 34, A = 1, PERM = 0;
+    template <int B, int NT>
+    __device__ static void blk(const uint8_t* cg, const ActCG<NT>& X, Acc<NT>& acc, int ntok) {
+        uint32_t hd[1], w[8];
+        ld_words<1>(cg + 34 * B, hd);
+        ld_words<8>(cg + 34 * B + 2, w);
+        const float d = h2f_ref(hd[0] & 0xFFFFu);
+        AXQ_FOR_TOKENS(32 * B, xb, dot_run<true, 8, 0, B & 1, NT>(w, d, 0.0f, xb, acc, t);)
+    }
     template <int AL, int NT>
-    __device__ static void process(const uint8_t* cg, int nblk_valid, const ActCG<NT>& X, float* acc, int ntok) {
-#pragma unroll
-        for (int b = 0; b < 8; ++b) {
-            if (b < nblk_valid) {
-                uint32_t hd[1], w[8];
-                ld_words<1>(cg + 34 * b, hd);
-                ld_words<8>(cg + 34 * b + 2, w);
-                run_dot<true, 8, NT>(w, h2f_ref(hd[0] & 0xFFFFu), 0.0f, X, 32 * b, acc, ntok);
-            }
+    __device__ static void process(const uint8_t* cg, int nblk_valid, const ActCG<NT>& X, Acc<NT>& acc, int ntok) {
+        if (nblk_valid >= 8) {
+            blk<0>(cg, X, acc, ntok); blk<1>(cg, X, acc, ntok); blk<2>(cg, X, acc, ntok); blk<3>(cg, X, acc, ntok);
+            blk<4>(cg, X, acc, ntok); blk<5>(cg, X, acc, ntok); blk<6>(cg, X, acc, ntok); blk<7>(cg, X, acc, ntok);
+        } else {
+            if (nblk_valid > 0) blk<0>(cg, X, acc, ntok);
+            if (nblk_valid > 1) blk<1>(cg, X, acc, ntok);
+            if (nblk_valid > 2) blk<2>(cg, X, acc, ntok);
+            if (nblk_valid > 3) blk<3>(cg, X, acc, ntok);
+            if (nblk_valid > 4) blk<4>(cg, X, acc, ntok);
+            if (nblk_valid > 5) blk<5>(cg, X, acc, ntok);
+            if (nblk_valid > 6) blk<6>(cg, X, acc, ntok);
         }
     }
 };
@@ -158,22 +193,33 @@ template <> struct Lane<F_Q8_0> {
 // prep orders each 32-block as evens then odds.
 template <> struct Lane<F_Q4_0> {
     static constexpr int CGB = 8 * 18, A = 1, PERM = 1;
+    template <int B, int NT>
+    __device__ static void blk(const uint8_t* cg, const ActCG<NT>& X, Acc<NT>& acc, int ntok) {
+        uint32_t hd[1], w[4], q[8];
+        ld_words<1>(cg + 18 * B, hd);
+        ld_words<4>(cg + 18 * B + 2, w);
+        const float d = h2f_ref(hd[0] & 0xFFFFu);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            q[j] = w[j] & 0x0F0F0F0Fu;
+            q[4 + j] = w[j] & 0xF0F0F0F0u;
+        }
+        AXQ_FOR_TOKENS(32 * B, xb, dot_run<false, 4, 0, 0, NT>(q, d, 8.0f * d, xb, acc, t);
+                       dot_run<false, 4, 1, 1, NT>(q + 4, d * 0.0625f, 8.0f * d, xb, acc, t);)
+    }
     template <int AL, int NT>
-    __device__ static void process(const uint8_t* cg, int nblk_valid, const ActCG<NT>& X, float* acc, int ntok) {
-#pragma unroll
-        for (int b = 0; b < 8; ++b) {
-            if (b < nblk_valid) {
-                uint32_t hd[1], w[4], q[4];
-                ld_words<1>(cg + 18 * b, hd);
-                ld_words<4>(cg + 18 * b + 2, w);
-                const float d = h2f_ref(hd[0] & 0xFFFFu);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) q[j] = w[j] & 0x0F0F0F0Fu;
-                run_dot<false, 4, NT>(q, d, 8.0f * d, X, 32 * b, acc, ntok);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) q[j] = w[j] & 0xF0F0F0F0u;
-                run_dot<false, 4, NT>(q, d * 0.0625f, 8.0f * d, X, 32 * b + 16, acc, ntok);
-            }
+    __device__ static void process(const uint8_t* cg, int nblk_valid, const ActCG<NT>& X, Acc<NT>& acc, int ntok) {
+        if (nblk_valid >= 8) {
+            blk<0>(cg, X, acc, ntok); blk<1>(cg, X, acc, ntok); blk<2>(cg, X, acc, ntok); blk<3>(cg, X, acc, ntok);
+            blk<4>(cg, X, acc, ntok); blk<5>(cg, X, acc, ntok); blk<6>(cg, X, acc, ntok); blk<7>(cg, X, acc, ntok);
+        } else {
+            if (nblk_valid > 0) blk<0>(cg, X, acc, ntok);
+            if (nblk_valid > 1) blk<1>(cg, X, acc, ntok);
+            if (nblk_valid > 2) blk<2>(cg, X, acc, ntok);
+            if (nblk_valid > 3) blk<3>(cg, X, acc, ntok);
+            if (nblk_valid > 4) blk<4>(cg, X, acc, ntok);
+            if (nblk_valid > 5) blk<5>(cg, X, acc, ntok);
+            if (nblk_valid > 6) blk<6>(cg, X, acc, ntok);
         }
     }
 };
@@ -183,7 +229,7 @@ template <> struct Lane<F_Q4_0> {
 template <> struct Lane<F_Q2_K> {
     static constexpr int CGB = 84, A = 4, PERM = 0;
     template <int AL, int NT>
-    __device__ static void process(const uint8_t* cg, int, const ActCG<NT>& X, float* acc, int ntok) {
+    __device__ static void process(const uint8_t* cg, int, const ActCG<NT>& X, Acc<NT>& acc, int ntok) {
         uint32_t hd[1], sc[4];
         ldw<1, AL>(cg, hd);
         ldw<4, AL>(cg + 4, sc);
@@ -194,17 +240,16 @@ template <> struct Lane<F_Q2_K> {
             ldw<8, AL>(cg + 20 + 32 * n, w);
 #pragma unroll
             for (int s = 0; s < 4; ++s) {
+                uint32_t q[8];
 #pragma unroll
-                for (int lh = 0; lh < 2; ++lh) {
-                    const int j = 8 * n + 2 * s + lh;
-                    const uint32_t scb = (sc[j >> 2] >> (8 * (j & 3))) & 0xFFu;
-                    uint32_t q[4];
-#pragma unroll
-                    for (int v = 0; v < 4; ++v) q[v] = w[4 * lh + v] & (0x03030303u << (2 * s));
-                    const float D = d * static_cast<float>(scb & 0xF) * (1.0f / static_cast<float>(1 << (2 * s)));
-                    run_dot<false, 4, NT>(q, D, mn * static_cast<float>(scb >> 4), X, 128 * n + 32 * s + 16 * lh, acc,
-                                          ntok);
-                }
+                for (int v = 0; v < 8; ++v) q[v] = w[v] & (0x03030303u << (2 * s));
+                const uint32_t sc0 = (sc[(8 * n + 2 * s) >> 2] >> (8 * ((2 * s) & 3))) & 0xFFu;
+                const uint32_t sc1 = (sc[(8 * n + 2 * s) >> 2] >> (8 * ((2 * s) & 3) + 8)) & 0xFFu;
+                const float inv = 1.0f / static_cast<float>(1 << (2 * s));
+                const float D0 = d * inv * static_cast<float>(sc0 & 0xF), M0 = mn * static_cast<float>(sc0 >> 4);
+                const float D1 = d * inv * static_cast<float>(sc1 & 0xF), M1 = mn * static_cast<float>(sc1 >> 4);
+                AXQ_FOR_TOKENS(128 * n + 32 * s, xb, dot_run<false, 4, 0, 0, NT>(q, D0, M0, xb, acc, t);
+                               dot_run<false, 4, 1, 1, NT>(q + 4, D1, M1, xb, acc, t);)
             }
         }
     }
@@ -214,35 +259,41 @@ template <> struct Lane<F_Q2_K> {
 // value = D*(code - 4), D = d * (6-bit scale - 32).
 template <> struct Lane<F_Q3_K> {
     static constexpr int CGB = 110, A = 1, PERM = 0;
+    template <int IS>
+    __device__ static float subscale(const uint32_t* s12, float d) {
+        constexpr int lo_byte = (IS < 8) ? IS : IS - 8, lo_sh = (IS < 8) ? 0 : 4;
+        const int lo4 = (s12[lo_byte >> 2] >> (8 * (lo_byte & 3) + lo_sh)) & 0xF;
+        const int hi2 = (s12[2] >> (8 * (IS & 3) + 2 * (IS >> 2))) & 3;
+        return d * static_cast<float>((lo4 | (hi2 << 4)) - 32);
+    }
+    template <int N, int S, int NT>
+    __device__ static void sblk(const uint32_t* w, const uint32_t* hm, const uint32_t* s12, float d,
+                                const ActCG<NT>& X, Acc<NT>& acc, int ntok) {
+        uint32_t q[8];
+#pragma unroll
+        for (int v = 0; v < 8; ++v)
+            q[v] = ((w[v] >> (2 * S)) & 0x03030303u) | (((hm[v] >> (4 * N + S)) & 0x01010101u) << 2);
+        const float D0 = subscale<8 * N + 2 * S>(s12, d), D1 = subscale<8 * N + 2 * S + 1>(s12, d);
+        AXQ_FOR_TOKENS(128 * N + 32 * S, xb, dot_run<false, 4, 0, 0, NT>(q, D0, 4.0f * D0, xb, acc, t);
+                       dot_run<false, 4, 1, 1, NT>(q + 4, D1, 4.0f * D1, xb, acc, t);)
+    }
     template <int AL, int NT>
-    __device__ static void process(const uint8_t* cg, int, const ActCG<NT>& X, float* acc, int ntok) {
-        uint32_t hd[1], s12[3], hm[8];
+    __device__ static void process(const uint8_t* cg, int, const ActCG<NT>& X, Acc<NT>& acc, int ntok) {
+        uint32_t hd[1], s12[3], hm[8], w[8];
         ld_words<1>(cg + 108, hd);
         ld_words<3>(cg + 96, s12);
         ld_words<8>(cg, hm);
         const float d = h2f_ref(hd[0] & 0xFFFFu);
-#pragma unroll
-        for (int n = 0; n < 2; ++n) {
-            uint32_t w[8];
-            ld_words<8>(cg + 32 + 32 * n, w);
-#pragma unroll
-            for (int s = 0; s < 4; ++s) {
-#pragma unroll
-                for (int lh = 0; lh < 2; ++lh) {
-                    const int is = 8 * n + 2 * s + lh;
-                    const int lo4 = (is < 8) ? ((s12[is >> 2] >> (8 * (is & 3))) & 0xF)
-                                             : ((s12[(is - 8) >> 2] >> (8 * ((is - 8) & 3) + 4)) & 0xF);
-                    const int hi2 = (s12[2] >> (8 * (is & 3) + 2 * (is >> 2))) & 3;
-                    const float D = d * static_cast<float>((lo4 | (hi2 << 4)) - 32);
-                    uint32_t q[4];
-#pragma unroll
-                    for (int v = 0; v < 4; ++v)
-                        q[v] = ((w[4 * lh + v] >> (2 * s)) & 0x03030303u) |
-                               (((hm[4 * lh + v] >> (4 * n + s)) & 0x01010101u) << 2);
-                    run_dot<false, 4, NT>(q, D, 4.0f * D, X, 128 * n + 32 * s + 16 * lh, acc, ntok);
-                }
-            }
-        }
+        ld_words<8>(cg + 32, w);
+        sblk<0, 0, NT>(w, hm, s12, d, X, acc, ntok);
+        sblk<0, 1, NT>(w, hm, s12, d, X, acc, ntok);
+        sblk<0, 2, NT>(w, hm, s12, d, X, acc, ntok);
+        sblk<0, 3, NT>(w, hm, s12, d, X, acc, ntok);
+        ld_words<8>(cg + 64, w);
+        sblk<1, 0, NT>(w, hm, s12, d, X, acc, ntok);
+        sblk<1, 1, NT>(w, hm, s12, d, X, acc, ntok);
+        sblk<1, 2, NT>(w, hm, s12, d, X, acc, ntok);
+        sblk<1, 3, NT>(w, hm, s12, d, X, acc, ntok);
     }
 };
 
@@ -250,44 +301,44 @@ template <> struct Lane<F_Q3_K> {
 // of qs[32c + l]; high nibbles masked in place (1/16 in D).
 template <> struct Lane<F_Q4_K> {
     static constexpr int CGB = 144, A = 16, PERM = 0;
-    template <int G, int AL, int NT>
+    template <int G, int NT>
     __device__ static void group(const uint32_t* hw, const uint32_t* w, float d, float mn, const ActCG<NT>& X,
-                                 float* acc, int ntok) {
+                                 Acc<NT>& acc, int ntok) {
         int sc, m;
         k4sm<G>(hw, sc, m);
         uint32_t q[8];
 #pragma unroll
         for (int v = 0; v < 8; ++v) q[v] = w[v] & ((G & 1) ? 0xF0F0F0F0u : 0x0F0F0F0Fu);
-        const float D = d * static_cast<float>(sc) * ((G & 1) ? 0.0625f : 1.0f);
-        run_dot<false, 8, NT>(q, D, mn * static_cast<float>(m), X, 32 * G, acc, ntok);
+        const float D = d * static_cast<float>(sc) * ((G & 1) ? 0.0625f : 1.0f), Mg = mn * static_cast<float>(m);
+        AXQ_FOR_TOKENS(32 * G, xb, dot_run<false, 8, 0, G & 1, NT>(q, D, Mg, xb, acc, t);)
     }
     template <int AL, int NT>
-    __device__ static void process(const uint8_t* cg, int, const ActCG<NT>& X, float* acc, int ntok) {
+    __device__ static void process(const uint8_t* cg, int, const ActCG<NT>& X, Acc<NT>& acc, int ntok) {
         uint32_t hw[4];
         ldw<4, AL>(cg, hw);
         const float d = h2f_ref(hw[0] & 0xFFFFu), mn = h2f_ref(hw[0] >> 16);
         uint32_t w[8];
         ldw<8, AL>(cg + 16, w);
-        group<0, AL, NT>(hw, w, d, mn, X, acc, ntok);
-        group<1, AL, NT>(hw, w, d, mn, X, acc, ntok);
+        group<0, NT>(hw, w, d, mn, X, acc, ntok);
+        group<1, NT>(hw, w, d, mn, X, acc, ntok);
         ldw<8, AL>(cg + 48, w);
-        group<2, AL, NT>(hw, w, d, mn, X, acc, ntok);
-        group<3, AL, NT>(hw, w, d, mn, X, acc, ntok);
+        group<2, NT>(hw, w, d, mn, X, acc, ntok);
+        group<3, NT>(hw, w, d, mn, X, acc, ntok);
         ldw<8, AL>(cg + 80, w);
-        group<4, AL, NT>(hw, w, d, mn, X, acc, ntok);
-        group<5, AL, NT>(hw, w, d, mn, X, acc, ntok);
+        group<4, NT>(hw, w, d, mn, X, acc, ntok);
+        group<5, NT>(hw, w, d, mn, X, acc, ntok);
         ldw<8, AL>(cg + 112, w);
-        group<6, AL, NT>(hw, w, d, mn, X, acc, ntok);
-        group<7, AL, NT>(hw, w, d, mn, X, acc, ntok);
+        group<6, NT>(hw, w, d, mn, X, acc, ntok);
+        group<7, NT>(hw, w, d, mn, X, acc, ntok);
     }
 };
 
 // Q5_K {d, dmin, scales[12], qh[32], qs[128]}: as Q4_K plus bit g of qh[l].
 template <> struct Lane<F_Q5_K> {
     static constexpr int CGB = 176, A = 16, PERM = 0;
-    template <int G, int AL, int NT>
+    template <int G, int NT>
     __device__ static void group(const uint32_t* hw, const uint32_t* qh, const uint32_t* w, float d, float mn,
-                                 const ActCG<NT>& X, float* acc, int ntok) {
+                                 const ActCG<NT>& X, Acc<NT>& acc, int ntok) {
         int sc, m;
         k4sm<G>(hw, sc, m);
         uint32_t q[8];
@@ -297,27 +348,28 @@ template <> struct Lane<F_Q5_K> {
             const uint32_t hb = (G <= 4) ? ((qh[v] << (4 - G)) & 0x10101010u) : ((qh[v] >> (G - 4)) & 0x10101010u);
             q[v] = nib | hb;
         }
-        run_dot<false, 8, NT>(q, d * static_cast<float>(sc), mn * static_cast<float>(m), X, 32 * G, acc, ntok);
+        const float D = d * static_cast<float>(sc), Mg = mn * static_cast<float>(m);
+        AXQ_FOR_TOKENS(32 * G, xb, dot_run<false, 8, 0, G & 1, NT>(q, D, Mg, xb, acc, t);)
     }
     template <int AL, int NT>
-    __device__ static void process(const uint8_t* cg, int, const ActCG<NT>& X, float* acc, int ntok) {
+    __device__ static void process(const uint8_t* cg, int, const ActCG<NT>& X, Acc<NT>& acc, int ntok) {
         uint32_t hw[4], qh[8];
         ldw<4, AL>(cg, hw);
         ldw<8, AL>(cg + 16, qh);
         const float d = h2f_ref(hw[0] & 0xFFFFu), mn = h2f_ref(hw[0] >> 16);
         uint32_t w[8];
         ldw<8, AL>(cg + 48, w);
-        group<0, AL, NT>(hw, qh, w, d, mn, X, acc, ntok);
-        group<1, AL, NT>(hw, qh, w, d, mn, X, acc, ntok);
+        group<0, NT>(hw, qh, w, d, mn, X, acc, ntok);
+        group<1, NT>(hw, qh, w, d, mn, X, acc, ntok);
         ldw<8, AL>(cg + 80, w);
-        group<2, AL, NT>(hw, qh, w, d, mn, X, acc, ntok);
-        group<3, AL, NT>(hw, qh, w, d, mn, X, acc, ntok);
+        group<2, NT>(hw, qh, w, d, mn, X, acc, ntok);
+        group<3, NT>(hw, qh, w, d, mn, X, acc, ntok);
         ldw<8, AL>(cg + 112, w);
-        group<4, AL, NT>(hw, qh, w, d, mn, X, acc, ntok);
-        group<5, AL, NT>(hw, qh, w, d, mn, X, acc, ntok);
+        group<4, NT>(hw, qh, w, d, mn, X, acc, ntok);
+        group<5, NT>(hw, qh, w, d, mn, X, acc, ntok);
         ldw<8, AL>(cg + 144, w);
-        group<6, AL, NT>(hw, qh, w, d, mn, X, acc, ntok);
-        group<7, AL, NT>(hw, qh, w, d, mn, X, acc, ntok);
+        group<6, NT>(hw, qh, w, d, mn, X, acc, ntok);
+        group<7, NT>(hw, qh, w, d, mn, X, acc, ntok);
     }
 };
 
@@ -325,34 +377,47 @@ template <> struct Lane<F_Q5_K> {
 // bits from ql (half t&1, nibble t>>1), high 2 bits from qh at shift 2t.
 template <> struct Lane<F_Q6_K> {
     static constexpr int CGB = 210, A = 1, PERM = 0;
+    template <int N, int T, int NT>
+    __device__ static void sblk(const uint32_t* qa, const uint32_t* qb, const uint32_t* qh, const uint32_t* sc, float d,
+                                const ActCG<NT>& X, Acc<NT>& acc, int ntok) {
+        uint32_t q[8];
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+            const uint32_t src = (T & 1) ? qb[v] : qa[v];
+            const uint32_t nib = (T & 2) ? ((src >> 4) & 0x0F0F0F0Fu) : (src & 0x0F0F0F0Fu);
+            q[v] = nib | (((qh[v] >> (2 * T)) & 0x03030303u) << 4);
+        }
+        constexpr int j0 = 8 * N + 2 * T, j1 = j0 + 1;
+        const float D0 = d * static_cast<float>(static_cast<int8_t>((sc[j0 >> 2] >> (8 * (j0 & 3))) & 0xFFu));
+        const float D1 = d * static_cast<float>(static_cast<int8_t>((sc[j1 >> 2] >> (8 * (j1 & 3))) & 0xFFu));
+        AXQ_FOR_TOKENS(128 * N + 32 * T, xb, dot_run<false, 4, 0, 0, NT>(q, D0, 32.0f * D0, xb, acc, t);
+                       dot_run<false, 4, 1, 1, NT>(q + 4, D1, 32.0f * D1, xb, acc, t);)
+    }
     template <int AL, int NT>
-    __device__ static void process(const uint8_t* cg, int, const ActCG<NT>& X, float* acc, int ntok) {
+    __device__ static void process(const uint8_t* cg, int, const ActCG<NT>& X, Acc<NT>& acc, int ntok) {
         uint32_t hd[1], sc[4];
         ld_words<1>(cg + 208, hd);
         ld_words<4>(cg + 192, sc);
         const float d = h2f_ref(hd[0] & 0xFFFFu);
-#pragma unroll
-        for (int n = 0; n < 2; ++n) {
+        {
             uint32_t qa[8], qb[8], qh[8];
-            ld_words<8>(cg + 64 * n, qa);
-            ld_words<8>(cg + 64 * n + 32, qb);
-            ld_words<8>(cg + 128 + 32 * n, qh);
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-#pragma unroll
-                for (int lh = 0; lh < 2; ++lh) {
-                    const int j = 8 * n + 2 * t + lh;
-                    const float D = d * static_cast<float>(static_cast<int8_t>((sc[j >> 2] >> (8 * (j & 3))) & 0xFFu));
-                    uint32_t q[4];
-#pragma unroll
-                    for (int v = 0; v < 4; ++v) {
-                        const uint32_t src = (t & 1) ? qb[4 * lh + v] : qa[4 * lh + v];
-                        const uint32_t nib = (t & 2) ? ((src >> 4) & 0x0F0F0F0Fu) : (src & 0x0F0F0F0Fu);
-                        q[v] = nib | (((qh[4 * lh + v] >> (2 * t)) & 0x03030303u) << 4);
-                    }
-                    run_dot<false, 4, NT>(q, D, 32.0f * D, X, 128 * n + 32 * t + 16 * lh, acc, ntok);
-                }
-            }
+            ld_words<8>(cg, qa);
+            ld_words<8>(cg + 32, qb);
+            ld_words<8>(cg + 128, qh);
+            sblk<0, 0, NT>(qa, qb, qh, sc, d, X, acc, ntok);
+            sblk<0, 1, NT>(qa, qb, qh, sc, d, X, acc, ntok);
+            sblk<0, 2, NT>(qa, qb, qh, sc, d, X, acc, ntok);
+            sblk<0, 3, NT>(qa, qb, qh, sc, d, X, acc, ntok);
+        }
+        {
+            uint32_t qa[8], qb[8], qh[8];
+            ld_words<8>(cg + 64, qa);
+            ld_words<8>(cg + 96, qb);
+            ld_words<8>(cg + 160, qh);
+            sblk<1, 0, NT>(qa, qb, qh, sc, d, X, acc, ntok);
+            sblk<1, 1, NT>(qa, qb, qh, sc, d, X, acc, ntok);
+            sblk<1, 2, NT>(qa, qb, qh, sc, d, X, acc, ntok);
+            sblk<1, 3, NT>(qa, qb, qh, sc, d, X, acc, ntok);
         }
     }
 };
@@ -428,7 +493,7 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
 }
 
 template <int F, int NT, int AL>
-__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvArgs a) {
+__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
     using L = Lane<F>;
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
@@ -503,9 +568,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvArgs a) {
 
     // ---------------- consumer warps ----------------
     const int r = lane & 15, cgl = 2 * warp + (lane >> 4);  // row in unit, CG in stage
-    float acc[NT];
+    Acc<NT> acc;
 #pragma unroll
-    for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
+    for (int t = 0; t < NT; ++t) acc.d[0][t] = acc.d[1][t] = acc.m[0][t] = acc.m[1][t] = 0.0f;
     int it = 0, unit_par = 0;
     for (int64_t u = blockIdx.x; u < a.units; u += gridDim.x, unit_par ^= 1) {
         const int64_t row = u * kUnitRows + r;
@@ -541,9 +606,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvArgs a) {
         float* rp = red + unit_par * (kConsumerWarps * kUnitRows * NT);
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
-            const float v = acc[t] + __shfl_xor_sync(0xffffffffu, acc[t], 16);
+            float v = (acc.d[0][t] + acc.d[1][t]) - (acc.m[0][t] + acc.m[1][t]);
+            v += __shfl_xor_sync(0xffffffffu, v, 16);
             if (lane < 16) rp[(warp * kUnitRows + lane) * NT + t] = v;
-            acc[t] = 0.0f;
+            acc.d[0][t] = acc.d[1][t] = acc.m[0][t] = acc.m[1][t] = 0.0f;
         }
         asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
         if (warp == 0 && lane < 16 && row_ok) {
@@ -562,7 +628,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvArgs a) {
 }
 
 struct GemvPlan {
-    int rs, stage_bytes, nstages, smem, grid;
+    int rs, stage_bytes, nstages, smem, grid, ctas_per_sm;
 };
 
 template <int F>
@@ -574,8 +640,16 @@ GemvPlan plan_gemv(int nt) {
     p.rs = ((kStageCG * L::CGB + 32 + 127) / 128) * 128 + 16;
     p.stage_bytes = kUnitRows * p.rs;
     const int red_bytes = ((2 * kConsumerWarps * kUnitRows * nt * 4 + 127) / 128) * 128;
-    const int budget = 200 * 1024 - kHeaderBytes - red_bytes;
-    p.nstages = std::max(2, std::min(kMaxStages, budget / p.stage_bytes));
+    // Two CTAs per SM (18 warps) when each can keep >= 2 stages in ~110 KB,
+    // else one CTA with up to 200 KB of stages.
+    const int budget2 = 110 * 1024 - kHeaderBytes - red_bytes;
+    if (budget2 / p.stage_bytes >= 2) {
+        p.ctas_per_sm = 2;
+        p.nstages = std::min(kMaxStages, budget2 / p.stage_bytes);
+    } else {
+        p.ctas_per_sm = 1;
+        p.nstages = std::max(2, std::min(kMaxStages, (200 * 1024 - kHeaderBytes - red_bytes) / p.stage_bytes));
+    }
     p.smem = kHeaderBytes + red_bytes + p.nstages * p.stage_bytes;
     return p;
 }
@@ -648,7 +722,7 @@ cudaError_t launch_gemv(const void* w, const float* x, float* out, int64_t M, in
         const int nt_run = static_cast<int>(std::min<int64_t>(8, N - t0));
         const int nt = nt_run == 1 ? 1 : nt_run == 2 ? 2 : nt_run <= 4 ? 4 : 8;
         GemvPlan p = plan_gemv<F>(nt);
-        p.grid = static_cast<int>(std::min<int64_t>(a.units, static_cast<int64_t>(sms)));
+        p.grid = static_cast<int>(std::min<int64_t>(a.units, static_cast<int64_t>(sms) * p.ctas_per_sm));
         a.rs = p.rs;
         a.stage_bytes = p.stage_bytes;
         a.nstages = p.nstages;
