@@ -127,9 +127,9 @@ int axq_dequantize(int fmt, const void* src, float* dst, int64_t rows, int64_t c
 }
 
 size_t axq_matmul_workspace_size(int fmt, int64_t M, int64_t K, int64_t N) {
-    (void)M;
     int be = host_block_elems(fmt);
-    if (!be || K < 0 || N < 0) return 0;
+    if (!be || K < 0 || N < 0 || M < 0) return 0;
+    if (N > kGemvMaxN) return kStatusBytes + gemm_workspace_bytes(fmt, M, K, N);
     const int64_t Kp = (K + be - 1) / be * be;
     return kStatusBytes + gemv_workspace_layout(Kp, N).total;
 }
@@ -164,8 +164,11 @@ int axq_matmul(int fmt, const void* a_q, const float* b, float* out, int64_t M, 
         return fail(AXQ_ERR_INVALID, std::string(fn) + ": workspace must be 256-byte aligned");
     auto* ws = static_cast<uint8_t*>(workspace);
     int* err = reinterpret_cast<int*>(ws);  // zeroed by the first kernel of the call
-    cudaError_t e = gemv_dispatch(fmt, a_q, b, out, M, K, N, static_cast<int>(flags), ws + kStatusBytes,
-                      workspace_bytes - kStatusBytes, err, s);
+    cudaError_t e = (N > kGemvMaxN)
+                        ? gemm_dispatch(fmt, a_q, b, out, M, K, N, static_cast<int>(flags), ws + kStatusBytes,
+                                        workspace_bytes - kStatusBytes, err, s)
+                        : gemv_dispatch(fmt, a_q, b, out, M, K, N, static_cast<int>(flags), ws + kStatusBytes,
+                                        workspace_bytes - kStatusBytes, err, s);
     if (e != cudaSuccess) return cuda_fail(e, fn);
     return AXQ_OK;
 }

@@ -25,4 +25,12 @@ GemvWorkspace gemv_workspace_layout(int64_t Kp, int64_t ntok);
 cudaError_t gemv_dispatch(int fmt, const void* w, const float* x, float* out, int64_t M, int64_t K, int64_t N, int flags,
                           void* ws, size_t ws_bytes, int* err, cudaStream_t s);
 
+// Tensor-core GEMM for N > 8 activation columns.
+size_t gemm_workspace_bytes(int fmt, int64_t M, int64_t K, int64_t N);
+cudaError_t gemm_dispatch(int fmt, const void* w, const float* x, float* out, int64_t M, int64_t K, int64_t N, int flags,
+                          void* ws, size_t ws_bytes, int* err, cudaStream_t s);
+
+// Largest N served by the GEMV kernel; larger batches use the GEMM.
+constexpr int64_t kGemvMaxN = 8;
+
 }  // namespace axq

@@ -134,3 +134,29 @@ def test_matmul_unaligned_weight_buffer(cuda, orc, fmt, offset):
         out = torch.empty(M, 3, device="cuda")
         ax.matmul_q(out, buf[offset:], torch.from_numpy(B).cuda(), ax.QuantFormat[fmt], M, K)
         assert rel_err(out.cpu().numpy(), orc.matmul(fmt, q, B, M, K)) <= TOL, (fmt, offset, M, K)
+
+
+# ---- batched path (N > 8 activation columns: tcgen05 tensor-core GEMM) ----
+
+@pytest.mark.parametrize("fmt", FORMATS)
+@pytest.mark.parametrize("M,K,N", [(128, 4096, 16), (200, 1000, 9), (256, 4096, 64), (130, 11008, 32),
+                                   (384, 2048, 256), (128, 512, 512), (64, 300, 40)])
+def test_gemm_matches_oracle(cuda, orc, fmt, M, K, N):
+    rng = np.random.default_rng(M * 7 + N)
+    q = orc.quantize(fmt, gen(rng, (M, K), "randn"))
+    B = rng.standard_normal((K, N)).astype(np.float32)
+    y_ref = orc.matmul(fmt, q, B, M, K)
+    y = gpu_matmul(fmt, q, B, M, K)
+    assert rel_err(y, y_ref) <= TOL, (fmt, M, K, N, rel_err(y, y_ref))
+
+
+@pytest.mark.parametrize("fmt", ["Q4_0", "Q4_K", "Q6_K"])
+def test_gemm_token_major_and_workload_distribution(cuda, orc, fmt):
+    rng = np.random.default_rng(21)
+    M, K, N = 256, 4096, 48
+    q = orc.quantize(fmt, gen(rng, (M, K), "w002"))
+    B = rng.standard_normal((K, N)).astype(np.float32)
+    y_ref = orc.matmul(fmt, q, B, M, K)
+    for bt in (False, True):
+        for ot in (False, True):
+            assert rel_err(gpu_matmul(fmt, q, B, M, K, bt, ot), y_ref) <= TOL, (bt, ot)
