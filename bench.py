@@ -383,6 +383,119 @@ def cpu_baseline(qs, x):
             "sample": f"{n} steps of {len(FORMATS)} GEMVs over {rows} of {ROWS} rows"}
 
 
+# ------------------------------------------------------------------ suite
+
+def run_suite(args):
+    """Every configuration of the quantized path on one GPU, one JSON line
+    each (not the driver's headline line).  Weights ~ N(0, 0.02^2) (C4 with
+    0.1% outliers ~ N(0, 0.5^2)), activations ~ N(0,1); enough weight copies
+    are rotated that each timed pass streams > 2x the 126 MB L2."""
+    import torch
+    import axon_b200 as ax
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(5)
+    ws = ax.Workspace()
+    peak, _ = load_peaks()
+    mp = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    bf16_peak = json.load(open(mp)).get("bf16_tflops", 1663.3) if os.path.exists(mp) else 1590.0
+
+    def weights(rows, cols, fmt, outliers=False):
+        F = ax.QuantFormat[fmt]
+        W = torch.randn(rows, cols, device=dev, generator=g) * 0.02
+        if outliers:
+            m = torch.rand(rows, cols, device=dev, generator=g) < 0.001
+            W[m] = torch.randn(int(m.sum().item()), device=dev, generator=g) * 0.5
+        q = ax.QTensor.empty(rows, cols, F, device=dev)
+        ax.quantize(q, W, F)
+        return q
+
+    def copies(rows, cols, fmt, outliers=False):
+        nbytes = ax.quantized_size_2d(rows, cols, ax.QuantFormat[fmt])
+        n = max(1, -(-(300 << 20) // nbytes))
+        base = weights(rows, cols, fmt, outliers)
+        out = [base]
+        for _ in range(n - 1):
+            out.append(ax.QTensor(base.data.clone(), base.shape, base.fmt))
+        return out
+
+    def time_calls(fn, n_iter):
+        for i in range(3):
+            fn(i)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(n_iter):
+            fn(i)
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / n_iter
+
+    def emit(d):
+        print(json.dumps(d), flush=True)
+
+    # C1, C2, C4: matmuls
+    cases = [("C1", "Q8_0", 4096, 4096, [1], False), ("C2", "Q4_0", 4096, 4096, [1, 16, 64, 256, 512], False)]
+    for fmt in ("Q2_K", "Q3_K", "Q5_K"):
+        cases.append(("C4", fmt, 28672, 8192, [1, 8, 128], True))
+    for cfg, fmt, rows, K, Ms, outl in cases:
+        qs = copies(rows, K, fmt, outl)
+        for M in Ms:
+            x = torch.randn(M, K, device=dev, generator=g)
+            y = torch.empty(M, rows, device=dev)
+            ms = time_calls(lambda i: ax.linear_q(x, qs[i % len(qs)], out=y, workspace=ws), 20)
+            wbytes = ax.quantized_size_2d(rows, K, ax.QuantFormat[fmt])
+            gbs = (wbytes + 4 * K * M + 4 * rows * M) / (ms / 1e3) / 1e9
+            tops = 2.0 * rows * K * M / (ms / 1e3) / 1e12
+            emit({"config": cfg, "format": fmt, "rows": rows, "K": K, "M": M, "ms": round(ms, 5),
+                  "weight_GBps": round(wbytes / (ms / 1e3) / 1e9, 1), "algo_GBps": round(gbs, 1),
+                  "hbm_frac": round(gbs / peak, 3), "TOPS": round(tops, 2),
+                  "bf16_peak_frac": round(tops / bf16_peak, 3)})
+        del qs
+
+    # C3: MLP block y = W_down . (SiLU(X W_gate^T) * (X W_up^T))
+    up, gate = copies(11008, 4096, "Q4_K")[:2], None
+    gate = [weights(11008, 4096, "Q4_K")]
+    down = copies(4096, 11008, "Q6_K")
+    for M in (1, 32):
+        x = torch.randn(M, 4096, device=dev, generator=g)
+        hu = torch.empty(M, 11008, device=dev)
+        hg = torch.empty(M, 11008, device=dev)
+        yo = torch.empty(M, 4096, device=dev)
+
+        def mlp(i):
+            ax.linear_q(x, gate[0], out=hg, workspace=ws)
+            ax.linear_q(x, up[i % len(up)], out=hu, workspace=ws)
+            h = torch.nn.functional.silu(hg) * hu
+            ax.linear_q(h, down[i % len(down)], out=yo, workspace=ws)
+
+        ms = time_calls(mlp, 20)
+        wbytes = 2 * ax.quantized_size_2d(11008, 4096, ax.QuantFormat.Q4_K) + \
+            ax.quantized_size_2d(4096, 11008, ax.QuantFormat.Q6_K)
+        emit({"config": "C3", "format": "Q4_K+Q6_K MLP", "M": M, "ms": round(ms, 5),
+              "weight_GBps": round(wbytes / (ms / 1e3) / 1e9, 1),
+              "TOPS": round(3 * 2.0 * 11008 * 4096 * M / (ms / 1e3) / 1e12, 2)})
+
+    # C5: pack sweep (fp32 read GB/s)
+    for p in (20, 24, 27, 30):
+        n = 1 << p
+        src = torch.randn(n // 4096, 4096, device=dev, generator=g)
+        m = torch.rand(n // 4096, 4096, device=dev, generator=g) < 0.01
+        src[m] = torch.rand(int(m.sum().item()), device=dev, generator=g) * 100 - 50
+        del m
+        for fmt in ("Q8_0", "Q4_0", "Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K"):
+            F = ax.QuantFormat[fmt]
+            dst = torch.empty(ax.quantized_size_2d(n // 4096, 4096, F), dtype=torch.uint8, device=dev)
+            ms = time_calls(lambda i: ax.quantize(dst, src, F), 5 if p >= 27 else 20)
+            emit({"config": "C5", "format": fmt, "elements": n, "ms": round(ms, 4),
+                  "read_GBps": round(4 * n / (ms / 1e3) / 1e9, 1),
+                  "hbm_frac": round((4 * n + dst.numel()) / (ms / 1e3) / 1e9 / peak, 3)})
+            del dst
+        del src
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -390,7 +503,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="axon_b200", choices=["axon_b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--suite", action="store_true", help="time every configuration (one JSON line each)")
     args = ap.parse_args()
+    if args.suite:
+        return run_suite(args)
     if args.impl == "reference":
         return run_reference_arm(args)
     return run_gpu(args)
