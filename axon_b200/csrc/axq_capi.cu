@@ -66,6 +66,8 @@ constexpr size_t kStatusBytes = 256;  // status words at the front of a workspac
 
 }  // namespace
 
+void set_last_error(const std::string& msg) { g_last_error = msg; }
+
 int device_sm_count() {
     static int cache[64] = {0};
     int dev = 0;

@@ -4,6 +4,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <string>
 #include <cuda_runtime.h>
 
 #include "../../include/axq.h"
@@ -12,6 +13,9 @@ namespace axq {
 
 // Multiprocessor count of the current device (cached per device).
 int device_sm_count();
+
+// Sets the calling thread's axq_last_error() message.
+void set_last_error(const std::string& msg);
 
 cudaError_t pack_dispatch(int fmt, const float* src, void* dst, int64_t rows, int64_t cols, cudaStream_t s);
 cudaError_t dequant_dispatch(int fmt, const void* src, float* dst, int64_t rows, int64_t cols, cudaStream_t s);

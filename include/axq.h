@@ -90,6 +90,29 @@ size_t axq_matmul_workspace_size(int fmt, int64_t M, int64_t K, int64_t N);
 int axq_matmul(int fmt, const void* a_q, const float* b, float* out, int64_t M, int64_t K, int64_t N,
                unsigned flags, void* workspace, size_t workspace_bytes, axq_stream_t stream);
 
+/* Bytes of the scratch array built into the library for
+ * axq_matmul_noalloc (16 MiB, held by every GPU that loads the library). */
+#define AXQ_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/* axq_matmul without a workspace argument: it allocates nothing and uses the
+ * library's own fixed device scratch (AXQ_NOALLOC_SCRATCH_BYTES) instead.
+ * No counterpart in the reference (its CPU kernels need no scratch).  For
+ * callers that cannot allocate device memory: a kernel behind Axon's
+ * KernelRegistry gets only its tensors (KernelContext has no allocator
+ * handle), and code embedded in a host that owns all device memory may not
+ * call cudaMalloc.
+ *  - Sizes whose scratch need (axq_matmul_workspace_size) exceeds the built-in
+ *    scratch return AXQ_ERR_WORKSPACE with a message; use axq_matmul then.
+ *  - The first call on each device looks up the scratch's device address
+ *    (cudaGetSymbolAddress) with that device current; make that first call
+ *    before any stream capture.
+ *  - All calls on a device share one scratch and it keeps the last call's
+ *    contents (each call clears what must start at zero): calls that may
+ *    overlap on the GPU (different streams, or host threads) race — serialize
+ *    them on one stream. */
+int axq_matmul_noalloc(int fmt, const void* a_q, const float* b, float* out, int64_t M, int64_t K, int64_t N,
+                       unsigned flags, axq_stream_t stream);
+
 /* Synchronizes `stream` and reports whether a kernel that used `workspace`
  * gave up a bounded wait (AXQ_ERR_TIMEOUT) — 0 otherwise. */
 int axq_workspace_status(const void* workspace, axq_stream_t stream);
