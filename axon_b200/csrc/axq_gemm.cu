@@ -37,8 +37,11 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kKStepsPerCG = 4;  // a column group is 256 elements
-constexpr int kThreadsGemm = 192;
-constexpr int kMaxPk = 3, kMaxAB = 4;
+// warps: 0 packed-weight producer, 1 MMA issuer, 2..9 dequant + epilogue,
+// 10 activation-tile producer
+constexpr int kDqWarps = 8;
+constexpr int kThreadsGemm = (3 + kDqWarps) * 32;
+constexpr int kMaxPk = 3, kMaxAB = 6;
 
 template <int F> struct CG {
     static constexpr int BE = Traits<F>::BE, BB = Traits<F>::BB;
@@ -57,12 +60,14 @@ struct GemmArgs {
     int nrt, nct, splits, cg_per_split;
     int rs;             // packed row stride in shared memory
     int npk, nab;
-    int pk_bytes, a_bytes, b_bytes;
+    int pk_bytes, b_bytes;
+    int tmem_cols;      // allocated: BN accumulator columns + nab A slots of 32 columns
     float* out;         // final output (splits == 1) or partial tiles
     int64_t out_ld;
     int out_tokmajor;
     int direct;         // 1: write `out`, 0: write partials [split][rows][ntok_pad]
     int64_t part_ld;
+    int aligned;        // rows and buffer 16-byte aligned: natural-alignment loads
     int* err;
 };
 
@@ -84,14 +89,284 @@ __device__ __forceinline__ bool gwait(uint64_t* bar, uint32_t parity, volatile i
     return false;
 }
 
+// ---------------------------------------------------------------- dequant
+//
+// One thread writes one weight row of a 64-element K-step as eight 16-byte
+// fp16 chunks (K order).  Codes are turned into exact fp16 integers with the
+// 0x6400 exponent trick (byte b -> half 1024 + b, minus 1024) and scaled with
+// one half2 FMA: value = D*code - M per sub-block.  Not bit-exact with the
+// reference (the MMA consumes fp16 anyway); the dot stays within tolerance.
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+    return r;
+}
+
+// Bytes (2p, 2p+1) of a word of byte codes (0..255) as exact half2
+// integers minus an exact offset: `sub` holds 1024 + offset.
+template <int P>
+__device__ __forceinline__ __half2 codes_h2(uint32_t w, __half2 sub) {
+    const uint32_t m = prmt(w, 0x64646464u, P ? 0x4342u : 0x4140u);
+    return __hsub2(*reinterpret_cast<const __half2*>(&m), sub);
+}
+
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+
+// 8 elements (two code words, 4 byte codes each) -> one fp16 chunk:
+// D*(c - offset) + Mneg, one rounding per element.
+__device__ __forceinline__ uint4 chunk8(uint32_t w0, uint32_t w1, __half2 sub, __half2 D, __half2 Mneg) {
+    uint4 o;
+    o.x = h2u(__hfma2(codes_h2<0>(w0, sub), D, Mneg));
+    o.y = h2u(__hfma2(codes_h2<1>(w0, sub), D, Mneg));
+    o.z = h2u(__hfma2(codes_h2<0>(w1, sub), D, Mneg));
+    o.w = h2u(__hfma2(codes_h2<1>(w1, sub), D, Mneg));
+    return o;
+}
+
+__device__ __forceinline__ __half2 hh(float v) { return __float2half2_rn(v); }
+
+// Scale/min pair of a K-quant sub-block as (1024 + q0, D, -(M - q0*D)) with
+// q0 = rint(M/D): the fp16 math then computes D*(c - q0) - M' and every
+// element is rounded once at its own magnitude (rounding D and M separately
+// would cost |M| * 2^-11 per element).
+struct Sm {
+    __half2 sub, D, Mneg;
+};
+__device__ __forceinline__ Sm scale_min(float D, float M) {
+    float q0 = 0.0f;
+    if (D != 0.0f) q0 = fminf(1024.0f, fmaxf(-1024.0f, rintf(__fdividef(M, D))));
+    Sm r;
+    r.sub = hh(1024.0f + q0);
+    r.D = hh(D);
+    r.Mneg = hh(fmaf(q0, D, -M));
+    return r;
+}
+__device__ __forceinline__ Sm scale_off(float D, float off) {
+    Sm r;
+    r.sub = hh(1024.0f + off);
+    r.D = hh(D);
+    r.Mneg = hh(0.0f);
+    return r;
+}
+
+template <int N, int A>
+__device__ __forceinline__ void ldg_w(const uint8_t* p, uint32_t* out) {
+    if constexpr (A >= 16 && N % 4 == 0) {
+#pragma unroll
+        for (int i = 0; i < N / 4; ++i) {
+            uint4 v = reinterpret_cast<const uint4*>(p)[i];
+            out[4 * i] = v.x; out[4 * i + 1] = v.y; out[4 * i + 2] = v.z; out[4 * i + 3] = v.w;
+        }
+    } else if constexpr (A >= 4) {
+#pragma unroll
+        for (int i = 0; i < N; ++i) out[i] = reinterpret_cast<const uint32_t*>(p)[i];
+    } else {
+        ld_words<N>(p, out);
+    }
+}
+
+template <int I>
+__device__ __forceinline__ uint32_t byte_i(const uint32_t* w) { return (w[I >> 2] >> (8 * (I & 3))) & 0xFFu; }
+
+template <int G>
+__device__ __forceinline__ void k4_sm(const uint32_t* hw, int& sc, int& m) {
+    if constexpr (G < 4) {
+        sc = byte_i<4 + G>(hw) & 63;
+        m = byte_i<8 + G>(hw) & 63;
+    } else {
+        sc = (byte_i<8 + G>(hw) & 0xF) | ((byte_i<G>(hw) >> 6) << 4);
+        m = (byte_i<8 + G>(hw) >> 4) | ((byte_i<4 + G>(hw) >> 6) << 4);
+    }
+}
+
+// Dq<F>::kstep<KS, H, A>(row, out): half H of K-step KS (elements
+// 64KS..64KS+63 of the column group at `row`, shared memory with alignment
+// A) into out[4] = fp16 chunks 4H..4H+3 of that K-step.  Every format splits
+// a K-step into two halves that share no scale: nibble, 2-bit shift, or block.
+template <int F> struct Dq;
+
+template <> struct Dq<F_Q4_K> {
+    static constexpr int A = 16;
+    template <int KS, int H, int AL>
+    __device__ static void kstep(const uint8_t* row, uint4* out) {
+        uint32_t hw[4], w[8];
+        ldg_w<4, AL>(row, hw);
+        ldg_w<8, AL>(row + 16 + 32 * KS, w);
+        const float d = h2f_ref(hw[0] & 0xFFFFu), mn = h2f_ref(hw[0] >> 16);
+        int sc, m;
+        k4_sm<2 * KS + H>(hw, sc, m);
+        const Sm g = scale_min(d * sc, mn * m);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const uint32_t w0 = H ? (w[2 * c] >> 4) : w[2 * c], w1 = H ? (w[2 * c + 1] >> 4) : w[2 * c + 1];
+            out[c] = chunk8(w0 & 0x0F0F0F0Fu, w1 & 0x0F0F0F0Fu, g.sub, g.D, g.Mneg);
+        }
+    }
+};
+
+template <> struct Dq<F_Q5_K> {
+    static constexpr int A = 16;
+    template <int KS, int H, int AL>
+    __device__ static void kstep(const uint8_t* row, uint4* out) {
+        uint32_t hw[4], w[8], qh[8];
+        ldg_w<4, AL>(row, hw);
+        ldg_w<8, AL>(row + 48 + 32 * KS, w);
+        ldg_w<8, AL>(row + 16, qh);
+        const float d = h2f_ref(hw[0] & 0xFFFFu), mn = h2f_ref(hw[0] >> 16);
+        constexpr int g = 2 * KS + H;
+        int sc, m;
+        k4_sm<g>(hw, sc, m);
+        const Sm s = scale_min(d * sc, mn * m);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            uint32_t cw[2];
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const uint32_t nib = (H ? (w[2 * c + i] >> 4) : w[2 * c + i]) & 0x0F0F0F0Fu;
+                const uint32_t hb = ((g <= 4) ? (qh[2 * c + i] << (4 - g)) : (qh[2 * c + i] >> (g - 4))) & 0x10101010u;
+                cw[i] = nib | hb;
+            }
+            out[c] = chunk8(cw[0], cw[1], s.sub, s.D, s.Mneg);
+        }
+    }
+};
+
+template <> struct Dq<F_Q2_K> {
+    static constexpr int A = 4;
+    template <int KS, int H, int AL>
+    __device__ static void kstep(const uint8_t* row, uint4* out) {
+        constexpr int n = KS >> 1, s = 2 * (KS & 1) + H;
+        uint32_t hd[1], sc[2], w[8];
+        ldg_w<1, AL>(row, hd);
+        ldg_w<2, AL>(row + 4 + 8 * n, sc);
+        ldg_w<8, AL>(row + 20 + 32 * n, w);
+        const float d = h2f_ref(hd[0] & 0xFFFFu), mn = h2f_ref(hd[0] >> 16);
+#pragma unroll
+        for (int lh = 0; lh < 2; ++lh) {
+            const uint32_t b = (sc[(2 * s + lh) >> 2] >> (8 * ((2 * s + lh) & 3))) & 0xFFu;
+            const Sm g = scale_min(d * static_cast<float>(b & 0xF), mn * static_cast<float>(b >> 4));
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                const int wi = 4 * lh + 2 * c;
+                out[2 * lh + c] =
+                    chunk8((w[wi] >> (2 * s)) & 0x03030303u, (w[wi + 1] >> (2 * s)) & 0x03030303u, g.sub, g.D, g.Mneg);
+            }
+        }
+    }
+};
+
+template <> struct Dq<F_Q3_K> {
+    static constexpr int A = 1;
+    template <int IS>
+    __device__ static float subscale(const uint32_t* s12, float d) {
+        constexpr int lo_byte = (IS < 8) ? IS : IS - 8, lo_sh = (IS < 8) ? 0 : 4;
+        const int lo4 = (s12[lo_byte >> 2] >> (8 * (lo_byte & 3) + lo_sh)) & 0xF;
+        const int hi2 = (s12[2] >> (8 * (IS & 3) + 2 * (IS >> 2))) & 3;
+        return d * static_cast<float>((lo4 | (hi2 << 4)) - 32);
+    }
+    template <int KS, int H, int AL>
+    __device__ static void kstep(const uint8_t* row, uint4* out) {
+        constexpr int n = KS >> 1, s = 2 * (KS & 1) + H;
+        uint32_t hd[1], s12[3], w[8], hm[8];
+        ld_words<1>(row + 108, hd);
+        ld_words<3>(row + 96, s12);
+        ld_words<8>(row + 32 + 32 * n, w);
+        ld_words<8>(row, hm);
+        const float d = h2f_ref(hd[0] & 0xFFFFu);
+        const Sm g0 = scale_off(subscale<8 * n + 2 * s>(s12, d), 4.0f);
+        const Sm g1 = scale_off(subscale<8 * n + 2 * s + 1>(s12, d), 4.0f);
+#pragma unroll
+        for (int lh = 0; lh < 2; ++lh) {
+            const Sm& g = lh ? g1 : g0;
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                const int wi = 4 * lh + 2 * c;
+                const uint32_t c0 = ((w[wi] >> (2 * s)) & 0x03030303u) | (((hm[wi] >> (4 * n + s)) & 0x01010101u) << 2);
+                const uint32_t c1 =
+                    ((w[wi + 1] >> (2 * s)) & 0x03030303u) | (((hm[wi + 1] >> (4 * n + s)) & 0x01010101u) << 2);
+                out[2 * lh + c] = chunk8(c0, c1, g.sub, g.D, g.Mneg);
+            }
+        }
+    }
+};
+
+template <> struct Dq<F_Q6_K> {
+    static constexpr int A = 1;
+    template <int KS, int H, int AL>
+    __device__ static void kstep(const uint8_t* row, uint4* out) {
+        constexpr int n = KS >> 1, t = 2 * (KS & 1) + H;
+        uint32_t hd[1], sc[2], qh[8], ql[8];
+        ld_words<1>(row + 208, hd);
+        ld_words<2>(row + 192 + 8 * n, sc);
+        ld_words<8>(row + 128 + 32 * n, qh);
+        ld_words<8>(row + 64 * n + 32 * (t & 1), ql);
+        const float d = h2f_ref(hd[0] & 0xFFFFu);
+#pragma unroll
+        for (int lh = 0; lh < 2; ++lh) {
+            const int j = 2 * t + lh;
+            const float Dv = d * static_cast<float>(static_cast<int8_t>((sc[j >> 2] >> (8 * (j & 3))) & 0xFFu));
+            const Sm g = scale_off(Dv, 32.0f);
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                const int wi = 4 * lh + 2 * c;
+                const uint32_t n0 = ((t & 2) ? (ql[wi] >> 4) : ql[wi]) & 0x0F0F0F0Fu;
+                const uint32_t n1 = ((t & 2) ? (ql[wi + 1] >> 4) : ql[wi + 1]) & 0x0F0F0F0Fu;
+                const uint32_t c0 = n0 | (((qh[wi] >> (2 * t)) & 0x03030303u) << 4);
+                const uint32_t c1 = n1 | (((qh[wi + 1] >> (2 * t)) & 0x03030303u) << 4);
+                out[2 * lh + c] = chunk8(c0, c1, g.sub, g.D, g.Mneg);
+            }
+        }
+    }
+};
+
+// Q8_0: half H = block 2KS+H of the column group; signed codes biased by 128.
+template <> struct Dq<F_Q8_0> {
+    static constexpr int A = 1;
+    template <int KS, int H, int AL>
+    __device__ static void kstep(const uint8_t* row, uint4* out) {
+        const uint8_t* blk = row + 34 * (2 * KS + H);
+        uint32_t hd[1], w[8];
+        ld_words<1>(blk, hd);
+        ld_words<8>(blk + 2, w);
+        const Sm g = scale_off(h2f_ref(hd[0] & 0xFFFFu), 128.0f);
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+            out[c] = chunk8(w[2 * c] ^ 0x80808080u, w[2 * c + 1] ^ 0x80808080u, g.sub, g.D, g.Mneg);
+    }
+};
+
+// Q4_0: half H = block 2KS+H; byte i holds elements 2i (low) and 2i+1 (high).
+template <> struct Dq<F_Q4_0> {
+    static constexpr int A = 1;
+    template <int KS, int H, int AL>
+    __device__ static void kstep(const uint8_t* row, uint4* out) {
+        const uint8_t* blk = row + 18 * (2 * KS + H);
+        uint32_t hd[1], w[4];
+        ld_words<1>(blk, hd);
+        ld_words<4>(blk + 2, w);
+        const Sm g = scale_off(h2f_ref(hd[0] & 0xFFFFu), 8.0f);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const uint32_t lo = w[c] & 0x0F0F0F0Fu, hi = (w[c] >> 4) & 0x0F0F0F0Fu;
+            out[c] = chunk8(prmt(lo, hi, 0x5140u), prmt(lo, hi, 0x7362u), g.sub, g.D, g.Mneg);
+        }
+    }
+};
+
+template <int F, int KS, int H>
+__device__ __forceinline__ void dq_step(const uint8_t* row, uint4* o, int aligned) {
+    if (aligned && Dq<F>::A > 1) Dq<F>::template kstep<KS, H, Dq<F>::A>(row, o);
+    else Dq<F>::template kstep<KS, H, 1>(row, o);
+}
+
 template <int F>
 __global__ void __launch_bounds__(kThreadsGemm, 1) gemm_kernel(GemmArgs a) {
     using C = CG<F>;
     extern __shared__ __align__(1024) uint8_t smem[];
     Bars* bars = reinterpret_cast<Bars*>(smem);
     uint8_t* pk_ring = smem + 1024;
-    uint8_t* a_ring = pk_ring + a.npk * a.pk_bytes;
-    uint8_t* b_ring = a_ring + a.nab * a.a_bytes;
+    uint8_t* b_ring = pk_ring + a.npk * a.pk_bytes;
     volatile int* abort_flag = &bars->abort_flag;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -108,11 +383,11 @@ __global__ void __launch_bounds__(kThreadsGemm, 1) gemm_kernel(GemmArgs a) {
 
     if (tid == 0) {
         for (int i = 0; i < kMaxPk; ++i) {
-            mbar_init(&bars->pk_full[i], 1);
-            mbar_init(&bars->pk_empty[i], 4);
+            mbar_init(&bars->pk_full[i], 32);  // one asynchronous arrive per producer lane
+            mbar_init(&bars->pk_empty[i], kDqWarps);
         }
         for (int i = 0; i < kMaxAB; ++i) {
-            mbar_init(&bars->a_full[i], 4);
+            mbar_init(&bars->a_full[i], kDqWarps);
             mbar_init(&bars->b_full[i], 1);
             mbar_init(&bars->ab_empty[i], 1);
         }
@@ -121,7 +396,7 @@ __global__ void __launch_bounds__(kThreadsGemm, 1) gemm_kernel(GemmArgs a) {
         bars->abort_flag = 0;
         fence_mbar_init();
     }
-    const uint32_t tmem_cols = a.BN <= 32 ? 32 : a.BN <= 64 ? 64 : a.BN <= 128 ? 128 : 256;
+    const uint32_t tmem_cols = static_cast<uint32_t>(a.tmem_cols);
     if (warp == 1) tmem_alloc(&bars->tmem_base, tmem_cols);
     tc_fence_before();
     __syncthreads();
@@ -132,62 +407,52 @@ __global__ void __launch_bounds__(kThreadsGemm, 1) gemm_kernel(GemmArgs a) {
     const uintptr_t wend = wbase + static_cast<uintptr_t>(a.rows * a.rb);
 
     if (warp == 0) {
-        // ------------------------------------------------------ producer
+        // ---------------------------- packed-weight producer (cp.async)
+        // Lane l copies rows l, l+32, l+64, l+96 of each column-group slice
+        // in 16-byte chunks of the row segment's 16-byte-rounded range (bytes
+        // of the neighbouring segments ride along); where that range would
+        // leave the weight buffer the lane copies bytes itself.
         for (int i = 0; i < ncg_here; ++i) {
             const int p = i % a.npk;
             if (i >= a.npk && !gwait(&bars->pk_empty[p], ((i / a.npk) - 1) & 1, abort_flag, a.err)) break;
             uint8_t* pk = pk_ring + p * a.pk_bytes;
             const int64_t off = static_cast<int64_t>(cg0 + i) * C::BYTES;
             const int64_t seg = min64(C::BYTES, a.rb - off);
-            uint32_t tx = 0;
-            uintptr_t lo4[4];
-            uint32_t n4[4];
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 const int r = lane + 32 * q;
                 const int64_t row = row0 + r;
-                n4[q] = 0;
                 if (row < a.rows) {
                     const uintptr_t ga = wbase + static_cast<uintptr_t>(row * a.rb + off);
                     const uintptr_t gb = ga + static_cast<uintptr_t>(seg);
                     const uintptr_t lo = ga & ~static_cast<uintptr_t>(15);
                     const uintptr_t hi = (gb + 15) & ~static_cast<uintptr_t>(15);
+                    uint8_t* dst = pk + r * a.rs;
                     if (lo >= wbase && hi <= wend) {
-                        lo4[q] = lo;
-                        n4[q] = static_cast<uint32_t>(hi - lo);
-                        tx += n4[q];
+                        for (uintptr_t g = lo; g < hi; g += 16)
+                            cp_async16(dst + (g - lo), reinterpret_cast<const void*>(g));
                     } else {
-                        uint8_t* dst = pk + r * a.rs + (ga & 15);
-                        for (uintptr_t g = ga; g < gb; ++g) dst[g - ga] = *reinterpret_cast<const uint8_t*>(g);
+                        for (uintptr_t g = ga; g < gb; ++g) dst[g - lo] = *reinterpret_cast<const uint8_t*>(g);
                     }
                 }
             }
-            const uint32_t txs = __reduce_add_sync(0xffffffffu, tx);
-            __syncwarp();
-            if (lane == 0) {
-                if (txs) mbar_arrive_expect_tx(&bars->pk_full[p], txs);
-                else mbar_arrive(&bars->pk_full[p]);
-            }
-            __syncwarp();
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-                if (n4[q]) bulk_g2s(pk + (lane + 32 * q) * a.rs, reinterpret_cast<const void*>(lo4[q]), n4[q],
-                                    &bars->pk_full[p]);
-            // activation tiles of this column group's four K-steps
-            for (int k = 0; k < kKStepsPerCG; ++k) {
-                const int j = i * kKStepsPerCG + k;
-                const int s = j % a.nab;
-                if (j >= a.nab && !gwait(&bars->ab_empty[s], ((j / a.nab) - 1) & 1, abort_flag, a.err)) break;
-                if (lane == 0) {
-                    const int ks = (cg0 + i) * kKStepsPerCG + k;
-                    const uint8_t* src = a.xh + (static_cast<int64_t>(ct) * a.nks_total + ks) * a.b_bytes;
-                    mbar_arrive_expect_tx(&bars->b_full[s], a.b_bytes);
-                    bulk_g2s(b_ring + s * a.b_bytes, src, a.b_bytes, &bars->b_full[s]);
-                }
-                __syncwarp();
-            }
+            __threadfence_block();
+            cp_async_arrive_noinc(&bars->pk_full[p]);
             if (*abort_flag) break;
         }
+    } else if (warp == 2 + kDqWarps) {
+        // ------------------------------------- activation-tile producer
+        if (lane == 0) {
+            for (int j = 0; j < nsteps; ++j) {
+                const int s = j % a.nab;
+                if (j >= a.nab && !gwait(&bars->ab_empty[s], ((j / a.nab) - 1) & 1, abort_flag, a.err)) break;
+                const int ks = cg0 * kKStepsPerCG + j;
+                const uint8_t* src = a.xh + (static_cast<int64_t>(ct) * a.nks_total + ks) * a.b_bytes;
+                mbar_arrive_expect_tx(&bars->b_full[s], a.b_bytes);
+                bulk_g2s(b_ring + s * a.b_bytes, src, a.b_bytes, &bars->b_full[s]);
+            }
+        }
+        __syncwarp();
     } else if (warp == 1) {
         // ------------------------------------------------------ MMA issuer
         if (lane == 0) {
@@ -198,13 +463,12 @@ __global__ void __launch_bounds__(kThreadsGemm, 1) gemm_kernel(GemmArgs a) {
                 if (!gwait(&bars->a_full[s], par, abort_flag, a.err)) break;
                 if (!gwait(&bars->b_full[s], par, abort_flag, a.err)) break;
                 tc_fence_after();
-                const uint32_t as = smem_u32(a_ring + s * a.a_bytes);
+                const uint32_t at = tmem + static_cast<uint32_t>(a.BN + 32 * s);  // A slot s (lanes 0..127)
                 const uint32_t bs = smem_u32(b_ring + s * a.b_bytes);
 #pragma unroll
                 for (int k16 = 0; k16 < BK / 16; ++k16) {
-                    const uint64_t ad = smem_desc_kmajor(as + k16 * 256, 128, 1024);
                     const uint64_t bd = smem_desc_kmajor(bs + k16 * 256, 128, 1024);
-                    mma_f16(tmem, ad, bd, idesc, (j > 0 || k16 > 0) ? 1u : 0u);
+                    mma_f16_ta(tmem, at + 8 * k16, bd, idesc, (j > 0 || k16 > 0) ? 1u : 0u);
                 }
                 mma_commit(&bars->ab_empty[s]);
             }
@@ -214,9 +478,10 @@ __global__ void __launch_bounds__(kThreadsGemm, 1) gemm_kernel(GemmArgs a) {
             gwait(&bars->done, 0, abort_flag, a.err);
         }
         __syncwarp();
-    } else {
+    } else if (warp >= 2 && warp < 2 + kDqWarps) {
         // ------------------------------------------- dequant + epilogue
-        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        const int q = warp & 3;          // TMEM lane quarter this warp may access
+        const int h = (warp - 2) >> 2;   // which half of each K-step this thread writes
         const int r = 32 * q + lane;
         const int64_t row = row0 + r;
         const bool row_ok = row < a.rows;
@@ -226,36 +491,47 @@ __global__ void __launch_bounds__(kThreadsGemm, 1) gemm_kernel(GemmArgs a) {
             const int cg = cg0 + i;
             const uintptr_t ga = wbase + static_cast<uintptr_t>(row * a.rb + static_cast<int64_t>(cg) * C::BYTES);
             const uint8_t* rowp = pk_ring + p * a.pk_bytes + r * a.rs + (ga & 15);
+            const bool tail = (static_cast<int64_t>(cg + 1) * 256 > a.K) || ((cg + 1) * C::BLK > a.nblk_row);
+#pragma unroll
             for (int k = 0; k < kKStepsPerCG; ++k) {
                 const int j = i * kKStepsPerCG + k;
                 const int s = j % a.nab;
                 if (j >= a.nab && !gwait(&bars->ab_empty[s], ((j / a.nab) - 1) & 1, abort_flag, a.err)) break;
-                uint8_t* at = a_ring + s * a.a_bytes + (r >> 3) * 1024 + (r & 7) * 16;
-#pragma unroll
-                for (int c8 = 0; c8 < 8; ++c8) {
-                    const int e = 64 * k + 8 * c8;  // element within the column group
-                    float v[8];
-                    const int blk = e / C::BE;
-                    const int64_t kglob = static_cast<int64_t>(cg) * 256 + e;
-                    if (row_ok && kglob < a.K && cg * C::BLK + blk < a.nblk_row) {
-                        Decode<F>::run(rowp + blk * C::BB, e % C::BE, v);
-#pragma unroll
-                        for (int u = 0; u < 8; ++u)
-                            if (kglob + u >= a.K) v[u] = 0.0f;
+                uint4 o[4];
+                if (row_ok) {
+                    if (h == 0) {
+                        if (k == 0) dq_step<F, 0, 0>(rowp, o, a.aligned);
+                        else if (k == 1) dq_step<F, 1, 0>(rowp, o, a.aligned);
+                        else if (k == 2) dq_step<F, 2, 0>(rowp, o, a.aligned);
+                        else dq_step<F, 3, 0>(rowp, o, a.aligned);
                     } else {
-#pragma unroll
-                        for (int u = 0; u < 8; ++u) v[u] = 0.0f;
+                        if (k == 0) dq_step<F, 0, 1>(rowp, o, a.aligned);
+                        else if (k == 1) dq_step<F, 1, 1>(rowp, o, a.aligned);
+                        else if (k == 2) dq_step<F, 2, 1>(rowp, o, a.aligned);
+                        else dq_step<F, 3, 1>(rowp, o, a.aligned);
                     }
-                    uint4 pk4;
-                    __half2 h0 = __floats2half2_rn(v[0], v[1]), h1 = __floats2half2_rn(v[2], v[3]);
-                    __half2 h2 = __floats2half2_rn(v[4], v[5]), h3 = __floats2half2_rn(v[6], v[7]);
-                    pk4.x = *reinterpret_cast<uint32_t*>(&h0);
-                    pk4.y = *reinterpret_cast<uint32_t*>(&h1);
-                    pk4.z = *reinterpret_cast<uint32_t*>(&h2);
-                    pk4.w = *reinterpret_cast<uint32_t*>(&h3);
-                    *reinterpret_cast<uint4*>(at + c8 * 128) = pk4;
+                    if (tail) {
+                        // zero the elements past K (and blocks past the row's end)
+#pragma unroll
+                        for (int c4 = 0; c4 < 4; ++c4) {
+                            const int e = 64 * k + 8 * (4 * h + c4);
+                            const int64_t kglob = static_cast<int64_t>(cg) * 256 + e;
+                            const bool blk_ok = cg * C::BLK + e / C::BE < a.nblk_row;
+                            uint32_t* ow = reinterpret_cast<uint32_t*>(&o[c4]);
+#pragma unroll
+                            for (int u = 0; u < 8; ++u)
+                                if (!blk_ok || kglob + u >= a.K) ow[u >> 1] &= (u & 1) ? 0x0000FFFFu : 0xFFFF0000u;
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int c4 = 0; c4 < 4; ++c4) o[c4] = make_uint4(0, 0, 0, 0);
                 }
-                fence_proxy_async_smem();
+                // this row's 32 elements = 16 TMEM columns of A slot s
+                tmem_st16(tmem + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(a.BN + 32 * s + 16 * h),
+                          reinterpret_cast<const uint32_t*>(o));
+                tmem_st_wait();
+                tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&bars->a_full[s]);
             }
@@ -267,7 +543,7 @@ __global__ void __launch_bounds__(kThreadsGemm, 1) gemm_kernel(GemmArgs a) {
         if (gwait(&bars->acc_full, 0, abort_flag, a.err)) {
             tc_fence_after();
             const int tok0 = ct * a.BN;
-            for (int c0 = 0; c0 < a.BN; c0 += 32) {
+            for (int c0 = 32 * h; c0 < a.BN; c0 += 64) {
                 float v[32];
                 tmem_ld32(tmem + (static_cast<uint32_t>(32 * q) << 16) + c0, v);
                 if (!row_ok) continue;
@@ -411,14 +687,27 @@ cudaError_t launch_gemm(const void* w, const float* x, float* out, int64_t M, in
     a.nct = g.nct;
     a.splits = g.splits;
     a.cg_per_split = g.cg_per_split;
+    // packed row stride: data + 16 B alignment slack + 4 B over-read, rounded to
+    // an odd multiple of 16 B so the 8 rows of a quarter-warp hit distinct banks
     a.rs = (C::BYTES + 32 + 15) / 16 * 16;
+    if ((a.rs / 16) % 2 == 0) a.rs += 16;
+    a.aligned = (reinterpret_cast<uintptr_t>(w) % 16 == 0) && (a.rb % 16 == 0);
     a.pk_bytes = BM * a.rs;
-    a.a_bytes = BM * BK * 2;
     a.b_bytes = g.BN * BK * 2;
     const int budget = 220 * 1024 - 1024;
-    a.npk = 2;
-    a.nab = std::max(2, std::min(kMaxAB, (budget - a.npk * a.pk_bytes) / (a.a_bytes + a.b_bytes)));
-    if (a.npk * a.pk_bytes + a.nab * (a.a_bytes + a.b_bytes) > budget) return cudaErrorInvalidConfiguration;
+    a.npk = 3;
+    a.nab = std::min(kMaxAB, (budget - a.npk * a.pk_bytes) / a.b_bytes);
+    if (a.nab < 3) {
+        a.npk = 2;
+        a.nab = std::max(2, std::min(kMaxAB, (budget - a.npk * a.pk_bytes) / a.b_bytes));
+    }
+    // TMEM: BN accumulator columns + one 32-column A slot per stage, <= 512
+    a.nab = std::min(a.nab, (512 - g.BN) / 32);
+    {
+        const int need = g.BN + 32 * a.nab;
+        a.tmem_cols = need <= 32 ? 32 : need <= 64 ? 64 : need <= 128 ? 128 : need <= 256 ? 256 : 512;
+    }
+    if (a.npk * a.pk_bytes + a.nab * a.b_bytes > budget) return cudaErrorInvalidConfiguration;
     a.out_tokmajor = (flags & AXQ_FLAG_OUT_TOKMAJOR) ? 1 : 0;
     a.err = err;
     if (g.splits == 1) {
@@ -430,7 +719,7 @@ cudaError_t launch_gemm(const void* w, const float* x, float* out, int64_t M, in
         a.out = part;
         a.part_ld = g.ntok_pad;
     }
-    const int smem = 1024 + a.npk * a.pk_bytes + a.nab * (a.a_bytes + a.b_bytes);
+    const int smem = 1024 + a.npk * a.pk_bytes + a.nab * a.b_bytes;
     auto kern = gemm_kernel<F>;
     static int configured[64] = {0};
     int dev = 0;

@@ -496,6 +496,43 @@ def run_suite(args):
     return 0
 
 
+def run_case(args):
+    """One matmul configuration, e.g. --case Q5_K:28672:8192:128 (format,
+    rows, K, tokens): --warmup untimed calls then --steps timed calls on
+    rotating weight copies; prints one JSON line.  Small enough to run under
+    a profiler."""
+    import torch
+    import axon_b200 as ax
+
+    fmt, rows, K, M = args.case.split(":")
+    rows, K, M = int(rows), int(K), int(M)
+    F = ax.QuantFormat[fmt]
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(3)
+    W = torch.randn(rows, K, device=dev, generator=g) * 0.02
+    base = ax.QTensor.empty(rows, K, F, device=dev)
+    ax.quantize(base, W, F)
+    del W
+    nbytes = ax.quantized_size_2d(rows, K, F)
+    qs = [base] + [ax.QTensor(base.data.clone(), base.shape, base.fmt) for _ in range(max(0, -(-(300 << 20) // nbytes) - 1))]
+    x = torch.randn(M, K, device=dev, generator=g)
+    y = torch.empty(M, rows, device=dev)
+    ws = ax.Workspace()
+    for i in range(args.warmup):
+        ax.linear_q(x, qs[i % len(qs)], out=y, workspace=ws)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        ax.linear_q(x, qs[i % len(qs)], out=y, workspace=ws)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / max(1, args.steps)
+    print(json.dumps({"case": args.case, "ms": round(ms, 5), "TOPS": round(2.0 * rows * K * M / (ms / 1e3) / 1e12, 2),
+                      "weight_GBps": round(nbytes / (ms / 1e3) / 1e9, 1)}), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -504,9 +541,12 @@ def main():
     ap.add_argument("--impl", default="axon_b200", choices=["axon_b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--suite", action="store_true", help="time every configuration (one JSON line each)")
+    ap.add_argument("--case", default=None, help="time one matmul, FMT:ROWS:K:TOKENS")
     args = ap.parse_args()
     if args.suite:
         return run_suite(args)
+    if args.case:
+        return run_case(args)
     if args.impl == "reference":
         return run_reference_arm(args)
     return run_gpu(args)
