@@ -180,53 +180,67 @@ __device__ __forceinline__ void k4_sm(const uint32_t* hw, int& sc, int& m) {
     }
 }
 
-// Dq<F>::kstep<KS, H, A>(row, out): half H of K-step KS (elements
-// 64KS..64KS+63 of the column group at `row`, shared memory with alignment
-// A) into out[4] = fp16 chunks 4H..4H+3 of that K-step.  Every format splits
-// a K-step into two halves that share no scale: nibble, 2-bit shift, or block.
+// Dq<F>::kstep<KS, A>(row, out, H): half H (0/1, warp-uniform at run time)
+// of K-step KS (elements 64KS..64KS+63 of the column group at `row`, shared
+// memory with alignment A) into out[4] = fp16 chunks 4H..4H+3 of that
+// K-step.  Every format splits a K-step into two halves that share no scale
+// (nibble, 2-bit shift, or block); H selects with register shifts and
+// selects, not branches, so all dequant warps run the same code.
 template <int F> struct Dq;
+
+__device__ __forceinline__ uint32_t sel(int h, uint32_t a, uint32_t b) { return h ? b : a; }
 
 template <> struct Dq<F_Q4_K> {
     static constexpr int A = 16;
-    template <int KS, int H, int AL>
-    __device__ static void kstep(const uint8_t* row, uint4* out) {
+    template <int KS, int AL>
+    __device__ static void kstep(const uint8_t* row, uint4* out, int H) {
         uint32_t hw[4], w[8];
         ldg_w<4, AL>(row, hw);
         ldg_w<8, AL>(row + 16 + 32 * KS, w);
         const float d = h2f_ref(hw[0] & 0xFFFFu), mn = h2f_ref(hw[0] >> 16);
         int sc, m;
-        k4_sm<2 * KS + H>(hw, sc, m);
-        const Sm g = scale_min(d * sc, mn * m);
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            const uint32_t w0 = H ? (w[2 * c] >> 4) : w[2 * c], w1 = H ? (w[2 * c + 1] >> 4) : w[2 * c + 1];
-            out[c] = chunk8(w0 & 0x0F0F0F0Fu, w1 & 0x0F0F0F0Fu, g.sub, g.D, g.Mneg);
+        if constexpr (KS < 2) {  // group 2KS+H < 4
+            sc = sel(H, byte_i<4 + 2 * KS>(hw), byte_i<5 + 2 * KS>(hw)) & 63;
+            m = sel(H, byte_i<8 + 2 * KS>(hw), byte_i<9 + 2 * KS>(hw)) & 63;
+        } else {
+            const uint32_t b8 = sel(H, byte_i<8 + 2 * KS>(hw), byte_i<9 + 2 * KS>(hw));
+            sc = (b8 & 0xF) | ((sel(H, byte_i<2 * KS>(hw), byte_i<2 * KS + 1>(hw)) >> 6) << 4);
+            m = (b8 >> 4) | ((sel(H, byte_i<4 + 2 * KS>(hw), byte_i<5 + 2 * KS>(hw)) >> 6) << 4);
         }
+        const Sm g = scale_min(d * sc, mn * m);
+        const uint32_t sh = 4 * H;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+            out[c] = chunk8((w[2 * c] >> sh) & 0x0F0F0F0Fu, (w[2 * c + 1] >> sh) & 0x0F0F0F0Fu, g.sub, g.D, g.Mneg);
     }
 };
 
 template <> struct Dq<F_Q5_K> {
     static constexpr int A = 16;
-    template <int KS, int H, int AL>
-    __device__ static void kstep(const uint8_t* row, uint4* out) {
+    template <int KS, int AL>
+    __device__ static void kstep(const uint8_t* row, uint4* out, int H) {
         uint32_t hw[4], w[8], qh[8];
         ldg_w<4, AL>(row, hw);
         ldg_w<8, AL>(row + 48 + 32 * KS, w);
         ldg_w<8, AL>(row + 16, qh);
         const float d = h2f_ref(hw[0] & 0xFFFFu), mn = h2f_ref(hw[0] >> 16);
-        constexpr int g = 2 * KS + H;
         int sc, m;
-        k4_sm<g>(hw, sc, m);
+        if constexpr (KS < 2) {
+            sc = sel(H, byte_i<4 + 2 * KS>(hw), byte_i<5 + 2 * KS>(hw)) & 63;
+            m = sel(H, byte_i<8 + 2 * KS>(hw), byte_i<9 + 2 * KS>(hw)) & 63;
+        } else {
+            const uint32_t b8 = sel(H, byte_i<8 + 2 * KS>(hw), byte_i<9 + 2 * KS>(hw));
+            sc = (b8 & 0xF) | ((sel(H, byte_i<2 * KS>(hw), byte_i<2 * KS + 1>(hw)) >> 6) << 4);
+            m = (b8 >> 4) | ((sel(H, byte_i<4 + 2 * KS>(hw), byte_i<5 + 2 * KS>(hw)) >> 6) << 4);
+        }
         const Sm s = scale_min(d * sc, mn * m);
+        const uint32_t sh = 4 * H, g = 2 * KS + H;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
             uint32_t cw[2];
 #pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                const uint32_t nib = (H ? (w[2 * c + i] >> 4) : w[2 * c + i]) & 0x0F0F0F0Fu;
-                const uint32_t hb = ((g <= 4) ? (qh[2 * c + i] << (4 - g)) : (qh[2 * c + i] >> (g - 4))) & 0x10101010u;
-                cw[i] = nib | hb;
-            }
+            for (int i = 0; i < 2; ++i)
+                cw[i] = ((w[2 * c + i] >> sh) & 0x0F0F0F0Fu) | (((qh[2 * c + i] >> g) & 0x01010101u) << 4);
             out[c] = chunk8(cw[0], cw[1], s.sub, s.D, s.Mneg);
         }
     }
@@ -234,17 +248,20 @@ template <> struct Dq<F_Q5_K> {
 
 template <> struct Dq<F_Q2_K> {
     static constexpr int A = 4;
-    template <int KS, int H, int AL>
-    __device__ static void kstep(const uint8_t* row, uint4* out) {
-        constexpr int n = KS >> 1, s = 2 * (KS & 1) + H;
+    template <int KS, int AL>
+    __device__ static void kstep(const uint8_t* row, uint4* out, int H) {
+        constexpr int n = KS >> 1, s0 = 2 * (KS & 1);
         uint32_t hd[1], sc[2], w[8];
         ldg_w<1, AL>(row, hd);
         ldg_w<2, AL>(row + 4 + 8 * n, sc);
         ldg_w<8, AL>(row + 20 + 32 * n, w);
         const float d = h2f_ref(hd[0] & 0xFFFFu), mn = h2f_ref(hd[0] >> 16);
+        const uint32_t s = s0 + H;
 #pragma unroll
         for (int lh = 0; lh < 2; ++lh) {
-            const uint32_t b = (sc[(2 * s + lh) >> 2] >> (8 * ((2 * s + lh) & 3))) & 0xFFu;
+            // scale byte of sub-block 8n + 2s + lh (bytes 2s0+lh or 2s0+2+lh)
+            const uint32_t b = sel(H, (sc[(2 * s0 + lh) >> 2] >> (8 * ((2 * s0 + lh) & 3))) & 0xFFu,
+                                   (sc[(2 * s0 + 2 + lh) >> 2] >> (8 * ((2 * s0 + 2 + lh) & 3))) & 0xFFu);
             const Sm g = scale_min(d * static_cast<float>(b & 0xF), mn * static_cast<float>(b >> 4));
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
@@ -265,26 +282,27 @@ template <> struct Dq<F_Q3_K> {
         const int hi2 = (s12[2] >> (8 * (IS & 3) + 2 * (IS >> 2))) & 3;
         return d * static_cast<float>((lo4 | (hi2 << 4)) - 32);
     }
-    template <int KS, int H, int AL>
-    __device__ static void kstep(const uint8_t* row, uint4* out) {
-        constexpr int n = KS >> 1, s = 2 * (KS & 1) + H;
+    template <int KS, int AL>
+    __device__ static void kstep(const uint8_t* row, uint4* out, int H) {
+        constexpr int n = KS >> 1, s0 = 2 * (KS & 1);
         uint32_t hd[1], s12[3], w[8], hm[8];
         ld_words<1>(row + 108, hd);
         ld_words<3>(row + 96, s12);
         ld_words<8>(row + 32 + 32 * n, w);
         ld_words<8>(row, hm);
         const float d = h2f_ref(hd[0] & 0xFFFFu);
-        const Sm g0 = scale_off(subscale<8 * n + 2 * s>(s12, d), 4.0f);
-        const Sm g1 = scale_off(subscale<8 * n + 2 * s + 1>(s12, d), 4.0f);
+        const float D0 = H ? subscale<8 * n + 2 * s0 + 2>(s12, d) : subscale<8 * n + 2 * s0>(s12, d);
+        const float D1 = H ? subscale<8 * n + 2 * s0 + 3>(s12, d) : subscale<8 * n + 2 * s0 + 1>(s12, d);
+        const Sm g0 = scale_off(D0, 4.0f), g1 = scale_off(D1, 4.0f);
+        const uint32_t s = s0 + H, hb = 4 * n + s;
 #pragma unroll
         for (int lh = 0; lh < 2; ++lh) {
             const Sm& g = lh ? g1 : g0;
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
                 const int wi = 4 * lh + 2 * c;
-                const uint32_t c0 = ((w[wi] >> (2 * s)) & 0x03030303u) | (((hm[wi] >> (4 * n + s)) & 0x01010101u) << 2);
-                const uint32_t c1 =
-                    ((w[wi + 1] >> (2 * s)) & 0x03030303u) | (((hm[wi + 1] >> (4 * n + s)) & 0x01010101u) << 2);
+                const uint32_t c0 = ((w[wi] >> (2 * s)) & 0x03030303u) | (((hm[wi] >> hb) & 0x01010101u) << 2);
+                const uint32_t c1 = ((w[wi + 1] >> (2 * s)) & 0x03030303u) | (((hm[wi + 1] >> hb) & 0x01010101u) << 2);
                 out[2 * lh + c] = chunk8(c0, c1, g.sub, g.D, g.Mneg);
             }
         }
@@ -293,25 +311,28 @@ template <> struct Dq<F_Q3_K> {
 
 template <> struct Dq<F_Q6_K> {
     static constexpr int A = 1;
-    template <int KS, int H, int AL>
-    __device__ static void kstep(const uint8_t* row, uint4* out) {
-        constexpr int n = KS >> 1, t = 2 * (KS & 1) + H;
-        uint32_t hd[1], sc[2], qh[8], ql[8];
+    template <int KS, int AL>
+    __device__ static void kstep(const uint8_t* row, uint4* out, int H) {
+        constexpr int n = KS >> 1, hi_nib = KS & 1;  // t = 2*(KS&1) + H
+        uint32_t hd[1], sc[4], qh[8], ql[8];
         ld_words<1>(row + 208, hd);
-        ld_words<2>(row + 192 + 8 * n, sc);
+        ld_words<4>(row + 192, sc);
         ld_words<8>(row + 128 + 32 * n, qh);
-        ld_words<8>(row + 64 * n + 32 * (t & 1), ql);
+        ld_words<8>(row + 64 * n + 32 * H, ql);
         const float d = h2f_ref(hd[0] & 0xFFFFu);
+        const uint32_t t = 2 * hi_nib + H;
 #pragma unroll
         for (int lh = 0; lh < 2; ++lh) {
-            const int j = 2 * t + lh;
-            const float Dv = d * static_cast<float>(static_cast<int8_t>((sc[j >> 2] >> (8 * (j & 3))) & 0xFFu));
+            constexpr int jb = 8 * n + 4 * hi_nib;  // sub-block 8n + 2t + lh
+            const uint32_t sb = sel(H, (sc[(jb + lh) >> 2] >> (8 * ((jb + lh) & 3))) & 0xFFu,
+                                    (sc[(jb + 2 + lh) >> 2] >> (8 * ((jb + 2 + lh) & 3))) & 0xFFu);
+            const float Dv = d * static_cast<float>(static_cast<int8_t>(sb));
             const Sm g = scale_off(Dv, 32.0f);
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
                 const int wi = 4 * lh + 2 * c;
-                const uint32_t n0 = ((t & 2) ? (ql[wi] >> 4) : ql[wi]) & 0x0F0F0F0Fu;
-                const uint32_t n1 = ((t & 2) ? (ql[wi + 1] >> 4) : ql[wi + 1]) & 0x0F0F0F0Fu;
+                const uint32_t n0 = (hi_nib ? (ql[wi] >> 4) : ql[wi]) & 0x0F0F0F0Fu;
+                const uint32_t n1 = (hi_nib ? (ql[wi + 1] >> 4) : ql[wi + 1]) & 0x0F0F0F0Fu;
                 const uint32_t c0 = n0 | (((qh[wi] >> (2 * t)) & 0x03030303u) << 4);
                 const uint32_t c1 = n1 | (((qh[wi + 1] >> (2 * t)) & 0x03030303u) << 4);
                 out[2 * lh + c] = chunk8(c0, c1, g.sub, g.D, g.Mneg);
@@ -323,8 +344,8 @@ template <> struct Dq<F_Q6_K> {
 // Q8_0: half H = block 2KS+H of the column group; signed codes biased by 128.
 template <> struct Dq<F_Q8_0> {
     static constexpr int A = 1;
-    template <int KS, int H, int AL>
-    __device__ static void kstep(const uint8_t* row, uint4* out) {
+    template <int KS, int AL>
+    __device__ static void kstep(const uint8_t* row, uint4* out, int H) {
         const uint8_t* blk = row + 34 * (2 * KS + H);
         uint32_t hd[1], w[8];
         ld_words<1>(blk, hd);
@@ -339,8 +360,8 @@ template <> struct Dq<F_Q8_0> {
 // Q4_0: half H = block 2KS+H; byte i holds elements 2i (low) and 2i+1 (high).
 template <> struct Dq<F_Q4_0> {
     static constexpr int A = 1;
-    template <int KS, int H, int AL>
-    __device__ static void kstep(const uint8_t* row, uint4* out) {
+    template <int KS, int AL>
+    __device__ static void kstep(const uint8_t* row, uint4* out, int H) {
         const uint8_t* blk = row + 18 * (2 * KS + H);
         uint32_t hd[1], w[4];
         ld_words<1>(blk, hd);
@@ -354,13 +375,7 @@ template <> struct Dq<F_Q4_0> {
     }
 };
 
-template <int F, int KS, int H>
-__device__ __forceinline__ void dq_step(const uint8_t* row, uint4* o, int aligned) {
-    if (aligned && Dq<F>::A > 1) Dq<F>::template kstep<KS, H, Dq<F>::A>(row, o);
-    else Dq<F>::template kstep<KS, H, 1>(row, o);
-}
-
-template <int F>
+template <int F, int AL>
 __global__ void __launch_bounds__(kThreadsGemm, 1) gemm_kernel(GemmArgs a) {
     using C = CG<F>;
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -499,17 +514,10 @@ __global__ void __launch_bounds__(kThreadsGemm, 1) gemm_kernel(GemmArgs a) {
                 if (j >= a.nab && !gwait(&bars->ab_empty[s], ((j / a.nab) - 1) & 1, abort_flag, a.err)) break;
                 uint4 o[4];
                 if (row_ok) {
-                    if (h == 0) {
-                        if (k == 0) dq_step<F, 0, 0>(rowp, o, a.aligned);
-                        else if (k == 1) dq_step<F, 1, 0>(rowp, o, a.aligned);
-                        else if (k == 2) dq_step<F, 2, 0>(rowp, o, a.aligned);
-                        else dq_step<F, 3, 0>(rowp, o, a.aligned);
-                    } else {
-                        if (k == 0) dq_step<F, 0, 1>(rowp, o, a.aligned);
-                        else if (k == 1) dq_step<F, 1, 1>(rowp, o, a.aligned);
-                        else if (k == 2) dq_step<F, 2, 1>(rowp, o, a.aligned);
-                        else dq_step<F, 3, 1>(rowp, o, a.aligned);
-                    }
+                    if (k == 0) Dq<F>::template kstep<0, AL>(rowp, o, h);
+                    else if (k == 1) Dq<F>::template kstep<1, AL>(rowp, o, h);
+                    else if (k == 2) Dq<F>::template kstep<2, AL>(rowp, o, h);
+                    else Dq<F>::template kstep<3, AL>(rowp, o, h);
                     if (tail) {
                         // zero the elements past K (and blocks past the row's end)
 #pragma unroll
@@ -720,15 +728,16 @@ cudaError_t launch_gemm(const void* w, const float* x, float* out, int64_t M, in
         a.part_ld = g.ntok_pad;
     }
     const int smem = 1024 + a.npk * a.pk_bytes + a.nab * a.b_bytes;
-    auto kern = gemm_kernel<F>;
-    static int configured[64] = {0};
+    auto kern = (a.aligned && Dq<F>::A > 1) ? gemm_kernel<F, Dq<F>::A> : gemm_kernel<F, 1>;
+    static int configured[2][64] = {{0}};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if (smem > configured[dev]) {
+    const int ai = (a.aligned && Dq<F>::A > 1) ? 1 : 0;
+    if (smem > configured[ai][dev]) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
-        configured[dev] = smem;
+        configured[ai][dev] = smem;
     }
     const int grid = g.nrt * g.nct * g.splits;
     kern<<<grid, kThreadsGemm, smem, s>>>(a);
