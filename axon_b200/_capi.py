@@ -72,7 +72,21 @@ SIGNATURES = {
     "axq_matmul": (ctypes.c_int, [ctypes.c_int, _vp, _vp, _vp, _i64, _i64, _i64, ctypes.c_uint, _vp, _sz, _vp]),
     "axq_workspace_status": (ctypes.c_int, [_vp, _vp]),
     "axq_matmul_noalloc": (ctypes.c_int, [ctypes.c_int, _vp, _vp, _vp, _i64, _i64, _i64, ctypes.c_uint, _vp]),
+    "axq_comm_unique_id": (ctypes.c_int, [_vp, _sz]),
+    "axq_comm_init": (ctypes.c_int, [ctypes.POINTER(_vp), _vp, _sz, ctypes.c_int, ctypes.c_int]),
+    "axq_comm_init_all": (ctypes.c_int, [ctypes.POINTER(_vp), ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
+    "axq_group_start": (ctypes.c_int, []),
+    "axq_group_end": (ctypes.c_int, []),
+    "axq_comm_destroy": (ctypes.c_int, [_vp]),
+    "axq_comm_abort": (ctypes.c_int, [_vp]),
+    "axq_comm_check": (ctypes.c_int, [_vp]),
+    "axq_comm_inject_failure": (ctypes.c_int, [_vp, _i64]),
+    "axq_allgather": (ctypes.c_int, [_vp, _vp, _sz, _vp]),
+    "axq_matmul_sharded": (ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, _vp, _i64, _i64, _i64, ctypes.c_uint, _vp,
+                                          _sz, _vp]),
 }
+
+COMM_ID_BYTES = 128  # AXQ_COMM_ID_BYTES
 
 _lib = None
 _lock = threading.Lock()

@@ -117,6 +117,56 @@ int axq_matmul_noalloc(int fmt, const void* a_q, const float* b, float* out, int
  * gave up a bounded wait (AXQ_ERR_TIMEOUT) — 0 otherwise. */
 int axq_workspace_status(const void* workspace, axq_stream_t stream);
 
+/* ---- Row-sharded multi-GPU matmul (NCCL, loaded at run time) ------------
+ * The reference runs on one CPU; these have no reference counterpart.  They
+ * shard the quantized operand by rows (blocks never span rows,
+ * cpu_backend.cpp:1174-1185): rank r of G holds packed rows
+ * [r*M/G, (r+1)*M/G) of A_q and a full copy of B.  Communicators are opaque
+ * handles bound to the device that was current when they were created. */
+#define AXQ_COMM_ID_BYTES 128 /* bytes of a communicator id (ncclUniqueId) */
+
+/* Writes a fresh communicator id to id_out (>= AXQ_COMM_ID_BYTES bytes); one
+ * rank creates it and hands it to every rank out of band. */
+int axq_comm_unique_id(void* id_out, size_t id_bytes);
+
+/* One process (or thread) per GPU: joins rank `rank` of `nranks` on the
+ * current device.  Collective across ranks; *comm_out is set on success. */
+int axq_comm_init(void** comm_out, const void* id, size_t id_bytes, int nranks, int rank);
+
+/* One process driving `ndev` GPUs: comms_out[i] is rank i on device devs[i].
+ * Calls on several of them must be bracketed by axq_group_start/_end. */
+int axq_comm_init_all(void** comms_out, int ndev, const int* devs);
+int axq_group_start(void);
+int axq_group_end(void);
+
+/* Frees a communicator after its work has finished (destroy) or at once,
+ * cancelling work in flight (abort, for error paths).  NULL is a no-op. */
+int axq_comm_destroy(void* comm);
+int axq_comm_abort(void* comm);
+
+/* AXQ_ERR_COMM (with NCCL's message) if the communicator recorded an
+ * asynchronous error (a peer failed or a collective timed out), else 0. */
+int axq_comm_check(void* comm);
+
+/* Host-side failure injection for testing callers' error paths: the
+ * communicator's `collective_index`-th collective from now (0 = the next)
+ * fails with AXQ_ERR_COMM before anything is enqueued on the GPU; a negative
+ * index disarms it.  No GPU work is faulted. */
+int axq_comm_inject_failure(void* comm, int64_t collective_index);
+
+/* In-place all-gather: rank r's `count_per_rank` floats sit at
+ * buf + r*count_per_rank; on completion every rank holds all of them. */
+int axq_allgather(void* comm, float* buf, size_t count_per_rank, axq_stream_t stream);
+
+/* out[M x N] (row-major, full size on every rank) = A_q . B where this rank
+ * passes only its row shard a_q_local (M/G packed rows of K elements).  The
+ * local rows are computed in place into out and then all-gathered on
+ * `stream`.  M must be divisible by the number of ranks;
+ * AXQ_FLAG_B_TOKMAJOR is honoured, AXQ_FLAG_OUT_TOKMAJOR is not supported.
+ * `workspace` as for axq_matmul with M/G rows. */
+int axq_matmul_sharded(void* comm, int fmt, const void* a_q_local, const float* b, float* out, int64_t M, int64_t K,
+                       int64_t N, unsigned flags, void* workspace, size_t workspace_bytes, axq_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

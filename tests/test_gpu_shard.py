@@ -1,0 +1,108 @@
+"""Row-sharded matmul through the C ABI on the GPU.
+
+One GPU: a one-rank communicator (axq_matmul_sharded then equals
+axq_matmul), failure injection and error checks.  Two or more GPUs: the
+parity run of tests/sharded_worker.py under torch.distributed.run, one
+process per GPU, every rank's gathered output checked against the oracle.
+"""
+import json
+import os
+import socket
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+from conftest import ROOT, gen, rel_err
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-3  # max|y - y_ref| <= TOL * max|y_ref|, the matmul parity rule
+
+
+@pytest.fixture(scope="module")
+def comm1(cuda):
+    import axon_b200 as ax
+    c = ax.Communicator.create(ax.Communicator.unique_id(), 1, 0)
+    yield c
+    c.destroy()
+
+
+@pytest.mark.parametrize("fmt,M,K,N", [("Q5_K", 256, 4096, 1), ("Q3_K", 128, 2048, 8), ("Q4_K", 256, 2048, 32)])
+def test_one_rank_sharded_equals_matmul_and_oracle(orc, comm1, fmt, M, K, N):
+    import torch
+    import axon_b200 as ax
+    rng = np.random.default_rng(M * N + K)
+    q = orc.quantize(fmt, gen(rng, (M, K), "randn"))
+    b = rng.standard_normal((K, N)).astype(np.float32)
+    F = ax.QuantFormat[fmt]
+    a = ax.QTensor(torch.from_numpy(q).cuda(), (M, K), F)
+    bd = torch.from_numpy(b).cuda()
+    out = torch.full((M, N), float("nan"), device="cuda")
+    ax.matmul_sharded(out, a, bd, comm1, M)
+    ref_out = torch.full((M, N), float("nan"), device="cuda")
+    ax.matmul_q(ref_out, a, bd)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref_out)
+    assert rel_err(out.cpu().numpy(), orc.matmul(fmt, q, b, M, K)) <= TOL
+
+
+def test_injected_failure_is_reported_and_comm_stays_usable(comm1):
+    import torch
+    import axon_b200 as ax
+    buf = torch.arange(16, dtype=torch.float32, device="cuda")
+    comm1.inject_failure(1)
+    ax.allgather_(buf, comm1)  # collective 0 runs
+    with pytest.raises(ax.AxqError) as e:
+        ax.allgather_(buf, comm1)  # collective 1 fails on the host
+    assert e.value.status == ax.Status.ERR_COMM and "injected" in str(e.value)
+    ax.allgather_(buf, comm1)
+    torch.cuda.synchronize()
+    comm1.check()
+    assert torch.equal(buf.cpu(), torch.arange(16, dtype=torch.float32))
+
+
+def test_sharded_argument_errors(comm1):
+    import torch
+    import axon_b200 as ax
+    L = ax.lib()
+    st = L.axq_matmul_sharded(comm1.handle, 5, None, None, None, 8, 256, 1, ax.FLAG_OUT_TOKMAJOR, None, 0, None)
+    assert st == ax.Status.ERR_UNSUPPORTED
+    a = ax.QTensor.empty(8, 256, ax.QuantFormat.Q5_K, device="cuda")
+    with pytest.raises(ax.AxqError, match="local shard"):
+        ax.matmul_sharded(torch.empty(16, 1, device="cuda"), a, torch.empty(256, 1, device="cuda"), comm1, 16)
+
+
+def test_destroyed_communicator_is_refused(cuda):
+    import axon_b200 as ax
+    c = ax.Communicator.create(ax.Communicator.unique_id(), 1, 0)
+    c.destroy()
+    with pytest.raises(ax.AxqError, match="destroyed"):
+        c.check()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("ranks", [2])
+def test_multi_gpu_sharded_parity(cuda, tmp_path, ranks):
+    import torch
+    if torch.cuda.device_count() < ranks:
+        pytest.skip(f"needs {ranks} GPUs, have {torch.cuda.device_count()}")
+    cmd = ["timeout", "-k", "30", "400", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           f"--nproc-per-node={ranks}", "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
+           os.path.join(ROOT, "tests", "sharded_worker.py"), str(tmp_path)]
+    r = subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    import axon_b200 as ax
+    for rank in range(ranks):
+        rep = json.load(open(tmp_path / f"rank{rank}.json"))
+        for c in rep["cases"]:
+            assert c["err"] <= TOL and c["err_tokmajor"] <= TOL, c
+        assert rep["injected"][0] == ax.Status.ERR_COMM, rep["injected"]
+        assert rep["allgather_ok"] and rep["check_ok"]
+        assert rep.get("wrong_device_status") == ax.Status.ERR_INVALID
