@@ -133,7 +133,7 @@ size_t axq_matmul_workspace_size(int fmt, int64_t M, int64_t K, int64_t N) {
     if (!be || K < 0 || N < 0 || M < 0) return 0;
     if (N > kGemvMaxN) return kStatusBytes + gemm_workspace_bytes(fmt, M, K, N);
     const int64_t Kp = (K + be - 1) / be * be;
-    return kStatusBytes + gemv_workspace_layout(Kp, N).total;
+    return kStatusBytes + gemv_workspace_bytes(Kp, N);
 }
 
 int axq_matmul(int fmt, const void* a_q, const float* b, float* out, int64_t M, int64_t K, int64_t N, unsigned flags,

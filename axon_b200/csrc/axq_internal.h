@@ -20,11 +20,9 @@ void set_last_error(const std::string& msg);
 cudaError_t pack_dispatch(int fmt, const float* src, void* dst, int64_t rows, int64_t cols, cudaStream_t s);
 cudaError_t dequant_dispatch(int fmt, const void* src, float* dst, int64_t rows, int64_t cols, cudaStream_t s);
 
-// Workspace for the block-quantized activations of a GEMV-class matmul.
-struct GemvWorkspace {
-    size_t off_hi, off_lo, off_u, off_s16, total;
-};
-GemvWorkspace gemv_workspace_layout(int64_t Kp, int64_t ntok);
+// Workspace bytes for the block-quantized activations of a GEMV-class
+// matmul (Kp = K rounded up to the format's block).
+size_t gemv_workspace_bytes(int64_t Kp, int64_t ntok);
 
 cudaError_t gemv_dispatch(int fmt, const void* w, const float* x, float* out, int64_t M, int64_t K, int64_t N, int flags,
                           void* ws, size_t ws_bytes, int* err, cudaStream_t s);
