@@ -28,6 +28,8 @@
 //    the bit decode.  The split's error is ~1e-5 of the chunk's max |x|, far
 //    inside the 1e-3 * max|y| tolerance.
 #include <algorithm>
+#include <type_traits>
+#include <utility>
 
 #include "axq_common.cuh"
 #include "axq_internal.h"
@@ -102,18 +104,18 @@ __device__ __forceinline__ float act_u(const ActCG& X, int t) {
     return __ldg(reinterpret_cast<const float*>(X.p + kActRec * t + 576));
 }
 
-// The 16 activation runs of one CG for NT tokens, loaded D runs ahead of
-// their use (every format consumes the runs in increasing order), so the
-// L1 latency of the loads overlaps the dot products of earlier runs.  SX:
-// also fetch the integer run sums.  Indexes are compile-time after
+// The 8 activation runs of one half CG (runs 8H..8H+7) for NT tokens,
+// loaded D runs ahead of their use (runs are consumed in increasing order),
+// so the L1 latency of the loads overlaps the dot products of earlier runs.
+// SX: also fetch the integer run sums.  Indexes are compile-time after
 // unrolling, so the arrays live in registers (only D+1 runs at a time).
-template <int NT, bool SX>
+template <int NT, bool SX, int H>
 struct ActPipe {
     static constexpr int D = (NT == 1) ? 3 : (NT == 2 ? 2 : 1);
     ActCG X;
     int ntok;
-    Run16 r[NT][16];
-    int sx[NT][16];
+    Run16 r[NT][8];
+    int sx[NT][8];
     __device__ __forceinline__ ActPipe(ActCG x, int nt) : X(x), ntok(nt) {
 #pragma unroll
         for (int j = 0; j < D; ++j) load(j);
@@ -121,15 +123,15 @@ struct ActPipe {
     __device__ __forceinline__ void load(int j) {
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
-            // tokens past ntok re-read the last token (never used)
+            // tokens past ntok re-read the last token (never written out)
             const int tt = (NT == 1 || t < ntok) ? t : ntok - 1;
-            ld_run(X, tt, 16 * j, r[t][j]);
-            if constexpr (SX) sx[t][j] = isx1(X, tt, j);
+            ld_run(X, tt, 16 * (8 * H + j), r[t][j]);
+            if constexpr (SX) sx[t][j] = isx1(X, tt, 8 * H + j);
         }
     }
-    // Call at the start of run j.
+    // Call at the start of run j (0..7 within the half).
     __device__ __forceinline__ void step(int j) {
-        if (j + D < 16) load(j + D);
+        if (j + D < 8) load(j + D);
     }
 };
 
@@ -140,15 +142,15 @@ __device__ __forceinline__ void dot16(const uint32_t* q, const Run16& r, int& H,
     L = dp4<SG>(q[3], r.l[3], dp4<SG>(q[2], r.l[2], dp4<SG>(q[1], r.l[1], dp4<SG>(q[0], r.l[0], 0))));
 }
 
-// Integer accumulators of one column group: sum_j s_j*H_j, sum_j s_j*L_j and
-// sum_j m_j*isx_j (bounds per format are stated at each use).
-template <int NT> struct IAcc {
-    int hs[NT], ls[NT], ms[NT];
-    __device__ __forceinline__ void zero() {
-#pragma unroll
-        for (int t = 0; t < NT; ++t) hs[t] = ls[t] = ms[t] = 0;
-    }
-};
+// Compile-time loop: f(std::integral_constant<int, J>) for J = 0..N-1.
+template <class Fn, int... Js>
+__device__ __forceinline__ void static_for_impl(Fn&& f, std::integer_sequence<int, Js...>) {
+    (f(std::integral_constant<int, Js>{}), ...);
+}
+template <int N, class Fn>
+__device__ __forceinline__ void static_for(Fn&& f) {
+    static_for_impl(f, std::make_integer_sequence<int, N>{});
+}
 
 // Byte i (compile-time) of a little-endian word array.
 template <int I>
@@ -174,436 +176,313 @@ __device__ __forceinline__ void k4sm(const uint32_t* hw, int& sc, int& m) {
     }
 }
 
-// Per-format processing of one full column group (256 elements) of one
-// row: decode (bit-level layouts of cpu_backend.cpp:1340-1504) into runs of
-// code words, dot them with the activations in integers, and add
-//   u * (dscale * (254*HS + LS) - mscale * MS)
-// to acc[t].  Nibbles and 2-bit fields are masked in place (not shifted);
-// the run's integer scale is multiplied by the complementary power of two so
-// every run of a group carries the same factor, divided out in dscale.
-template <int F> struct Lane;
+// ---- K-quant row decoders --------------------------------------------------
+// Row<F, H, AL> decodes half H (elements 128H..128H+127) of one K-quant
+// block (bit-level layouts of cpu_backend.cpp:1340-1504) of one row into
+// runs of RL = 16 or 32 elements: run<J>(q, sc, m) gives the run's code
+// words and its integer scale and offset weight, such that
+//   sum_i x_i * value_i = u * (dscale * (254*HS + LS) - mscale * MS),
+//   HS = sum_J sc_J * dot(q_J, hi), LS = sum_J sc_J * dot(q_J, lo),
+//   MS = sum_J m_J * (run sum of 254*hi + lo).
+// Nibbles and 2-bit fields are masked in place (not shifted); sc carries the
+// complementary power of two so every run of the block has the same factor,
+// which dscale divides out.  Per-block int32 bounds are stated per format.
 
-// Q8_0: CG = 8 blocks {u16 d; i8 qs[32]}; one signed 32-element run each,
-// S = 254*H + L <= 32*127*32385 per block.
-template <> struct Lane<F_Q8_0> {
-    static constexpr int CGB = 8 * 34, A = 1, PERM = 0;
-    static constexpr bool PIPE_SX = false;
-    template <int B, int NT>
-    __device__ __forceinline__ static void blk(const uint8_t* cg, ActPipe<NT, false>& P, float* accf, int ntok) {
-        uint32_t hd[1], w[8];
-        ld_words<1>(cg + 34 * B, hd);
-        ld_words<8>(cg + 34 * B + 2, w);
-        const float d = h2f_ref(hd[0] & 0xFFFFu);
-        P.step(2 * B);
-        P.step(2 * B + 1);
+// Q2_K {d, dmin, scales[16], qs[64]}: half H = qs[32H..32H+31]; run J = 2s+lh
+// holds the 2-bit field at shift 2s of qs[32H + 16lh + l] (x4^s in place,
+// scale x4^(3-s)): |HS|, |LS| <= 16 * 15*64 * 16*3*127 < 1e8,
+// MS <= 16*15*16*32385.
+template <int H, int AL> struct RowQ2K {
+    static constexpr int RL = 16;
+    uint32_t hd, scw[2], mw[2], w[8];
+    __device__ __forceinline__ void load(const uint8_t* cg) {
+        uint32_t h[1], sc[2];
+        ldw<1, AL>(cg, h);
+        ldw<2, AL>(cg + 4 + 8 * H, sc);
+        hd = h[0];
 #pragma unroll
-        for (int t = 0; t < NT; ++t) {
-            if (t < ntok) {
-                int h0, l0, h1, l1;
-                dot16<true>(w, P.r[t][2 * B], h0, l0);
-                dot16<true>(w + 4, P.r[t][2 * B + 1], h1, l1);
-                const int S = (h0 + h1) * 254 + (l0 + l1);
-                accf[t] = fmaf(d, static_cast<float>(S), accf[t]);
-            }
+        for (int i = 0; i < 2; ++i) {
+            scw[i] = sc[i] & 0x0F0F0F0Fu;
+            mw[i] = (sc[i] >> 4) & 0x0F0F0F0Fu;
         }
+        ldw<8, AL>(cg + 20 + 32 * H, w);
     }
-    template <int AL, int NT>
-    __device__ __forceinline__ static void process(const uint8_t* cg, int nblk_valid, const ActCG& X, float* acc, int ntok) {
-        ActPipe<NT, PIPE_SX> P(X, ntok);
-        float accf[NT];
+    template <int J>
+    __device__ __forceinline__ void run(uint32_t* q, int& sc, int& m) const {
+        constexpr int s = J >> 1, lh = J & 1;
 #pragma unroll
-        for (int t = 0; t < NT; ++t) accf[t] = 0.0f;
-        if (nblk_valid >= 8) {
-            blk<0, NT>(cg, P, accf, ntok); blk<1, NT>(cg, P, accf, ntok); blk<2, NT>(cg, P, accf, ntok); blk<3, NT>(cg, P, accf, ntok);
-            blk<4, NT>(cg, P, accf, ntok); blk<5, NT>(cg, P, accf, ntok); blk<6, NT>(cg, P, accf, ntok); blk<7, NT>(cg, P, accf, ntok);
-        } else {
-            if (nblk_valid > 0) blk<0, NT>(cg, P, accf, ntok);
-            if (nblk_valid > 1) blk<1, NT>(cg, P, accf, ntok);
-            if (nblk_valid > 2) blk<2, NT>(cg, P, accf, ntok);
-            if (nblk_valid > 3) blk<3, NT>(cg, P, accf, ntok);
-            if (nblk_valid > 4) blk<4, NT>(cg, P, accf, ntok);
-            if (nblk_valid > 5) blk<5, NT>(cg, P, accf, ntok);
-            if (nblk_valid > 6) blk<6, NT>(cg, P, accf, ntok);
-        }
-#pragma unroll
-        for (int t = 0; t < NT; ++t)
-            if (t < ntok) acc[t] = fmaf(act_u(X, t), accf[t], acc[t]);
+        for (int v = 0; v < 4; ++v) q[v] = w[4 * lh + v] & (0x03030303u << (2 * s));
+        sc = static_cast<int>(__byte_perm(scw[J >> 2], 0u, 0x4440u | (J & 3))) << (6 - 2 * s);
+        m = static_cast<int>(__byte_perm(mw[J >> 2], 0u, 0x4440u | (J & 3)));
     }
+    __device__ __forceinline__ float dscale() const { return h2f_ref(hd & 0xFFFFu) * (1.0f / 64.0f); }
+    __device__ __forceinline__ float mscale() const { return h2f_ref(hd >> 16); }
 };
 
-// Q4_0: CG = 8 blocks {u16 d; u8 qs[16]}; low nibbles = even elements, high
-// nibbles (kept in place, x16) = odd elements; the activation prep orders
-// each 32-block as evens then odds.  Per block
-// S16 = 16*(254*H + L) - 128*isx32 = 16*sum (code - 8)*X, |S16| < 4e8.
-template <> struct Lane<F_Q4_0> {
-    static constexpr int CGB = 8 * 18, A = 1, PERM = 1;
-    static constexpr bool PIPE_SX = true;
-    template <int B, int NT>
-    __device__ __forceinline__ static void blk(const uint8_t* cg, ActPipe<NT, true>& P, float* accf, int ntok) {
-        uint32_t hd[1], w[4], ql[4], qh[4];
-        ld_words<1>(cg + 18 * B, hd);
-        ld_words<4>(cg + 18 * B + 2, w);
-        const float d16 = h2f_ref(hd[0] & 0xFFFFu) * 0.0625f;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            ql[j] = w[j] & 0x0F0F0F0Fu;
-            qh[j] = w[j] & 0xF0F0F0F0u;
-        }
-        P.step(2 * B);
-        P.step(2 * B + 1);
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-            if (t < ntok) {
-                const int sx = P.sx[t][2 * B] + P.sx[t][2 * B + 1];
-                int h0, l0, h1, l1;
-                dot16<false>(ql, P.r[t][2 * B], h0, l0);
-                dot16<false>(qh, P.r[t][2 * B + 1], h1, l1);
-                const int S16 = (16 * h0 + h1) * 254 + (16 * l0 + l1) - 128 * sx;
-                accf[t] = fmaf(d16, static_cast<float>(S16), accf[t]);
-            }
-        }
+// Q3_K {hmask[32], qs[64], scales[12], d}: half H = qs[32H..]; run J = 2s+lh,
+// code = 2-bit field (shift 2s of qs[32H + 16lh + l]) + 4 * bit (4H+s) of
+// hmask[16lh + l]; value = d * (6-bit scale - 32) * (code - 4).  The code is
+// assembled in place at bit p = min(2s, 4) (x2^p), the scale multiplied by
+// 2^(4-p): |HS| <= 16 * 32*16 * 16*7*127 < 1.2e8; |MS| <= 16*32*16*32385.
+template <int H, int AL> struct RowQ3K {
+    static constexpr int RL = 16;
+    uint32_t hd, s12[3], hm[8], w[8];
+    __device__ __forceinline__ void load(const uint8_t* cg) {
+        uint32_t h[1];
+        ld_words<1>(cg + 108, h);
+        hd = h[0];
+        ld_words<3>(cg + 96, s12);
+        ld_words<8>(cg, hm);
+        ld_words<8>(cg + 32 + 32 * H, w);
     }
-    template <int AL, int NT>
-    __device__ __forceinline__ static void process(const uint8_t* cg, int nblk_valid, const ActCG& X, float* acc, int ntok) {
-        ActPipe<NT, PIPE_SX> P(X, ntok);
-        float accf[NT];
-#pragma unroll
-        for (int t = 0; t < NT; ++t) accf[t] = 0.0f;
-        if (nblk_valid >= 8) {
-            blk<0, NT>(cg, P, accf, ntok); blk<1, NT>(cg, P, accf, ntok); blk<2, NT>(cg, P, accf, ntok); blk<3, NT>(cg, P, accf, ntok);
-            blk<4, NT>(cg, P, accf, ntok); blk<5, NT>(cg, P, accf, ntok); blk<6, NT>(cg, P, accf, ntok); blk<7, NT>(cg, P, accf, ntok);
-        } else {
-            if (nblk_valid > 0) blk<0, NT>(cg, P, accf, ntok);
-            if (nblk_valid > 1) blk<1, NT>(cg, P, accf, ntok);
-            if (nblk_valid > 2) blk<2, NT>(cg, P, accf, ntok);
-            if (nblk_valid > 3) blk<3, NT>(cg, P, accf, ntok);
-            if (nblk_valid > 4) blk<4, NT>(cg, P, accf, ntok);
-            if (nblk_valid > 5) blk<5, NT>(cg, P, accf, ntok);
-            if (nblk_valid > 6) blk<6, NT>(cg, P, accf, ntok);
-        }
-#pragma unroll
-        for (int t = 0; t < NT; ++t)
-            if (t < ntok) acc[t] = fmaf(act_u(X, t), accf[t], acc[t]);
-    }
-};
-
-// Q2_K {d, dmin, scales[16], qs[64]}: sub-block j = 8n + 2s + lh holds the
-// 2-bit field at shift 2s of qs[32n + 16lh + l]; masked in place (x4^s), the
-// 4-bit scale is multiplied by 4^(3-s), so HS carries x64:
-// |HS|, |LS| <= 16 runs * 15*64 * 16*3*127 < 1e8; MS <= 16*15*16*32385.
-template <> struct Lane<F_Q2_K> {
-    static constexpr int CGB = 84, A = 4, PERM = 0;
-    template <int AL, int NT>
-    __device__ __forceinline__ static void process(const uint8_t* cg, int, const ActCG& X, float* acc, int ntok) {
-        uint32_t hd[1], sc[4];
-        ldw<1, AL>(cg, hd);
-        ldw<4, AL>(cg + 4, sc);
-        ActPipe<NT, true> P(X, ntok);
-        IAcc<NT> ia;
-        ia.zero();
-#pragma unroll
-        for (int n = 0; n < 2; ++n) {
-            uint32_t w[8];
-            ldw<8, AL>(cg + 20 + 32 * n, w);
-#pragma unroll
-            for (int s = 0; s < 4; ++s) {
-#pragma unroll
-                for (int lh = 0; lh < 2; ++lh) {
-                    const int j = 8 * n + 2 * s + lh;
-                    uint32_t q[4];
-#pragma unroll
-                    for (int v = 0; v < 4; ++v) q[v] = w[4 * lh + v] & (0x03030303u << (2 * s));
-                    const uint32_t b = (sc[j >> 2] >> (8 * (j & 3))) & 0xFFu;
-                    const int scl = static_cast<int>((b & 0xFu) << (6 - 2 * s));
-                    const int mj = static_cast<int>(b >> 4);
-                    P.step(j);
-#pragma unroll
-                    for (int t = 0; t < NT; ++t) {
-                        if (t < ntok) {
-                            int H, L;
-                            dot16<false>(q, P.r[t][j], H, L);
-                            ia.hs[t] += scl * H;
-                            ia.ls[t] += scl * L;
-                            ia.ms[t] += mj * P.sx[t][j];
-                        }
-                    }
-                }
-            }
-        }
-        const float d64 = h2f_ref(hd[0] & 0xFFFFu) * (1.0f / 64.0f), mn = h2f_ref(hd[0] >> 16);
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-            if (t < ntok) {
-                const float dot = fmaf(254.0f, static_cast<float>(ia.hs[t]), static_cast<float>(ia.ls[t]));
-                acc[t] = fmaf(act_u(X, t), fmaf(d64, dot, -mn * static_cast<float>(ia.ms[t])), acc[t]);
-            }
-        }
-    }
-};
-
-// Q3_K {hmask[32], qs[64], scales[12], d}: code = 2-bit field + 4*hmask bit,
-// value = d * (6-bit scale - 32) * (code - 4).  The code is assembled in
-// place at bit p = min(2s, 4) (x2^p) and the scale multiplied by 2^(4-p):
-// |HS| <= 16 runs * 32*16 * 16*7*127 < 1.2e8; |MS| <= 16*32*16*32385.
-template <> struct Lane<F_Q3_K> {
-    static constexpr int CGB = 110, A = 1, PERM = 0;
     template <int IS>
-    __device__ __forceinline__ static int subscale(const uint32_t* s12) {
+    __device__ __forceinline__ int subscale() const {
         constexpr int lo_byte = (IS < 8) ? IS : IS - 8, lo_sh = (IS < 8) ? 0 : 4;
         const int lo4 = (s12[lo_byte >> 2] >> (8 * (lo_byte & 3) + lo_sh)) & 0xF;
         const int hi2 = (s12[2] >> (8 * (IS & 3) + 2 * (IS >> 2))) & 3;
         return (lo4 | (hi2 << 4)) - 32;
     }
-    template <int N, int S, int NT>
-    __device__ __forceinline__ static void sblk(const uint32_t* w, const uint32_t* hm, const uint32_t* s12, ActPipe<NT, true>& P,
-                                IAcc<NT>& ia, int ntok) {
-        constexpr int PB = (2 * S < 4) ? 2 * S : 4;         // in-place bit of the 2-bit field
-        constexpr int WS = 2 * S - PB;                       // right shift of the qs word
-        constexpr int HS = (PB + 2) - (4 * N + S);           // left shift of the hmask word
-        uint32_t q[8];
+    template <int J>
+    __device__ __forceinline__ void run(uint32_t* q, int& sc, int& m) const {
+        constexpr int s = J >> 1, lh = J & 1;
+        constexpr int PB = (2 * s < 4) ? 2 * s : 4;  // in-place bit of the 2-bit field
+        constexpr int WS = 2 * s - PB;               // right shift of the qs word
+        constexpr int HSH = (PB + 2) - (4 * H + s);  // left shift of the hmask word
 #pragma unroll
-        for (int v = 0; v < 8; ++v)
-            q[v] = ((w[v] >> WS) & (0x03030303u << PB)) | (shl<HS>(hm[v]) & (0x04040404u << PB));
-#pragma unroll
-        for (int lh = 0; lh < 2; ++lh) {
-            constexpr int jb = 8 * N + 2 * S;
-            const int sj = (lh ? subscale<jb + 1>(s12) : subscale<jb>(s12));
-            const int scl = sj * (1 << (4 - PB));
-            P.step(jb + lh);
-#pragma unroll
-            for (int t = 0; t < NT; ++t) {
-                if (t < ntok) {
-                    int H, L;
-                    dot16<false>(q + 4 * lh, P.r[t][jb + lh], H, L);
-                    ia.hs[t] += scl * H;
-                    ia.ls[t] += scl * L;
-                    ia.ms[t] += sj * P.sx[t][jb + lh];
-                }
-            }
-        }
+        for (int v = 0; v < 4; ++v)
+            q[v] = ((w[4 * lh + v] >> WS) & (0x03030303u << PB)) | (shl<HSH>(hm[4 * lh + v]) & (0x04040404u << PB));
+        m = subscale<8 * H + J>();
+        sc = m * (1 << (4 - PB));
     }
-    template <int AL, int NT>
-    __device__ __forceinline__ static void process(const uint8_t* cg, int, const ActCG& X, float* acc, int ntok) {
-        uint32_t hd[1], s12[3], hm[8], w[8];
-        ld_words<1>(cg + 108, hd);
-        ld_words<3>(cg + 96, s12);
-        ld_words<8>(cg, hm);
-        ActPipe<NT, true> P(X, ntok);
-        IAcc<NT> ia;
-        ia.zero();
-        ld_words<8>(cg + 32, w);
-        sblk<0, 0, NT>(w, hm, s12, P, ia, ntok);
-        sblk<0, 1, NT>(w, hm, s12, P, ia, ntok);
-        sblk<0, 2, NT>(w, hm, s12, P, ia, ntok);
-        sblk<0, 3, NT>(w, hm, s12, P, ia, ntok);
-        ld_words<8>(cg + 64, w);
-        sblk<1, 0, NT>(w, hm, s12, P, ia, ntok);
-        sblk<1, 1, NT>(w, hm, s12, P, ia, ntok);
-        sblk<1, 2, NT>(w, hm, s12, P, ia, ntok);
-        sblk<1, 3, NT>(w, hm, s12, P, ia, ntok);
-        const float d = h2f_ref(hd[0] & 0xFFFFu);
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-            if (t < ntok) {
-                const float dot = fmaf(254.0f, static_cast<float>(ia.hs[t]), static_cast<float>(ia.ls[t]));
-                acc[t] = fmaf(act_u(X, t) * d, fmaf(0.0625f, dot, -4.0f * static_cast<float>(ia.ms[t])), acc[t]);
-            }
-        }
-    }
+    __device__ __forceinline__ float dscale() const { return h2f_ref(hd & 0xFFFFu) * 0.0625f; }
+    __device__ __forceinline__ float mscale() const { return h2f_ref(hd & 0xFFFFu) * 4.0f; }
 };
 
-// Q4_K {d, dmin, scales[12], qs[128]}: group g = 2c + nib covers nibble nib
-// of qs[32c + l]; high nibbles masked in place (x16), the low-nibble groups'
-// scales multiplied by 16: |HS| <= 8 * 63*16 * 32*15*127 < 5e8;
-// MS <= 8*63*32*32385.
-template <> struct Lane<F_Q4_K> {
-    static constexpr int CGB = 144, A = 16, PERM = 0;
-    template <int G, int NT>
-    __device__ __forceinline__ static void group(const uint32_t* hw, const uint32_t* w, ActPipe<NT, true>& P, IAcc<NT>& ia, int ntok) {
-        int sc, m;
-        k4sm<G>(hw, sc, m);
-        uint32_t q[8];
+// Q4_K {d, dmin, scales[12], qs[128]}: group G = 4H + J covers nibble G&1 of
+// qs[32(G>>1) + l]; high nibbles in place (x16), low-nibble scales x16:
+// |HS| <= 8 * 63*16 * 32*15*127 < 5e8; MS <= 8*63*32*32385.
+template <int H, int AL> struct RowQ4K {
+    static constexpr int RL = 32;
+    uint32_t hw[4];
+    const uint8_t* p;
+    __device__ __forceinline__ void load(const uint8_t* cg) {
+        ldw<4, AL>(cg, hw);
+        p = cg;
+    }
+    template <int J>
+    __device__ __forceinline__ void run(uint32_t* q, int& sc, int& m) const {
+        constexpr int G = 4 * H + J;
+        uint32_t w[8];
+        ldw<8, AL>(p + 16 + 32 * (G >> 1), w);
 #pragma unroll
         for (int v = 0; v < 8; ++v) q[v] = w[v] & ((G & 1) ? 0xF0F0F0F0u : 0x0F0F0F0Fu);
-        const int scl = (G & 1) ? sc : (sc << 4);
-        P.step(2 * G);
-        P.step(2 * G + 1);
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-            if (t < ntok) {
-                const int sx = P.sx[t][2 * G] + P.sx[t][2 * G + 1];
-                int h0, l0, h1, l1;
-                dot16<false>(q, P.r[t][2 * G], h0, l0);
-                dot16<false>(q + 4, P.r[t][2 * G + 1], h1, l1);
-                ia.hs[t] += scl * (h0 + h1);
-                ia.ls[t] += scl * (l0 + l1);
-                ia.ms[t] += m * sx;
-            }
-        }
+        int s6;
+        k4sm<G>(hw, s6, m);
+        sc = (G & 1) ? s6 : (s6 << 4);
     }
-    template <int AL, int NT>
-    __device__ __forceinline__ static void process(const uint8_t* cg, int, const ActCG& X, float* acc, int ntok) {
-        uint32_t hw[4];
-        ldw<4, AL>(cg, hw);
-        ActPipe<NT, true> P(X, ntok);
-        IAcc<NT> ia;
-        ia.zero();
-        uint32_t w[8];
-        ldw<8, AL>(cg + 16, w);
-        group<0, NT>(hw, w, P, ia, ntok);
-        group<1, NT>(hw, w, P, ia, ntok);
-        ldw<8, AL>(cg + 48, w);
-        group<2, NT>(hw, w, P, ia, ntok);
-        group<3, NT>(hw, w, P, ia, ntok);
-        ldw<8, AL>(cg + 80, w);
-        group<4, NT>(hw, w, P, ia, ntok);
-        group<5, NT>(hw, w, P, ia, ntok);
-        ldw<8, AL>(cg + 112, w);
-        group<6, NT>(hw, w, P, ia, ntok);
-        group<7, NT>(hw, w, P, ia, ntok);
-        const float d16 = h2f_ref(hw[0] & 0xFFFFu) * 0.0625f, mn = h2f_ref(hw[0] >> 16);
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-            if (t < ntok) {
-                const float dot = fmaf(254.0f, static_cast<float>(ia.hs[t]), static_cast<float>(ia.ls[t]));
-                acc[t] = fmaf(act_u(X, t), fmaf(d16, dot, -mn * static_cast<float>(ia.ms[t])), acc[t]);
-            }
-        }
-    }
+    __device__ __forceinline__ float dscale() const { return h2f_ref(hw[0] & 0xFFFFu) * 0.0625f; }
+    __device__ __forceinline__ float mscale() const { return h2f_ref(hw[0] >> 16); }
 };
 
-// Q5_K {d, dmin, scales[12], qh[32], qs[128]}: as Q4_K plus bit g of qh[l]
+// Q5_K {d, dmin, scales[12], qh[32], qs[128]}: as Q4_K plus bit G of qh[l]
 // as bit 4 of the code (no in-place factor): |HS| <= 8 * 63 * 32*31*127.
-template <> struct Lane<F_Q5_K> {
-    static constexpr int CGB = 176, A = 16, PERM = 0;
-    template <int G, int NT>
-    __device__ __forceinline__ static void group(const uint32_t* hw, const uint32_t* qh, const uint32_t* w, ActPipe<NT, true>& P,
-                                 IAcc<NT>& ia, int ntok) {
-        int sc, m;
-        k4sm<G>(hw, sc, m);
-        uint32_t q[8];
+template <int H, int AL> struct RowQ5K {
+    static constexpr int RL = 32;
+    uint32_t hw[4], qh[8];
+    const uint8_t* p;
+    __device__ __forceinline__ void load(const uint8_t* cg) {
+        ldw<4, AL>(cg, hw);
+        ldw<8, AL>(cg + 16, qh);
+        p = cg;
+    }
+    template <int J>
+    __device__ __forceinline__ void run(uint32_t* q, int& sc, int& m) const {
+        constexpr int G = 4 * H + J;
+        uint32_t w[8];
+        ldw<8, AL>(p + 48 + 32 * (G >> 1), w);
 #pragma unroll
         for (int v = 0; v < 8; ++v) {
             const uint32_t nib = (G & 1) ? (w[v] >> 4) : w[v];
             q[v] = (nib & 0x0F0F0F0Fu) | (shl<4 - G>(qh[v]) & 0x10101010u);
         }
-        P.step(2 * G);
-        P.step(2 * G + 1);
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-            if (t < ntok) {
-                const int sx = P.sx[t][2 * G] + P.sx[t][2 * G + 1];
-                int h0, l0, h1, l1;
-                dot16<false>(q, P.r[t][2 * G], h0, l0);
-                dot16<false>(q + 4, P.r[t][2 * G + 1], h1, l1);
-                ia.hs[t] += sc * (h0 + h1);
-                ia.ls[t] += sc * (l0 + l1);
-                ia.ms[t] += m * sx;
-            }
-        }
+        k4sm<G>(hw, sc, m);
     }
-    template <int AL, int NT>
-    __device__ __forceinline__ static void process(const uint8_t* cg, int, const ActCG& X, float* acc, int ntok) {
-        uint32_t hw[4], qh[8];
-        ldw<4, AL>(cg, hw);
-        ldw<8, AL>(cg + 16, qh);
-        ActPipe<NT, true> P(X, ntok);
-        IAcc<NT> ia;
-        ia.zero();
-        uint32_t w[8];
-        ldw<8, AL>(cg + 48, w);
-        group<0, NT>(hw, qh, w, P, ia, ntok);
-        group<1, NT>(hw, qh, w, P, ia, ntok);
-        ldw<8, AL>(cg + 80, w);
-        group<2, NT>(hw, qh, w, P, ia, ntok);
-        group<3, NT>(hw, qh, w, P, ia, ntok);
-        ldw<8, AL>(cg + 112, w);
-        group<4, NT>(hw, qh, w, P, ia, ntok);
-        group<5, NT>(hw, qh, w, P, ia, ntok);
-        ldw<8, AL>(cg + 144, w);
-        group<6, NT>(hw, qh, w, P, ia, ntok);
-        group<7, NT>(hw, qh, w, P, ia, ntok);
-        const float d = h2f_ref(hw[0] & 0xFFFFu), mn = h2f_ref(hw[0] >> 16);
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-            if (t < ntok) {
-                const float dot = fmaf(254.0f, static_cast<float>(ia.hs[t]), static_cast<float>(ia.ls[t]));
-                acc[t] = fmaf(act_u(X, t), fmaf(d, dot, -mn * static_cast<float>(ia.ms[t])), acc[t]);
-            }
-        }
-    }
+    __device__ __forceinline__ float dscale() const { return h2f_ref(hw[0] & 0xFFFFu); }
+    __device__ __forceinline__ float mscale() const { return h2f_ref(hw[0] >> 16); }
 };
 
-// Q6_K {ql[128], qh[64], scales[16], d}: sub-block j = 8n + 2t + lh; low 4
-// bits from ql (half t&1, nibble t>>1), high 2 bits from qh at shift 2t;
-// value = d * scale_j * (code - 32): |HS| <= 16 * 128 * 16*63*127 < 3e8,
-// |MS| = |sum_j scale_j * isx_j| <= 16*128*16*32385 < 1.1e9.
-template <> struct Lane<F_Q6_K> {
-    static constexpr int CGB = 210, A = 1, PERM = 0;
-    template <int N, int T, int NT>
-    __device__ __forceinline__ static void sblk(const uint32_t* qa, const uint32_t* qb, const uint32_t* qh, const uint32_t* sc,
-                                ActPipe<NT, true>& P, IAcc<NT>& ia, int ntok) {
-        uint32_t q[8];
+// Q6_K {ql[128], qh[64], scales[16], d}: half H; run J = 2T + lh: low 4 bits
+// from ql[64H + 32(T&1) + 16lh + l] (nibble T>>1), high 2 bits from
+// qh[32H + 16lh + l] at shift 2T; value = d * scale * (code - 32):
+// |HS| <= 16 * 128 * 16*63*127 < 3e8, |MS| <= 16*128*16*32385 < 1.1e9.
+template <int H, int AL> struct RowQ6K {
+    static constexpr int RL = 16;
+    uint32_t hd, sc2[2];
+    const uint8_t* p;
+    __device__ __forceinline__ void load(const uint8_t* cg) {
+        uint32_t h[1];
+        ld_words<1>(cg + 208, h);
+        hd = h[0];
+        ld_words<2>(cg + 192 + 8 * H, sc2);
+        p = cg;
+    }
+    template <int J>
+    __device__ __forceinline__ void run(uint32_t* q, int& sc, int& m) const {
+        constexpr int T = J >> 1, lh = J & 1;
+        uint32_t src[4], hb[4];
+        ld_words<4>(p + 64 * H + 32 * (T & 1) + 16 * lh, src);
+        ld_words<4>(p + 128 + 32 * H + 16 * lh, hb);
 #pragma unroll
-        for (int v = 0; v < 8; ++v) {
-            const uint32_t src = (T & 1) ? qb[v] : qa[v];
-            const uint32_t nib = (T & 2) ? (src >> 4) : src;
-            q[v] = (nib & 0x0F0F0F0Fu) | (shl<4 - 2 * T>(qh[v]) & 0x30303030u);
+        for (int v = 0; v < 4; ++v) {
+            const uint32_t nib = (T & 2) ? (src[v] >> 4) : src[v];
+            q[v] = (nib & 0x0F0F0F0Fu) | (shl<4 - 2 * T>(hb[v]) & 0x30303030u);
         }
+        sc = m = static_cast<int>(static_cast<int8_t>(bt<J>(sc2)));
+    }
+    __device__ __forceinline__ float dscale() const { return h2f_ref(hd & 0xFFFFu); }
+    __device__ __forceinline__ float mscale() const { return h2f_ref(hd & 0xFFFFu) * 32.0f; }
+};
+
+template <int F, int H, int AL> struct RowOf;
+template <int H, int AL> struct RowOf<F_Q2_K, H, AL> { using T = RowQ2K<H, AL>; };
+template <int H, int AL> struct RowOf<F_Q3_K, H, AL> { using T = RowQ3K<H, AL>; };
+template <int H, int AL> struct RowOf<F_Q4_K, H, AL> { using T = RowQ4K<H, AL>; };
+template <int H, int AL> struct RowOf<F_Q5_K, H, AL> { using T = RowQ5K<H, AL>; };
+template <int H, int AL> struct RowOf<F_Q6_K, H, AL> { using T = RowQ6K<H, AL>; };
+
+// Half CG of two rows (c0, c1) of a K-quant format: every activation run is
+// loaded once and dotted with both rows' codes; acc[i][t] += row i's part.
+template <int F, int H, int AL, int NT>
+__device__ __forceinline__ void kquant_half(const uint8_t* c0, const uint8_t* c1, const ActCG& X, int ntok,
+                                            float (*acc)[NT]) {
+    using R = typename RowOf<F, H, AL>::T;
+    constexpr int RL = R::RL, NW = RL / 4, NR = 128 / RL;
+    R r0, r1;
+    r0.load(c0);
+    r1.load(c1);
+    ActPipe<NT, true, H> P(X, ntok);
+    int hs[2][NT], ls[2][NT], ms[2][NT];
 #pragma unroll
-        for (int lh = 0; lh < 2; ++lh) {
-            constexpr int jb = 8 * N + 2 * T;
-            const int sj = lh ? static_cast<int>(static_cast<int8_t>(bt<jb + 1>(sc)))
-                              : static_cast<int>(static_cast<int8_t>(bt<jb>(sc)));
-            P.step(jb + lh);
+    for (int t = 0; t < NT; ++t) hs[0][t] = hs[1][t] = ls[0][t] = ls[1][t] = ms[0][t] = ms[1][t] = 0;
+    static_for<NR>([&](auto Jc) {
+        constexpr int J = decltype(Jc)::value, j0 = J * (RL / 16);
+        uint32_t qa[NW], qb[NW];
+        int sa, ma, sb, mb;
+        r0.template run<J>(qa, sa, ma);
+        r1.template run<J>(qb, sb, mb);
+        P.step(j0);
+        if constexpr (RL == 32) P.step(j0 + 1);
 #pragma unroll
-            for (int t = 0; t < NT; ++t) {
-                if (t < ntok) {
-                    int H, L;
-                    dot16<false>(q + 4 * lh, P.r[t][jb + lh], H, L);
-                    ia.hs[t] += sj * H;
-                    ia.ls[t] += sj * L;
-                    ia.ms[t] += sj * P.sx[t][jb + lh];
+        for (int t = 0; t < NT; ++t) {  // padded tokens compute on the last token's data; never written
+            int ha, la, hb, lb, sx = P.sx[t][j0];
+            dot16<false>(qa, P.r[t][j0], ha, la);
+            dot16<false>(qb, P.r[t][j0], hb, lb);
+            if constexpr (RL == 32) {
+                int ha2, la2, hb2, lb2;
+                dot16<false>(qa + 4, P.r[t][j0 + 1], ha2, la2);
+                dot16<false>(qb + 4, P.r[t][j0 + 1], hb2, lb2);
+                ha += ha2; la += la2; hb += hb2; lb += lb2;
+                sx += P.sx[t][j0 + 1];
+            }
+            hs[0][t] += sa * ha; ls[0][t] += sa * la; ms[0][t] += ma * sx;
+            hs[1][t] += sb * hb; ls[1][t] += sb * lb; ms[1][t] += mb * sx;
+        }
+    });
+    const float d0 = r0.dscale(), m0 = r0.mscale(), d1 = r1.dscale(), m1 = r1.mscale();
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+        const float u = act_u(X, t);
+        const float dot0 = fmaf(254.0f, static_cast<float>(hs[0][t]), static_cast<float>(ls[0][t]));
+        const float dot1 = fmaf(254.0f, static_cast<float>(hs[1][t]), static_cast<float>(ls[1][t]));
+        acc[0][t] = fmaf(u, fmaf(d0, dot0, -m0 * static_cast<float>(ms[0][t])), acc[0][t]);
+        acc[1][t] = fmaf(u, fmaf(d1, dot1, -m1 * static_cast<float>(ms[1][t])), acc[1][t]);
+    }
+}
+
+// ---- Q8_0 / Q4_0 ------------------------------------------------------------
+// A CG is 8 blocks of 32 with one fp16 scale each; half H = blocks 4H..4H+3.
+// Q8_0 {u16 d; i8 qs[32]}: S = 254*H + L <= 32*127*32385 per block.
+// Q4_0 {u16 d; u8 qs[16]}: low nibbles = even elements, high nibbles (kept in
+// place, x16) = odd elements; the activation prep orders each 32-block as
+// evens then odds.  S16 = 16*(254*H + L) - 128*isx = 16*sum (code - 8)*X,
+// |S16| < 4e8.  Blocks at or past nblk_valid (a row's last, partial CG) are
+// skipped.
+template <int F, int H, int NT>
+__device__ __forceinline__ void block32_half(const uint8_t* c0, const uint8_t* c1, int nblk_valid, const ActCG& X,
+                                             int ntok, float (*acc)[NT]) {
+    constexpr bool Q8 = (F == F_Q8_0);
+    constexpr int BB = Q8 ? 34 : 18;
+    ActPipe<NT, !Q8, H> P(X, ntok);
+    float accf[2][NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) accf[0][t] = accf[1][t] = 0.0f;
+    static_for<4>([&](auto Bc) {
+        constexpr int BL = decltype(Bc)::value, B = 4 * H + BL;
+        if (B < nblk_valid) {
+            uint32_t h0[1], h1[1];
+            ld_words<1>(c0 + BB * B, h0);
+            ld_words<1>(c1 + BB * B, h1);
+            const float da = h2f_ref(h0[0] & 0xFFFFu) * (Q8 ? 1.0f : 0.0625f);
+            const float db = h2f_ref(h1[0] & 0xFFFFu) * (Q8 ? 1.0f : 0.0625f);
+            uint32_t qa[8], qb[8];
+            if constexpr (Q8) {
+                ld_words<8>(c0 + BB * B + 2, qa);
+                ld_words<8>(c1 + BB * B + 2, qb);
+            } else {
+                uint32_t wa[4], wb[4];
+                ld_words<4>(c0 + BB * B + 2, wa);
+                ld_words<4>(c1 + BB * B + 2, wb);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    qa[j] = wa[j] & 0x0F0F0F0Fu;
+                    qa[4 + j] = wa[j] & 0xF0F0F0F0u;
+                    qb[j] = wb[j] & 0x0F0F0F0Fu;
+                    qb[4 + j] = wb[j] & 0xF0F0F0F0u;
                 }
             }
-        }
-    }
-    template <int AL, int NT>
-    __device__ __forceinline__ static void process(const uint8_t* cg, int, const ActCG& X, float* acc, int ntok) {
-        uint32_t hd[1], sc[4];
-        ld_words<1>(cg + 208, hd);
-        ld_words<4>(cg + 192, sc);
-        ActPipe<NT, true> P(X, ntok);
-        IAcc<NT> ia;
-        ia.zero();
-        {
-            uint32_t qa[8], qb[8], qh[8];
-            ld_words<8>(cg, qa);
-            ld_words<8>(cg + 32, qb);
-            ld_words<8>(cg + 128, qh);
-            sblk<0, 0, NT>(qa, qb, qh, sc, P, ia, ntok);
-            sblk<0, 1, NT>(qa, qb, qh, sc, P, ia, ntok);
-            sblk<0, 2, NT>(qa, qb, qh, sc, P, ia, ntok);
-            sblk<0, 3, NT>(qa, qb, qh, sc, P, ia, ntok);
-        }
-        {
-            uint32_t qa[8], qb[8], qh[8];
-            ld_words<8>(cg + 64, qa);
-            ld_words<8>(cg + 96, qb);
-            ld_words<8>(cg + 160, qh);
-            sblk<1, 0, NT>(qa, qb, qh, sc, P, ia, ntok);
-            sblk<1, 1, NT>(qa, qb, qh, sc, P, ia, ntok);
-            sblk<1, 2, NT>(qa, qb, qh, sc, P, ia, ntok);
-            sblk<1, 3, NT>(qa, qb, qh, sc, P, ia, ntok);
-        }
-        const float d = h2f_ref(hd[0] & 0xFFFFu);
+            P.step(2 * BL);
+            P.step(2 * BL + 1);
 #pragma unroll
-        for (int t = 0; t < NT; ++t) {
-            if (t < ntok) {
-                const float dot = fmaf(254.0f, static_cast<float>(ia.hs[t]), static_cast<float>(ia.ls[t]));
-                acc[t] = fmaf(act_u(X, t) * d, fmaf(-32.0f, static_cast<float>(ia.ms[t]), dot), acc[t]);
+            for (int t = 0; t < NT; ++t) {  // padded tokens compute on the last token's data; never written
+                int ha0, la0, ha1, la1, hb0, lb0, hb1, lb1;
+                dot16<Q8>(qa, P.r[t][2 * BL], ha0, la0);
+                dot16<Q8>(qa + 4, P.r[t][2 * BL + 1], ha1, la1);
+                dot16<Q8>(qb, P.r[t][2 * BL], hb0, lb0);
+                dot16<Q8>(qb + 4, P.r[t][2 * BL + 1], hb1, lb1);
+                int Sa, Sb;
+                if constexpr (Q8) {
+                    Sa = (ha0 + ha1) * 254 + (la0 + la1);
+                    Sb = (hb0 + hb1) * 254 + (lb0 + lb1);
+                } else {
+                    const int sx = P.sx[t][2 * BL] + P.sx[t][2 * BL + 1];
+                    Sa = (16 * ha0 + ha1) * 254 + (16 * la0 + la1) - 128 * sx;
+                    Sb = (16 * hb0 + hb1) * 254 + (16 * lb0 + lb1) - 128 * sx;
+                }
+                accf[0][t] = fmaf(da, static_cast<float>(Sa), accf[0][t]);
+                accf[1][t] = fmaf(db, static_cast<float>(Sb), accf[1][t]);
             }
         }
+    });
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+        const float u = act_u(X, t);
+        acc[0][t] = fmaf(u, accf[0][t], acc[0][t]);
+        acc[1][t] = fmaf(u, accf[1][t], acc[1][t]);
+    }
+}
+
+// Per-format constants and the half-CG entry point: CGB = packed bytes of a
+// CG (256 elements), A = natural alignment of a row's CGs, PERM = activation
+// order within 32-blocks (Q4_0: evens then odds).
+template <int F> struct Lane {
+    static constexpr int CGB = (F == F_Q8_0) ? 8 * 34 : (F == F_Q4_0) ? 8 * 18 : Traits<F>::BB;
+    static constexpr int A = (F == F_Q2_K) ? 4 : (F == F_Q4_K || F == F_Q5_K) ? 16 : 1;
+    static constexpr int PERM = (F == F_Q4_0) ? 1 : 0;
+    template <int H, int AL, int NT>
+    __device__ __forceinline__ static void half(const uint8_t* c0, const uint8_t* c1, int nblk_valid, const ActCG& X,
+                                                int ntok, float (*acc)[NT]) {
+        if constexpr (F == F_Q8_0 || F == F_Q4_0) block32_half<F, H, NT>(c0, c1, nblk_valid, X, ntok, acc);
+        else kquant_half<F, H, AL, NT>(c0, c1, X, ntok, acc);
     }
 };
 
@@ -714,12 +593,11 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
 
     if (warp == kConsumerWarps) {
         // ---------------- producer warp: lane r copies row r of each stage ----
-        int it = 0;
+        int s = 0, pass = 0;  // ring slot and how many times the ring was filled
         for (int64_t u = blockIdx.x; u < a.units; u += gridDim.x) {
-            for (int ks = 0; ks < a.nks; ++ks, ++it) {
-                const int s = it % a.nstages;
-                if (it >= a.nstages) {
-                    if (!wait_or_abort(&empty[s], ((it / a.nstages) - 1) & 1, abort_flag)) {
+            for (int ks = 0; ks < a.nks; ++ks) {
+                if (pass > 0) {
+                    if (!wait_or_abort(&empty[s], (pass - 1) & 1, abort_flag)) {
                         if (lane == 0) {
                             *abort_flag = 1;
                             atomicExch(a.err, 1);
@@ -756,57 +634,81 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
                 }
                 __syncwarp();
                 if (bulk) bulk_g2s(st + lane * a.rs, reinterpret_cast<const void*>(lo), my_tx, &full[s]);
+                if (++s == a.nstages) {
+                    s = 0;
+                    ++pass;
+                }
             }
         }
         return;
     }
 
     // ---------------- consumer warps ----------------
-    const int r = lane & 15, cgl = 2 * warp + (lane >> 4);  // row in unit, CG in stage
-    float acc[NT];
+    // Warp w decodes half h = w/4 of the stage's CGs 4(w%4)..4(w%4)+3; lane l
+    // takes CG 4(w%4) + l/8 for rows l%8 and l%8 + 8 of the unit, so every
+    // activation run it loads serves two rows.
+    const int h = warp >> 2;
+    const int cgl = 4 * (warp & 3) + (lane >> 3);  // CG slot in the stage
+    const int pr = lane & 7;                        // rows pr and pr + 8 of the unit
+    float acc[2][NT];
 #pragma unroll
-    for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
-    int it = 0, unit_par = 0;
+    for (int t = 0; t < NT; ++t) acc[0][t] = acc[1][t] = 0.0f;
+    int s = 0, unit_par = 0;
+    uint32_t phase = 0;
     for (int64_t u = blockIdx.x; u < a.units; u += gridDim.x, unit_par ^= 1) {
-        const int64_t row = u * kUnitRows + r;
-        const bool row_ok = row < a.rows;
-        for (int ks = 0; ks < a.nks; ++ks, ++it) {
-            const int s = it % a.nstages;
-            if (!wait_or_abort(&full[s], (it / a.nstages) & 1, abort_flag)) {
+        const int64_t row0 = u * kUnitRows + pr, row1 = row0 + 8;
+        const bool ok0 = row0 < a.rows, ok1 = row1 < a.rows;
+        for (int ks = 0; ks < a.nks; ++ks) {
+            if (!wait_or_abort(&full[s], phase, abort_flag)) {
                 if (lane == 0) {
                     *abort_flag = 1;
                     atomicExch(a.err, 1);
                 }
             }
             const int cg = ks * kStageCG + cgl;
-            if (row_ok && cg < a.ncg && !*abort_flag) {
-                const uintptr_t ga = wbase + static_cast<uintptr_t>(row * a.rb + static_cast<int64_t>(ks) * step_bytes);
-                const uint8_t* cgp = stages + s * a.stage_bytes + r * a.rs + (ga & 15) + cgl * L::CGB;
+            if (ok0 && cg < a.ncg && !*abort_flag) {
+                const int64_t off = static_cast<int64_t>(ks) * step_bytes;
+                const uint8_t* st = stages + s * a.stage_bytes + cgl * L::CGB;
+                const uint8_t* c0 = st + pr * a.rs + ((wbase + static_cast<uintptr_t>(row0 * a.rb + off)) & 15);
+                // a row past the end decodes row0 again; its sum is never written
+                const uint8_t* c1 =
+                    ok1 ? st + (pr + 8) * a.rs + ((wbase + static_cast<uintptr_t>(row1 * a.rb + off)) & 15) : c0;
                 const ActCG X{a.act + static_cast<int64_t>(cg) * a.act_cg_stride};
-                L::template process<AL, NT>(cgp, a.nblk_row - cg * 8, X, acc, a.ntok);
+                const int nbv = a.nblk_row - cg * 8;
+                if (h == 0) L::template half<0, AL, NT>(c0, c1, nbv, X, a.ntok, acc);
+                else L::template half<1, AL, NT>(c0, c1, nbv, X, a.ntok, acc);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
+            if (++s == a.nstages) {
+                s = 0;
+                phase ^= 1;
+            }
         }
-        // combine the two column groups of each lane pair, then the warps
+        // combine the four CG slots of each warp, then the warps
         float* rp = red + unit_par * (kConsumerWarps * kUnitRows * NT);
 #pragma unroll
-        for (int t = 0; t < NT; ++t) {
-            float v = acc[t];
-            v += __shfl_xor_sync(0xffffffffu, v, 16);
-            if (lane < 16) rp[(warp * kUnitRows + lane) * NT + t] = v;
-            acc[t] = 0.0f;
+        for (int i = 0; i < 2; ++i) {
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                float v = acc[i][t];
+                v += __shfl_xor_sync(0xffffffffu, v, 8);
+                v += __shfl_xor_sync(0xffffffffu, v, 16);
+                if (lane < 8) rp[(warp * kUnitRows + pr + 8 * i) * NT + t] = v;
+                acc[i][t] = 0.0f;
+            }
         }
         asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
-        if (warp == 0 && lane < 16 && row_ok) {
+        const int64_t orow = u * kUnitRows + lane;
+        if (warp == 0 && lane < 16 && orow < a.rows) {
 #pragma unroll
             for (int t = 0; t < NT; ++t) {
                 if (t < a.ntok) {
                     float v = 0.0f;
 #pragma unroll
                     for (int w2 = 0; w2 < kConsumerWarps; ++w2) v += rp[(w2 * kUnitRows + lane) * NT + t];
-                    if (a.out_tokmajor) a.out[t * a.out_ld + row] = v;
-                    else a.out[row * a.out_ld + t] = v;
+                    if (a.out_tokmajor) a.out[t * a.out_ld + orow] = v;
+                    else a.out[orow * a.out_ld + t] = v;
                 }
             }
         }
