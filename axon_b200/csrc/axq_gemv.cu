@@ -497,6 +497,10 @@ template <int F> struct Lane {
 __global__ void act_prep_kernel(const float* __restrict__ x, int64_t K, int64_t ntok, int x_tokmajor, int perm,
                                 int64_t nch, uint8_t* __restrict__ rec, int* __restrict__ err) {
     const int lane = threadIdx.x & 31;
+    // x may come from the previous kernel; only after it has finished may the
+    // matmul kernel (launched early) start streaming weights.
+    pdl_wait();
+    pdl_launch_dependents();
     if (blockIdx.x == 0 && threadIdx.x == 0) *err = 0;  // status word of this call
     const int64_t wid = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (wid >= nch * ntok) return;
@@ -577,6 +581,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
     uint8_t* stages = smem + kHeaderBytes + ((2 * kConsumerWarps * kUnitRows * NT * 4 + 127) / 128) * 128;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // The weights were complete before the activation prep started; only the
+    // consumers read its records, after pdl_wait below.
+    pdl_launch_dependents();
     if (tid == 0) {
         for (int s = 0; s < kMaxStages; ++s) {
             mbar_init(&full[s], 1);
@@ -647,6 +654,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
     // Warp w decodes half h = w/4 of the stage's CGs 4(w%4)..4(w%4)+3; lane l
     // takes CG 4(w%4) + l/8 for rows l%8 and l%8 + 8 of the unit, so every
     // activation run it loads serves two rows.
+    pdl_wait();  // activation records of this call are complete
     const int h = warp >> 2;
     const int cgl = 4 * (warp & 3) + (lane >> 3);  // CG slot in the stage
     const int pr = lane & 7;                        // rows pr and pr + 8 of the unit
@@ -754,8 +762,8 @@ cudaError_t launch_nt(const GemvPlan& p, const GemvArgs& a, cudaStream_t s) {
         if (e != cudaSuccess) return e;
         configured[dev] = p.smem;
     }
-    kern<<<p.grid, kThreads, p.smem, s>>>(a);
-    return cudaGetLastError();
+    cudaError_t e = launch_pdl(kern, dim3(p.grid), dim3(kThreads), p.smem, s, a);
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 template <int F, int AL>
@@ -781,9 +789,9 @@ cudaError_t launch_gemv(const void* w, const float* x, float* out, int64_t M, in
     {
         const int64_t warps = nch * N;
         const int64_t grid = (warps + 7) / 8;
-        act_prep_kernel<<<static_cast<unsigned>(grid), 256, 0, s>>>(x, K, N, (flags & AXQ_FLAG_B_TOKMAJOR) ? 1 : 0,
-                                                                    L::PERM, nch, rec, err);
-        cudaError_t e = cudaGetLastError();
+        cudaError_t e = launch_pdl(act_prep_kernel, dim3(static_cast<unsigned>(grid)), dim3(256), 0, s, x, K, N,
+                                   (flags & AXQ_FLAG_B_TOKMAJOR) ? 1 : 0, static_cast<int>(L::PERM), nch, rec, err);
+        if (e == cudaSuccess) e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
     GemvArgs a{};

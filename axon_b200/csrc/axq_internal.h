@@ -5,6 +5,7 @@
 #include <cstddef>
 #include <cstdint>
 #include <string>
+#include <utility>
 #include <cuda_runtime.h>
 
 #include "../../include/axq.h"
@@ -31,6 +32,25 @@ cudaError_t gemv_dispatch(int fmt, const void* w, const float* x, float* out, in
 size_t gemm_workspace_bytes(int fmt, int64_t M, int64_t K, int64_t N);
 cudaError_t gemm_dispatch(int fmt, const void* w, const float* x, float* out, int64_t M, int64_t K, int64_t N, int flags,
                           void* ws, size_t ws_bytes, int* err, cudaStream_t s);
+
+// Launches `kernel` on `s` with programmatic stream serialization: it may
+// be scheduled while the previous kernel of the stream is still running and
+// must call griddepcontrol.wait (pdl_wait) before touching memory that
+// kernel writes.
+template <typename... Params, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Largest N served by the GEMV kernel; larger batches use the GEMM.
 constexpr int64_t kGemvMaxN = 8;

@@ -92,6 +92,14 @@ __device__ __forceinline__ void ld_words(const uint8_t* p, uint32_t* out) {
     for (int i = 0; i < N; ++i) out[i] = __funnelshift_r(w[i], w[i + 1], sh);
 }
 
+// Programmatic dependent launch (sm_90+).  wait: block until the
+// preceding kernel of the stream has completed and its writes are visible
+// (returns at once when this grid was launched without the attribute).
+// launch_dependents: allow the next kernel, if launched with the attribute,
+// to be scheduled before this grid completes.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ uint32_t byte_of(const uint32_t* w, int i) { return (w[i >> 2] >> (8 * (i & 3))) & 0xFFu; }
 
 }  // namespace axq
