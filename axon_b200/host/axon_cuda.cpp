@@ -1,0 +1,412 @@
+// Implementation of the host-side mirror (axon_cuda.h) over libaxq.so.
+#include "axon_cuda.h"
+
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+namespace axon::cuda {
+namespace {
+
+int fmt_code(QuantFormat f) { return static_cast<int>(f); }  // same ordinals as axq_format
+
+Error last_error(const std::string& where) {
+    const char* m = axq_last_error();
+    return Error{where + ": " + ((m && *m) ? m : "unknown error")};
+}
+
+thread_local axq_stream_t t_stream = nullptr;
+
+// One growing device scratch per device for axq_matmul's workspace (the
+// reference's kernels get no allocator through KernelContext, so the
+// backend owns it).  Grows under a lock; the old buffer is freed by
+// cudaFree, which waits for the work already issued on the device.
+struct Scratch {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+};
+std::mutex g_scratch_mu;
+std::unordered_map<int, Scratch> g_scratch;
+
+Expected<void*> scratch(int device, size_t need) {
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    Scratch& s = g_scratch[device];
+    if (s.bytes < need) {
+        if (s.ptr) cudaFree(s.ptr);
+        s.ptr = nullptr;
+        s.bytes = 0;
+        size_t want = need + need / 2;
+        if (cudaMalloc(&s.ptr, want) != cudaSuccess) {
+            cudaGetLastError();
+            return Error{"matmul: cannot allocate " + std::to_string(want) + " bytes of device workspace"};
+        }
+        s.bytes = want;
+    }
+    return s.ptr;
+}
+
+constexpr QuantFormat format_of(OpId op) {
+    switch (op) {
+        case OpId::MatMulQ8_0: return QuantFormat::Q8_0;
+        case OpId::MatMulQ4_0: return QuantFormat::Q4_0;
+        case OpId::MatMulQ2_K: return QuantFormat::Q2_K;
+        case OpId::MatMulQ3_K: return QuantFormat::Q3_K;
+        case OpId::MatMulQ4_K: return QuantFormat::Q4_K;
+        case OpId::MatMulQ5_K: return QuantFormat::Q5_K;
+        case OpId::MatMulQ6_K: return QuantFormat::Q6_K;
+        default: return QuantFormat::None;
+    }
+}
+
+const char* format_name(QuantFormat f) {
+    switch (f) {
+        case QuantFormat::Q8_0: return "Q8_0";
+        case QuantFormat::Q6_K: return "Q6_K";
+        case QuantFormat::Q5_K: return "Q5_K";
+        case QuantFormat::Q4_0: return "Q4_0";
+        case QuantFormat::Q4_K: return "Q4_K";
+        case QuantFormat::Q3_K: return "Q3_K";
+        case QuantFormat::Q2_K: return "Q2_K";
+        default: return "None";
+    }
+}
+
+Expected<void> check_same_device(const DeviceTensor& a, const DeviceTensor& b, const char* fn) {
+    if (a.device_index() != b.device_index())
+        return Error{std::string(fn) + ": tensors are on different devices"};
+    return {};
+}
+
+// matmul kernel body shared by every format: out[M,N] = A_q[M,K] . B[K,N].
+template <OpId OP>
+Expected<void> matmul_kernel(KernelContext& ctx) {
+    constexpr QuantFormat F = format_of(OP);
+    const char* fn = "matmul";
+    if (ctx.outputs.size() < 1 || ctx.inputs.size() < 2) return Error{std::string(fn) + ": expects 1 output, 2 inputs"};
+    DeviceTensor& out = ctx.outputs[0];
+    const DeviceTensor& a = ctx.inputs[0];
+    const DeviceTensor& b = ctx.inputs[1];
+    if (a.quant().format != F)
+        return Error{std::string(fn) + ": A is " + format_name(a.quant().format) + ", kernel is " + format_name(F)};
+    if (b.is_quantized() || b.dtype() != DType::Float32 || out.is_quantized() || out.dtype() != DType::Float32)
+        return Error{std::string(fn) + ": B and out must be fp32"};
+    const int64_t M = a.rows(), K = a.cols(), N = b.cols();
+    if (b.rows() != K) return Error{std::string(fn) + ": inner dimensions differ"};
+    if (out.rows() != M || out.cols() != N) return Error{std::string(fn) + ": output shape mismatch"};
+    if (auto e = check_same_device(a, b, fn); !e) return e;
+    if (auto e = check_same_device(a, out, fn); !e) return e;
+    if (M == 0 || N == 0) return {};
+    const size_t need = axq_matmul_workspace_size(fmt_code(F), M, K, N);
+    auto ws = scratch(a.device_index(), need);
+    if (!ws) return ws.error();
+    const int st = axq_matmul(fmt_code(F), a.data(), static_cast<const float*>(b.data()), static_cast<float*>(out.data()),
+                              M, K, N, 0u, ws.value(), need, t_stream);
+    if (st != AXQ_OK) return last_error(fn);
+    return {};
+}
+
+Expected<void> quantize_kernel(KernelContext& ctx) {
+    if (ctx.outputs.size() < 1 || ctx.inputs.size() < 1) return Error{"quantize: expects 1 output, 1 input"};
+    DeviceTensor& dst = ctx.outputs[0];
+    const DeviceTensor& src = ctx.inputs[0];
+    if (src.is_quantized() || src.dtype() != DType::Float32) return Error{"quantize: source must be fp32"};
+    if (!dst.is_quantized()) return Error{"quantize: destination has no quantization format"};
+    if (dst.rows() != src.rows() || dst.cols() != src.cols()) return Error{"quantize: shape mismatch"};
+    if (dst.size_bytes() < quantized_size_2d(src.rows(), src.cols(), dst.quant().format))
+        return Error{"quantize: destination too small"};
+    if (auto e = check_same_device(dst, src, "quantize"); !e) return e;
+    const int st = axq_quantize(fmt_code(dst.quant().format), static_cast<const float*>(src.data()), dst.data(),
+                                src.rows(), src.cols(), t_stream);
+    if (st != AXQ_OK) return last_error("quantize");
+    return {};
+}
+
+Expected<void> dequantize_kernel(KernelContext& ctx) {
+    if (ctx.outputs.size() < 1 || ctx.inputs.size() < 1) return Error{"dequantize: expects 1 output, 1 input"};
+    DeviceTensor& dst = ctx.outputs[0];
+    const DeviceTensor& src = ctx.inputs[0];
+    if (!src.is_quantized()) return Error{"dequantize: source is not quantized"};
+    if (dst.is_quantized() || dst.dtype() != DType::Float32) return Error{"dequantize: destination must be fp32"};
+    if (dst.rows() != src.rows() || dst.cols() != src.cols()) return Error{"dequantize: shape mismatch"};
+    if (auto e = check_same_device(dst, src, "dequantize"); !e) return e;
+    const int st = axq_dequantize(fmt_code(src.quant().format), src.data(), static_cast<float*>(dst.data()),
+                                  src.rows(), src.cols(), t_stream);
+    if (st != AXQ_OK) return last_error("dequantize");
+    return {};
+}
+
+KernelKey cuda_key(OpId op) { return KernelKey{op, Device::CUDA, DType::Float32, Provider::CUDA}; }
+
+bool name_to_op(const std::string& name, OpId& op) {
+    static const std::unordered_map<std::string, OpId> names = {
+        {"matmul_q8_0", OpId::MatMulQ8_0}, {"matmul_q4_0", OpId::MatMulQ4_0}, {"matmul_q2_K", OpId::MatMulQ2_K},
+        {"matmul_q3_K", OpId::MatMulQ3_K}, {"matmul_q4_K", OpId::MatMulQ4_K}, {"matmul_q5_K", OpId::MatMulQ5_K},
+        {"matmul_q6_K", OpId::MatMulQ6_K}, {"quantize", OpId::Quantize},     {"dequantize", OpId::Dequantize},
+        {"matmul", OpId::MatMul},
+    };
+    auto it = names.find(name);
+    if (it == names.end()) return false;
+    op = it->second;
+    return true;
+}
+
+Expected<void> run_named(const std::string& name, DeviceTensor& out, const DeviceTensor& a, const DeviceTensor& b) {
+    register_cuda_kernels();
+    KernelFn fn = KernelRegistry::instance().dispatch(name);
+    if (!fn) return Error{"matmul: no CUDA kernel registered for " + name};
+    DeviceTensor outs[1];
+    // KernelContext holds spans of tensors; pass views (the caller keeps ownership).
+    outs[0] = DeviceTensor::view(out.data(), out.rows(), out.cols(), out.dtype(), out.quant().format, out.device_index());
+    const DeviceTensor ins[2] = {
+        DeviceTensor::view(const_cast<void*>(a.data()), a.rows(), a.cols(), a.dtype(), a.quant().format,
+                           a.device_index()),
+        DeviceTensor::view(const_cast<void*>(b.data()), b.rows(), b.cols(), b.dtype(), b.quant().format,
+                           b.device_index())};
+    KernelContext ctx{outs, ins, nullptr};
+    return fn(ctx);
+}
+
+}  // namespace
+
+// ---- blocks ---------------------------------------------------------------
+
+int block_elems(QuantFormat f) {
+    switch (f) {
+        case QuantFormat::Q8_0:
+        case QuantFormat::Q4_0: return 32;
+        case QuantFormat::None: return 0;
+        default: return 256;
+    }
+}
+
+size_t block_bytes(QuantFormat f) {
+    switch (f) {
+        case QuantFormat::Q8_0: return 34;
+        case QuantFormat::Q4_0: return 18;
+        case QuantFormat::Q2_K: return 84;
+        case QuantFormat::Q3_K: return 110;
+        case QuantFormat::Q4_K: return 144;
+        case QuantFormat::Q5_K: return 176;
+        case QuantFormat::Q6_K: return 210;
+        default: return 0;
+    }
+}
+
+size_t quantized_size(size_t num_elements, QuantFormat format) {
+    return axq_quantized_size(num_elements, fmt_code(format));
+}
+
+size_t quantized_size_2d(int64_t M, int64_t K, QuantFormat format) {
+    return axq_quantized_size_2d(M, K, fmt_code(format));
+}
+
+// ---- DeviceTensor -----------------------------------------------------------
+
+DeviceTensor::~DeviceTensor() {
+    if (owned_ && data_) cudaFree(data_);
+}
+
+DeviceTensor::DeviceTensor(DeviceTensor&& o) noexcept { *this = std::move(o); }
+
+DeviceTensor& DeviceTensor::operator=(DeviceTensor&& o) noexcept {
+    if (this != &o) {
+        if (owned_ && data_) cudaFree(data_);
+        data_ = o.data_;
+        rows_ = o.rows_;
+        cols_ = o.cols_;
+        dtype_ = o.dtype_;
+        quant_ = o.quant_;
+        bytes_ = o.bytes_;
+        device_ = o.device_;
+        owned_ = o.owned_;
+        o.data_ = nullptr;
+        o.owned_ = false;
+    }
+    return *this;
+}
+
+Expected<DeviceTensor> DeviceTensor::empty(int64_t rows, int64_t cols, QuantFormat quant) {
+    if (rows < 0 || cols < 0) return Error{"empty: negative shape"};
+    DeviceTensor t;
+    t.rows_ = rows;
+    t.cols_ = cols;
+    t.quant_ = QuantizationDescriptor{quant, block_elems(quant)};
+    t.dtype_ = (quant == QuantFormat::None) ? DType::Float32 : DType::UInt8;
+    t.bytes_ = (quant == QuantFormat::None) ? static_cast<size_t>(rows * cols) * 4 : quantized_size_2d(rows, cols, quant);
+    cudaGetDevice(&t.device_);
+    if (t.bytes_ > 0) {
+        if (cudaMalloc(&t.data_, t.bytes_) != cudaSuccess) {
+            cudaGetLastError();
+            return Error{"empty: cudaMalloc of " + std::to_string(t.bytes_) + " bytes failed"};
+        }
+        t.owned_ = true;
+    }
+    return t;
+}
+
+Expected<DeviceTensor> DeviceTensor::from_host(const float* host, int64_t rows, int64_t cols) {
+    auto t = empty(rows, cols, QuantFormat::None);
+    if (!t) return t.error();
+    if (t.value().bytes_ &&
+        cudaMemcpy(t.value().data_, host, t.value().bytes_, cudaMemcpyHostToDevice) != cudaSuccess) {
+        cudaGetLastError();
+        return Error{"from_host: copy failed"};
+    }
+    return std::move(t.value());
+}
+
+DeviceTensor DeviceTensor::view(void* data, int64_t rows, int64_t cols, DType dtype, QuantFormat quant, int device) {
+    DeviceTensor t;
+    t.data_ = data;
+    t.rows_ = rows;
+    t.cols_ = cols;
+    t.dtype_ = dtype;
+    t.quant_ = QuantizationDescriptor{quant, block_elems(quant)};
+    t.bytes_ = (quant == QuantFormat::None) ? static_cast<size_t>(rows * cols) * 4 : quantized_size_2d(rows, cols, quant);
+    t.device_ = device;
+    t.owned_ = false;
+    return t;
+}
+
+Expected<void> DeviceTensor::to_host(void* host, size_t nbytes) const {
+    if (nbytes < bytes_) return Error{"to_host: host buffer too small"};
+    if (bytes_ == 0) return {};
+    if (cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(t_stream)) != cudaSuccess ||
+        cudaMemcpy(host, data_, bytes_, cudaMemcpyDeviceToHost) != cudaSuccess) {
+        const char* m = cudaGetErrorString(cudaGetLastError());
+        return Error{std::string("to_host: ") + m};
+    }
+    return {};
+}
+
+// ---- registry ---------------------------------------------------------------
+
+size_t KernelKeyHash::operator()(const KernelKey& k) const noexcept {
+    const uint64_t v = static_cast<uint64_t>(k.op) | (static_cast<uint64_t>(k.device) << 16) |
+                       (static_cast<uint64_t>(k.dtype) << 24) | (static_cast<uint64_t>(k.provider) << 32);
+    return std::hash<uint64_t>{}(v);
+}
+
+KernelRegistry& KernelRegistry::instance() {
+    static KernelRegistry reg;
+    return reg;
+}
+
+void KernelRegistry::register_kernel(KernelKey key, KernelFn fn) { registry_[key] = fn; }
+
+KernelFn KernelRegistry::lookup(KernelKey key) const {
+    auto it = registry_.find(key);
+    return it == registry_.end() ? nullptr : it->second;
+}
+
+KernelFn KernelRegistry::dispatch(KernelKey key) const { return lookup(key); }
+
+KernelFn KernelRegistry::dispatch(const std::string& op_name) const {
+    OpId op;
+    if (!name_to_op(op_name, op)) return nullptr;
+    return lookup(cuda_key(op));
+}
+
+void KernelRegistry::clear() { registry_.clear(); }
+
+namespace {
+std::mutex g_register_mu;
+}
+
+void register_cuda_kernels() {
+    std::lock_guard<std::mutex> lk(g_register_mu);
+    auto& reg = KernelRegistry::instance();
+    if (reg.lookup(cuda_key(OpId::Dequantize))) return;  // already registered (re-registers after clear())
+    {
+        reg.register_kernel(cuda_key(OpId::MatMulQ8_0), matmul_kernel<OpId::MatMulQ8_0>);
+        reg.register_kernel(cuda_key(OpId::MatMulQ4_0), matmul_kernel<OpId::MatMulQ4_0>);
+        reg.register_kernel(cuda_key(OpId::MatMulQ2_K), matmul_kernel<OpId::MatMulQ2_K>);
+        reg.register_kernel(cuda_key(OpId::MatMulQ3_K), matmul_kernel<OpId::MatMulQ3_K>);
+        reg.register_kernel(cuda_key(OpId::MatMulQ4_K), matmul_kernel<OpId::MatMulQ4_K>);
+        reg.register_kernel(cuda_key(OpId::MatMulQ5_K), matmul_kernel<OpId::MatMulQ5_K>);
+        reg.register_kernel(cuda_key(OpId::MatMulQ6_K), matmul_kernel<OpId::MatMulQ6_K>);
+        reg.register_kernel(cuda_key(OpId::Quantize), quantize_kernel);
+        reg.register_kernel(cuda_key(OpId::Dequantize), dequantize_kernel);
+    }
+}
+
+std::string gemm_kernel_name(QuantFormat quant_a) {
+    switch (quant_a) {
+        case QuantFormat::Q4_0: return "matmul_q4_0";
+        case QuantFormat::Q4_K: return "matmul_q4_K";
+        case QuantFormat::Q5_K: return "matmul_q5_K";
+        case QuantFormat::Q8_0: return "matmul_q8_0";
+        case QuantFormat::Q2_K: return "matmul_q2_K";
+        case QuantFormat::Q3_K: return "matmul_q3_K";
+        case QuantFormat::Q6_K: return "matmul_q6_K";
+        default: return "matmul";
+    }
+}
+
+// ---- front doors ------------------------------------------------------------
+
+Expected<void> quantize(DeviceTensor& dst, const DeviceTensor& src, QuantFormat format) {
+    if (format == QuantFormat::None) return Error{"quantize: format is None"};
+    if (dst.quant().format != format) return Error{"quantize: destination descriptor does not name the format"};
+    register_cuda_kernels();
+    KernelFn fn = KernelRegistry::instance().dispatch(std::string("quantize"));
+    if (!fn) return Error{"quantize: no CUDA kernel registered"};
+    DeviceTensor outs[1] = {DeviceTensor::view(dst.data(), dst.rows(), dst.cols(), dst.dtype(), format, dst.device_index())};
+    const DeviceTensor ins[1] = {DeviceTensor::view(const_cast<void*>(src.data()), src.rows(), src.cols(), src.dtype(),
+                                                    src.quant().format, src.device_index())};
+    KernelContext ctx{outs, ins, nullptr};
+    return fn(ctx);
+}
+
+Expected<void> dequantize(DeviceTensor& dst, const DeviceTensor& src) {
+    register_cuda_kernels();
+    KernelFn fn = KernelRegistry::instance().dispatch(std::string("dequantize"));
+    if (!fn) return Error{"dequantize: no CUDA kernel registered"};
+    DeviceTensor outs[1] = {
+        DeviceTensor::view(dst.data(), dst.rows(), dst.cols(), dst.dtype(), dst.quant().format, dst.device_index())};
+    const DeviceTensor ins[1] = {DeviceTensor::view(const_cast<void*>(src.data()), src.rows(), src.cols(), src.dtype(),
+                                                    src.quant().format, src.device_index())};
+    KernelContext ctx{outs, ins, nullptr};
+    return fn(ctx);
+}
+
+Expected<void> matmul(DeviceTensor& out, const DeviceTensor& a, const DeviceTensor& b) {
+    if (!a.is_quantized()) return Error{"matmul: the CUDA backend serves quantized A only"};
+    return run_named(gemm_kernel_name(a.quant().format), out, a, b);
+}
+
+#define AXON_FIXED_MATMUL(NAME, FMT)                                                              \
+    Expected<void> NAME(DeviceTensor& out, const DeviceTensor& a, const DeviceTensor& b) {       \
+        if (a.quant().format != QuantFormat::FMT) return Error{#NAME ": A is not " #FMT};          \
+        return run_named(gemm_kernel_name(QuantFormat::FMT), out, a, b);                           \
+    }
+AXON_FIXED_MATMUL(matmul_q8_0, Q8_0)
+AXON_FIXED_MATMUL(matmul_q4, Q4_0)
+AXON_FIXED_MATMUL(matmul_q2_K, Q2_K)
+AXON_FIXED_MATMUL(matmul_q3_K, Q3_K)
+AXON_FIXED_MATMUL(matmul_q4_K, Q4_K)
+AXON_FIXED_MATMUL(matmul_q5_K, Q5_K)
+AXON_FIXED_MATMUL(matmul_q6_K, Q6_K)
+#undef AXON_FIXED_MATMUL
+
+void set_stream(axq_stream_t stream) { t_stream = stream; }
+axq_stream_t current_stream() { return t_stream; }
+
+Expected<void> synchronize() {
+    if (cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(t_stream)) != cudaSuccess) {
+        const char* m = cudaGetErrorString(cudaGetLastError());
+        return Error{std::string("synchronize: ") + m};
+    }
+    int dev = 0;
+    cudaGetDevice(&dev);
+    void* ws = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_scratch_mu);
+        auto it = g_scratch.find(dev);
+        if (it != g_scratch.end()) ws = it->second.ptr;
+    }
+    if (ws && axq_workspace_status(ws, t_stream) != AXQ_OK) return last_error("synchronize");
+    return {};
+}
+
+}  // namespace axon::cuda

@@ -1,0 +1,101 @@
+// Host mirror on the GPU, against the oracle (oracle/axq_oracle.h): for
+// every format, quantize through the registry-dispatched CUDA kernel and
+// compare the packed bytes with the oracle's (bit-exact), dequantize and
+// compare (bit-exact), and multiply through matmul() (routed by the A
+// operand's format, as choose_gemm_strategy does) for a GEMV-sized and a
+// GEMM-sized batch, within max|y - y_ref| <= 1e-3 * max|y_ref|.
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "axon_cuda.h"
+#include "axq_oracle.h"
+#include "check.h"
+
+using namespace axon::cuda;
+
+namespace {
+
+// Seeded normal samples (xorshift64* + Box-Muller).
+struct Rng {
+    uint64_t s;
+    explicit Rng(uint64_t seed) : s(seed * 0x9E3779B97F4A7C15ull + 1) {}
+    double uni() {
+        s ^= s >> 12; s ^= s << 25; s ^= s >> 27;
+        return ((s * 0x2545F4914F6CDD1Dull) >> 11) * (1.0 / 9007199254740992.0);
+    }
+    float normal() {
+        const double u1 = uni() + 1e-300, u2 = uni();
+        return static_cast<float>(std::sqrt(-2.0 * std::log(u1)) * std::cos(6.283185307179586 * u2));
+    }
+};
+
+double rel_err(const std::vector<float>& y, const std::vector<float>& ref) {
+    double num = 0, den = 0;
+    for (size_t i = 0; i < y.size(); ++i) {
+        num = std::fmax(num, std::fabs(static_cast<double>(y[i]) - ref[i]));
+        den = std::fmax(den, std::fabs(static_cast<double>(ref[i])));
+    }
+    return den == 0 ? (num == 0 ? 0 : INFINITY) : num / den;
+}
+
+void run_format(QuantFormat f, const char* name) {
+    const int fmt = static_cast<int>(f);
+    const int64_t M = 96, K = (f == QuantFormat::Q8_0 || f == QuantFormat::Q4_0) ? 1056 : 2304;
+    Rng rng(static_cast<uint64_t>(fmt) * 7 + 3);
+    std::vector<float> w(static_cast<size_t>(M * K));
+    for (auto& v : w) v = rng.normal();
+
+    // quantize through the mirror
+    auto src = DeviceTensor::from_host(w.data(), M, K);
+    CHECK_MSG(static_cast<bool>(src), name);
+    auto q = DeviceTensor::empty(M, K, f);
+    CHECK_MSG(static_cast<bool>(q), name);
+    auto r = quantize(q.value(), src.value(), f);
+    CHECK_MSG(static_cast<bool>(r), std::string(name) + ": " + (r ? "" : r.error().message));
+    std::vector<uint8_t> packed(quantized_size_2d(M, K, f)), packed_ref(packed.size());
+    CHECK(static_cast<bool>(q.value().to_host(packed.data(), packed.size())));
+    CHECK(orc_quantize(fmt, w.data(), M, K, packed_ref.data()) == 0);
+    CHECK_MSG(packed == packed_ref, std::string(name) + ": packed bytes differ from the oracle");
+
+    // dequantize
+    auto deq = DeviceTensor::empty(M, K);
+    r = dequantize(deq.value(), q.value());
+    CHECK_MSG(static_cast<bool>(r), name);
+    std::vector<float> wd(w.size()), wd_ref(w.size());
+    CHECK(static_cast<bool>(deq.value().to_host(wd.data(), wd.size() * 4)));
+    CHECK(orc_dequantize(fmt, packed_ref.data(), M, K, wd_ref.data()) == 0);
+    CHECK_MSG(std::memcmp(wd.data(), wd_ref.data(), wd.size() * 4) == 0, std::string(name) + ": dequant differs");
+
+    // matmul, one GEMV-sized and one GEMM-sized batch
+    for (int64_t N : {int64_t(3), int64_t(40)}) {
+        std::vector<float> b(static_cast<size_t>(K * N));
+        for (auto& v : b) v = rng.normal();
+        auto bd = DeviceTensor::from_host(b.data(), K, N);
+        auto out = DeviceTensor::empty(M, N);
+        r = matmul(out.value(), q.value(), bd.value());
+        CHECK_MSG(static_cast<bool>(r), std::string(name) + ": " + (r ? "" : r.error().message));
+        CHECK(static_cast<bool>(synchronize()));
+        std::vector<float> y(static_cast<size_t>(M * N)), y_ref(y.size());
+        CHECK(static_cast<bool>(out.value().to_host(y.data(), y.size() * 4)));
+        CHECK(orc_matmul(fmt, packed_ref.data(), b.data(), y_ref.data(), M, K, N) == 0);
+        const double e = rel_err(y, y_ref);
+        CHECK_MSG(e <= 1e-3, std::string(name) + " N=" + std::to_string(N) + " rel_err=" + std::to_string(e));
+    }
+}
+
+}  // namespace
+
+int main() {
+    register_cuda_kernels();
+    run_format(QuantFormat::Q8_0, "Q8_0");
+    run_format(QuantFormat::Q4_0, "Q4_0");
+    run_format(QuantFormat::Q2_K, "Q2_K");
+    run_format(QuantFormat::Q3_K, "Q3_K");
+    run_format(QuantFormat::Q4_K, "Q4_K");
+    run_format(QuantFormat::Q5_K, "Q5_K");
+    run_format(QuantFormat::Q6_K, "Q6_K");
+    return report("quant_cuda_test");
+}
