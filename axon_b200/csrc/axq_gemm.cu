@@ -376,7 +376,7 @@ template <> struct Dq<F_Q4_0> {
 };
 
 template <int F, int AL>
-__global__ void __launch_bounds__(kThreadsGemm, 1) gemm_kernel(GemmArgs a) {
+__global__ void __launch_bounds__(kThreadsGemm, 2) gemm_kernel(GemmArgs a) {
     using C = CG<F>;
     extern __shared__ __align__(1024) uint8_t smem[];
     Bars* bars = reinterpret_cast<Bars*>(smem);
@@ -427,9 +427,9 @@ __global__ void __launch_bounds__(kThreadsGemm, 1) gemm_kernel(GemmArgs a) {
         // in 16-byte chunks of the row segment's 16-byte-rounded range (bytes
         // of the neighbouring segments ride along); where that range would
         // leave the weight buffer the lane copies bytes itself.
+        int p = 0, pass = 0;  // ring slot, times the ring was filled
         for (int i = 0; i < ncg_here; ++i) {
-            const int p = i % a.npk;
-            if (i >= a.npk && !gwait(&bars->pk_empty[p], ((i / a.npk) - 1) & 1, abort_flag, a.err)) break;
+            if (pass > 0 && !gwait(&bars->pk_empty[p], (pass - 1) & 1, abort_flag, a.err)) break;
             uint8_t* pk = pk_ring + p * a.pk_bytes;
             const int64_t off = static_cast<int64_t>(cg0 + i) * C::BYTES;
             const int64_t seg = min64(C::BYTES, a.rb - off);
@@ -453,18 +453,26 @@ __global__ void __launch_bounds__(kThreadsGemm, 1) gemm_kernel(GemmArgs a) {
             }
             __threadfence_block();
             cp_async_arrive_noinc(&bars->pk_full[p]);
+            if (++p == a.npk) {
+                p = 0;
+                ++pass;
+            }
             if (*abort_flag) break;
         }
     } else if (warp == 2 + kDqWarps) {
         // ------------------------------------- activation-tile producer
         if (lane == 0) {
+            int s = 0, pass = 0;
             for (int j = 0; j < nsteps; ++j) {
-                const int s = j % a.nab;
-                if (j >= a.nab && !gwait(&bars->ab_empty[s], ((j / a.nab) - 1) & 1, abort_flag, a.err)) break;
+                if (pass > 0 && !gwait(&bars->ab_empty[s], (pass - 1) & 1, abort_flag, a.err)) break;
                 const int ks = cg0 * kKStepsPerCG + j;
                 const uint8_t* src = a.xh + (static_cast<int64_t>(ct) * a.nks_total + ks) * a.b_bytes;
                 mbar_arrive_expect_tx(&bars->b_full[s], a.b_bytes);
                 bulk_g2s(b_ring + s * a.b_bytes, src, a.b_bytes, &bars->b_full[s]);
+                if (++s == a.nab) {
+                    s = 0;
+                    ++pass;
+                }
             }
         }
         __syncwarp();
@@ -472,20 +480,26 @@ __global__ void __launch_bounds__(kThreadsGemm, 1) gemm_kernel(GemmArgs a) {
         // ------------------------------------------------------ MMA issuer
         if (lane == 0) {
             const uint32_t idesc = idesc_f16_f32(a.BN, BM);
+            // descriptor of slot 0, k16 = 0; other slots / K offsets add to its
+            // start-address field (bytes >> 4), which never carries out
+            const uint64_t bd0 = smem_desc_kmajor(smem_u32(b_ring), 128, 1024);
+            int s = 0;
+            uint32_t par = 0;
             for (int j = 0; j < nsteps; ++j) {
-                const int s = j % a.nab;
-                const uint32_t par = (j / a.nab) & 1;
                 if (!gwait(&bars->a_full[s], par, abort_flag, a.err)) break;
                 if (!gwait(&bars->b_full[s], par, abort_flag, a.err)) break;
                 tc_fence_after();
                 const uint32_t at = tmem + static_cast<uint32_t>(a.BN + 32 * s);  // A slot s (lanes 0..127)
-                const uint32_t bs = smem_u32(b_ring + s * a.b_bytes);
+                const uint64_t bds = bd0 + static_cast<uint64_t>((s * a.b_bytes) >> 4);
 #pragma unroll
-                for (int k16 = 0; k16 < BK / 16; ++k16) {
-                    const uint64_t bd = smem_desc_kmajor(bs + k16 * 256, 128, 1024);
-                    mma_f16_ta(tmem, at + 8 * k16, bd, idesc, (j > 0 || k16 > 0) ? 1u : 0u);
-                }
+                for (int k16 = 0; k16 < BK / 16; ++k16)
+                    mma_f16_ta(tmem, at + 8 * k16, bds + static_cast<uint64_t>(k16 * 16), idesc,
+                               (j > 0 || k16 > 0) ? 1u : 0u);
                 mma_commit(&bars->ab_empty[s]);
+                if (++s == a.nab) {
+                    s = 0;
+                    par ^= 1;
+                }
             }
             mma_commit(&bars->acc_full);
             // every MMA of this thread has completed once `done` fires
@@ -500,18 +514,17 @@ __global__ void __launch_bounds__(kThreadsGemm, 1) gemm_kernel(GemmArgs a) {
         const int r = 32 * q + lane;
         const int64_t row = row0 + r;
         const bool row_ok = row < a.rows;
+        int p = 0, s = 0, pass = 0;
+        uint32_t ppar = 0;
         for (int i = 0; i < ncg_here; ++i) {
-            const int p = i % a.npk;
-            if (!gwait(&bars->pk_full[p], (i / a.npk) & 1, abort_flag, a.err)) break;
+            if (!gwait(&bars->pk_full[p], ppar, abort_flag, a.err)) break;
             const int cg = cg0 + i;
             const uintptr_t ga = wbase + static_cast<uintptr_t>(row * a.rb + static_cast<int64_t>(cg) * C::BYTES);
             const uint8_t* rowp = pk_ring + p * a.pk_bytes + r * a.rs + (ga & 15);
             const bool tail = (static_cast<int64_t>(cg + 1) * 256 > a.K) || ((cg + 1) * C::BLK > a.nblk_row);
 #pragma unroll
             for (int k = 0; k < kKStepsPerCG; ++k) {
-                const int j = i * kKStepsPerCG + k;
-                const int s = j % a.nab;
-                if (j >= a.nab && !gwait(&bars->ab_empty[s], ((j / a.nab) - 1) & 1, abort_flag, a.err)) break;
+                if (pass > 0 && !gwait(&bars->ab_empty[s], (pass - 1) & 1, abort_flag, a.err)) break;
                 uint4 o[4];
                 if (row_ok) {
                     if (k == 0) Dq<F>::template kstep<0, AL>(rowp, o, h);
@@ -542,9 +555,17 @@ __global__ void __launch_bounds__(kThreadsGemm, 1) gemm_kernel(GemmArgs a) {
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&bars->a_full[s]);
+                if (++s == a.nab) {
+                    s = 0;
+                    ++pass;
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars->pk_empty[p]);
+            if (++p == a.npk) {
+                p = 0;
+                ppar ^= 1;
+            }
             if (*abort_flag) break;
         }
         // epilogue: TMEM lane r holds row r, column t holds token t
@@ -633,6 +654,7 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits,
 
 struct GemmGeom {
     int BN, nct, nrt, splits, cg_per_split, ncg, nks_total, ntok_pad;
+    int ctas_per_sm;  // 2 when BN <= 128 (see launch_gemm), else 1
     int64_t Kpad;
 };
 
@@ -649,8 +671,9 @@ GemmGeom gemm_geom(int64_t M, int64_t K, int64_t N) {
     g.ntok_pad = g.nct * g.BN;
     g.nrt = static_cast<int>((M + BM - 1) / BM);
     const int base = g.nrt * g.nct;
-    const int sms = device_sm_count();
-    int splits = std::max(1, std::min(g.ncg, sms / std::max(1, base)));
+    g.ctas_per_sm = (g.BN <= 128) ? 2 : 1;
+    const int slots = device_sm_count() * g.ctas_per_sm;
+    int splits = std::max(1, std::min(g.ncg, slots / std::max(1, base)));
     g.cg_per_split = (g.ncg + splits - 1) / splits;
     g.splits = (g.ncg + g.cg_per_split - 1) / g.cg_per_split;
     return g;
@@ -702,20 +725,31 @@ cudaError_t launch_gemm(const void* w, const float* x, float* out, int64_t M, in
     a.aligned = (reinterpret_cast<uintptr_t>(w) % 16 == 0) && (a.rb % 16 == 0);
     a.pk_bytes = BM * a.rs;
     a.b_bytes = g.BN * BK * 2;
-    const int budget = 220 * 1024 - 1024;
-    a.npk = 3;
-    a.nab = std::min(kMaxAB, (budget - a.npk * a.pk_bytes) / a.b_bytes);
-    if (a.nab < 3) {
+    // Two CTAs per SM (each with half the TMEM and ~110 KB of shared memory)
+    // when BN <= 128 leaves room for 2 packed slots and >= 3 activation/A
+    // slots: twice the dequant warps per SM and, for large M, one wave.
+    // Otherwise one CTA per SM with deeper rings.
+    const int budget2 = 110 * 1024 - 1024;
+    const int nab2 = std::min({kMaxAB, (budget2 - 2 * a.pk_bytes) / a.b_bytes, (256 - g.BN) / 32});
+    if (g.ctas_per_sm == 2 && nab2 >= 3) {
         a.npk = 2;
-        a.nab = std::max(2, std::min(kMaxAB, (budget - a.npk * a.pk_bytes) / a.b_bytes));
+        a.nab = nab2;
+    } else {
+        const int budget = 220 * 1024 - 1024;
+        a.npk = 3;
+        a.nab = std::min(kMaxAB, (budget - a.npk * a.pk_bytes) / a.b_bytes);
+        if (a.nab < 3) {
+            a.npk = 2;
+            a.nab = std::max(2, std::min(kMaxAB, (budget - a.npk * a.pk_bytes) / a.b_bytes));
+        }
+        // TMEM: BN accumulator columns + one 32-column A slot per stage, <= 512
+        a.nab = std::min(a.nab, (512 - g.BN) / 32);
     }
-    // TMEM: BN accumulator columns + one 32-column A slot per stage, <= 512
-    a.nab = std::min(a.nab, (512 - g.BN) / 32);
     {
         const int need = g.BN + 32 * a.nab;
         a.tmem_cols = need <= 32 ? 32 : need <= 64 ? 64 : need <= 128 ? 128 : need <= 256 ? 256 : 512;
     }
-    if (a.npk * a.pk_bytes + a.nab * a.b_bytes > budget) return cudaErrorInvalidConfiguration;
+    if (1024 + a.npk * a.pk_bytes + a.nab * a.b_bytes > 220 * 1024) return cudaErrorInvalidConfiguration;
     a.out_tokmajor = (flags & AXQ_FLAG_OUT_TOKMAJOR) ? 1 : 0;
     a.err = err;
     if (g.splits == 1) {

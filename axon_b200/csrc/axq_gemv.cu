@@ -226,21 +226,23 @@ template <int H, int AL> struct RowQ2K {
 // 2^(4-p): |HS| <= 16 * 32*16 * 16*7*127 < 1.2e8; |MS| <= 16*32*16*32385.
 template <int H, int AL> struct RowQ3K {
     static constexpr int RL = 16;
-    uint32_t hd, s12[3], hm[8], w[8];
+    uint32_t hd, sv[2], hm[8], w[8];  // sv: the half's eight 6-bit scales, one per byte
     __device__ __forceinline__ void load(const uint8_t* cg) {
-        uint32_t h[1];
+        uint32_t h[1], s12[3];
         ld_words<1>(cg + 108, h);
         hd = h[0];
         ld_words<3>(cg + 96, s12);
+        // scale IS = 8H + J: low 4 bits from nibble H of byte (IS & 7) of the
+        // first 8 scale bytes, high 2 bits from bits 2*(IS >> 2) of byte 8 + (IS & 3)
+        if constexpr (H == 0) {
+            sv[0] = (s12[0] & 0x0F0F0F0Fu) | ((s12[2] << 4) & 0x30303030u);
+            sv[1] = (s12[1] & 0x0F0F0F0Fu) | ((s12[2] << 2) & 0x30303030u);
+        } else {
+            sv[0] = ((s12[0] >> 4) & 0x0F0F0F0Fu) | (s12[2] & 0x30303030u);
+            sv[1] = ((s12[1] >> 4) & 0x0F0F0F0Fu) | ((s12[2] >> 2) & 0x30303030u);
+        }
         ld_words<8>(cg, hm);
         ld_words<8>(cg + 32 + 32 * H, w);
-    }
-    template <int IS>
-    __device__ __forceinline__ int subscale() const {
-        constexpr int lo_byte = (IS < 8) ? IS : IS - 8, lo_sh = (IS < 8) ? 0 : 4;
-        const int lo4 = (s12[lo_byte >> 2] >> (8 * (lo_byte & 3) + lo_sh)) & 0xF;
-        const int hi2 = (s12[2] >> (8 * (IS & 3) + 2 * (IS >> 2))) & 3;
-        return (lo4 | (hi2 << 4)) - 32;
     }
     template <int J>
     __device__ __forceinline__ void run(uint32_t* q, int& sc, int& m) const {
@@ -251,7 +253,7 @@ template <int H, int AL> struct RowQ3K {
 #pragma unroll
         for (int v = 0; v < 4; ++v)
             q[v] = ((w[4 * lh + v] >> WS) & (0x03030303u << PB)) | (shl<HSH>(hm[4 * lh + v]) & (0x04040404u << PB));
-        m = subscale<8 * H + J>();
+        m = static_cast<int>(__byte_perm(sv[J >> 2], 0u, 0x4440u | (J & 3))) - 32;
         sc = m * (1 << (4 - PB));
     }
     __device__ __forceinline__ float dscale() const { return h2f_ref(hd & 0xFFFFu) * 0.0625f; }
