@@ -385,6 +385,9 @@ __global__ void __launch_bounds__(kThreadsGemm, 2) gemm_kernel(GemmArgs a) {
     volatile int* abort_flag = &bars->abort_flag;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // The weights were complete before the activation conversion started; only
+    // the activation-tile producer reads its output, after pdl_wait below.
+    pdl_launch_dependents();
     int bid = blockIdx.x;
     const int split = bid % a.splits;
     bid /= a.splits;
@@ -461,6 +464,7 @@ __global__ void __launch_bounds__(kThreadsGemm, 2) gemm_kernel(GemmArgs a) {
         }
     } else if (warp == 2 + kDqWarps) {
         // ------------------------------------- activation-tile producer
+        pdl_wait();  // fp16 activation tiles of this call are complete
         if (lane == 0) {
             int s = 0, pass = 0;
             for (int j = 0; j < nsteps; ++j) {
@@ -608,6 +612,10 @@ __global__ void __launch_bounds__(kThreadsGemm, 2) gemm_kernel(GemmArgs a) {
 // tile (ct, ks) = BN tokens x 64 K, byte (n8*8 + kc)*128 + (n%8)*16 + (k%8)*2.
 __global__ void act_f16_kernel(const float* __restrict__ x, int64_t K, int64_t ntok, int x_tokmajor, int BN,
                                int nks_total, uint8_t* __restrict__ xh, int64_t nchunks, int* __restrict__ err) {
+    // x may come from the previous kernel; only after it has finished may the
+    // GEMM (launched early) start streaming weights.
+    pdl_wait();
+    pdl_launch_dependents();
     if (blockIdx.x == 0 && threadIdx.x == 0) *err = 0;  // status word of this call
     const int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // one 8-element chunk
     if (c >= nchunks) return;
@@ -636,6 +644,8 @@ __global__ void act_f16_kernel(const float* __restrict__ x, int64_t K, int64_t n
 // Sums the split-K partial tiles in split order.
 __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, int64_t rows, int64_t ntok,
                                      int64_t part_ld, float* __restrict__ out, int64_t out_ld, int out_tokmajor) {
+    pdl_wait();  // the partial tiles are complete
+    pdl_launch_dependents();
     const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= rows * ntok) return;
     int64_t row, t;
@@ -698,9 +708,9 @@ cudaError_t launch_gemm(const void* w, const float* x, float* out, int64_t M, in
     {
         const int64_t nchunks = static_cast<int64_t>(g.ntok_pad) * g.nks_total * 8;
         const int64_t grid = (nchunks + 255) / 256;
-        act_f16_kernel<<<static_cast<unsigned>(grid), 256, 0, s>>>(x, K, N, (flags & AXQ_FLAG_B_TOKMAJOR) ? 1 : 0,
-                                                                  g.BN, g.nks_total, xh, nchunks, err);
-        cudaError_t e = cudaGetLastError();
+        cudaError_t e = launch_pdl(act_f16_kernel, dim3(static_cast<unsigned>(grid)), dim3(256), 0, s, x, K, N,
+                                   (flags & AXQ_FLAG_B_TOKMAJOR) ? 1 : 0, g.BN, g.nks_total, xh, nchunks, err);
+        if (e == cudaSuccess) e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
     GemmArgs a{};
@@ -774,14 +784,18 @@ cudaError_t launch_gemm(const void* w, const float* x, float* out, int64_t M, in
         configured[ai][dev] = smem;
     }
     const int grid = g.nrt * g.nct * g.splits;
-    kern<<<grid, kThreadsGemm, smem, s>>>(a);
+    {
+        cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kThreadsGemm), smem, s, a);
+        if (e != cudaSuccess) return e;
+    }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     if (g.splits > 1) {
         const int64_t n = M * N;
-        splitk_reduce_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(
-            part, g.splits, M, N, g.ntok_pad, out, a.out_tokmajor ? M : N, a.out_tokmajor);
-        e = cudaGetLastError();
+        e = launch_pdl(splitk_reduce_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, s,
+                       static_cast<const float*>(part), g.splits, M, N, static_cast<int64_t>(g.ntok_pad), out,
+                       static_cast<int64_t>(a.out_tokmajor ? M : N), a.out_tokmajor);
+        if (e == cudaSuccess) e = cudaGetLastError();
     }
     return e;
 }

@@ -252,32 +252,48 @@ def run_gpu(args):
     yfull = {f: torch.empty(world * ROWS, M_TOK, device=dev) for f in FORMATS}
     ws = ax.Workspace()
     stream = torch.cuda.current_stream()
-    ev_fmt = {f: [] for f in FORMATS}  # CUDA events around each matmul (act prep + GEMV)
 
-    def step(record=False):
+    def run_fmt(fmt):
+        """One matmul of the step (activation prep + GEMV) and, with several
+        ranks, the all-gather of its output."""
+        if world > 1:
+            ax.matmul_q(yfull[fmt][rank * ROWS:(rank + 1) * ROWS], qs[fmt], x, b_tokmajor=True, workspace=ws)
+            ax.allgather_(yfull[fmt], comm)
+        else:
+            ax.linear_q(x, qs[fmt], out=ys[fmt], workspace=ws)
+
+    def step():
         for fmt in FORMATS:
-            if record:
-                e0 = torch.cuda.Event(enable_timing=True)
-                e1 = torch.cuda.Event(enable_timing=True)
-                e0.record(stream)
-            if world > 1:
-                ax.matmul_q(yfull[fmt][rank * ROWS:(rank + 1) * ROWS], qs[fmt], x, b_tokmajor=True, workspace=ws)
-            else:
-                ax.linear_q(x, qs[fmt], out=ys[fmt], workspace=ws)
-            if record:
-                e1.record(stream)
-                ev_fmt[fmt].append((e0, e1))
-            if world > 1:
-                ax.allgather_(yfull[fmt], comm)
+            run_fmt(fmt)
 
     def barrier():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
 
+    def capture(fn):
+        """fn's launches captured once in a CUDA graph (the step is a handful
+        of kernels; replaying removes the host's per-call cost), or None."""
+        try:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+                fn()
+            return graph
+        except Exception as exc:
+            print(f"graph capture failed, timing eagerly: {exc}", file=sys.stderr)
+            torch.cuda.synchronize()
+            return None
+
     for _ in range(max(args.warmup, 3)):
         step()
     barrier()
+    g_step = capture(step)
+    g_fmt = {f: capture(lambda f=f: run_fmt(f)) for f in FORMATS}
+    replay = (lambda g, fn: g.replay() if g is not None else fn())
+    for _ in range(max(args.warmup, 3)):
+        replay(g_step, step)
+    barrier()
+
     sampler = ClockSampler(local) if rank == 0 else None
     if sampler:
         sampler.start()
@@ -287,12 +303,24 @@ def run_gpu(args):
     barrier()
     t0.record(stream)
     for _ in range(args.steps):
-        step(record=True)
+        replay(g_step, step)
     t1.record(stream)
     barrier()
     ms = t0.elapsed_time(t1) / args.steps
-    fmt_ms = {f: sum(a.elapsed_time(b) for a, b in ev) / max(1, len(ev)) for f, ev in ev_fmt.items()}
+    # each format's matmul alone, replayed back to back (its average duration)
+    fmt_ms = {}
+    for f in FORMATS:
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        barrier()
+        e0.record(stream)
+        for _ in range(args.steps):
+            replay(g_fmt[f], lambda f=f: run_fmt(f))
+        e1.record(stream)
+        barrier()
+        fmt_ms[f] = e0.elapsed_time(e1) / args.steps
     clocks = sampler.stop() if sampler else None
+    del g_step, g_fmt  # graphs holding NCCL calls go before the communicator
     if world > 1:
         t = torch.tensor([ms] + [fmt_ms[f] for f in FORMATS], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -355,6 +383,7 @@ def run_gpu(args):
             "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8-dp4a/f32-acc", "data": "synthetic",
             "config": {"workload": WORKLOAD, "rows_per_gpu": ROWS, "K": K_DIM, "M": M_TOK,
+                       "timing": "one step captured in a CUDA graph, replayed; e2e is eager through linear_q",
                        "formats": list(FORMATS), "parallelism": f"row-shard x{world} + in-place NCCL all-gather (library communicator)",
                        "l2": "inputs larger than L2 (340 MB of packed weights per GPU)"},
             "roofline": {"bound": "hbm", "achieved": by_fmt[dom]["achieved"], "peak": peak, "unit": "GB/s",
@@ -451,6 +480,33 @@ def run_suite(args):
         torch.cuda.synchronize()
         return e0.elapsed_time(e1) / n_iter
 
+    def time_graph(fn, n_iter, replays=5):
+        """Per-call time with the n_iter calls captured once in a CUDA graph
+        and replayed (no host launch cost); None if capture fails."""
+        for i in range(3):
+            fn(i)
+        torch.cuda.synchronize()
+        try:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+                for i in range(n_iter):
+                    fn(i)
+            graph.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(replays):
+                graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / (replays * n_iter)
+            del graph
+            return ms
+        except Exception as exc:  # capture unsupported: report eager timing only
+            print(f"graph capture failed: {exc}", file=sys.stderr)
+            torch.cuda.synchronize()
+            return None
+
     def emit(d):
         print(json.dumps(d), flush=True)
 
@@ -463,19 +519,24 @@ def run_suite(args):
         for M in Ms:
             x = torch.randn(M, K, device=dev, generator=g)
             y = torch.empty(M, rows, device=dev)
-            ms = time_calls(lambda i: ax.linear_q(x, qs[i % len(qs)], out=y, workspace=ws), 20)
+            call = (lambda i, x=x, y=y, qs=qs: ax.linear_q(x, qs[i % len(qs)], out=y, workspace=ws))
+            ms_eager = time_calls(call, 20)
+            ms_graph = time_graph(call, 20)
+            ms = ms_graph if ms_graph is not None else ms_eager
             wbytes = ax.quantized_size_2d(rows, K, ax.QuantFormat[fmt])
             gbs = (wbytes + 4 * K * M + 4 * rows * M) / (ms / 1e3) / 1e9
             tops = 2.0 * rows * K * M / (ms / 1e3) / 1e12
             emit({"config": cfg, "format": fmt, "rows": rows, "K": K, "M": M, "ms": round(ms, 5),
+                  "timing": "cuda-graph replay" if ms_graph is not None else "eager",
+                  "eager_ms": round(ms_eager, 5),
                   "weight_GBps": round(wbytes / (ms / 1e3) / 1e9, 1), "algo_GBps": round(gbs, 1),
                   "hbm_frac": round(gbs / peak, 3), "TOPS": round(tops, 2),
                   "bf16_peak_frac": round(tops / bf16_peak, 3)})
         del qs
 
     # C3: MLP block y = W_down . (SiLU(X W_gate^T) * (X W_up^T))
-    up, gate = copies(11008, 4096, "Q4_K")[:2], None
-    gate = [weights(11008, 4096, "Q4_K")]
+    up = copies(11008, 4096, "Q4_K")
+    gate = copies(11008, 4096, "Q4_K")
     down = copies(4096, 11008, "Q6_K")
     for M in (1, 32):
         x = torch.randn(M, 4096, device=dev, generator=g)
@@ -483,16 +544,19 @@ def run_suite(args):
         hg = torch.empty(M, 11008, device=dev)
         yo = torch.empty(M, 4096, device=dev)
 
-        def mlp(i):
-            ax.linear_q(x, gate[0], out=hg, workspace=ws)
+        def mlp(i, x=x, hg=hg, hu=hu, yo=yo):
+            ax.linear_q(x, gate[i % len(gate)], out=hg, workspace=ws)
             ax.linear_q(x, up[i % len(up)], out=hu, workspace=ws)
             h = torch.nn.functional.silu(hg) * hu
             ax.linear_q(h, down[i % len(down)], out=yo, workspace=ws)
 
-        ms = time_calls(mlp, 20)
+        ms_eager = time_calls(mlp, 20)
+        ms_graph = time_graph(mlp, 20)
+        ms = ms_graph if ms_graph is not None else ms_eager
         wbytes = 2 * ax.quantized_size_2d(11008, 4096, ax.QuantFormat.Q4_K) + \
             ax.quantized_size_2d(4096, 11008, ax.QuantFormat.Q6_K)
         emit({"config": "C3", "format": "Q4_K+Q6_K MLP", "M": M, "ms": round(ms, 5),
+              "timing": "cuda-graph replay" if ms_graph is not None else "eager", "eager_ms": round(ms_eager, 5),
               "weight_GBps": round(wbytes / (ms / 1e3) / 1e9, 1),
               "TOPS": round(3 * 2.0 * 11008 * 4096 * M / (ms / 1e3) / 1e12, 2)})
 
