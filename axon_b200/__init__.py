@@ -44,6 +44,8 @@ from .ops import (  # noqa: F401
     matmul_q5_K,
     matmul_q6_K,
     linear_q,
+    gate_up_silu,
+    mlp_q,
 )
 from .shard import (  # noqa: F401
     Communicator,
@@ -57,6 +59,6 @@ from .shard import (  # noqa: F401
 __all__ = [
     "AxqError", "QuantFormat", "QTensor", "Status", "Workspace", "quantize", "dequantize", "matmul_q",
     "matmul_q8_0", "matmul_q4", "matmul_q2_K", "matmul_q3_K", "matmul_q4_K", "matmul_q5_K", "matmul_q6_K",
-    "linear_q", "quantized_size", "quantized_size_2d", "matmul_workspace_size", "lib", "lib_path",
+    "linear_q", "gate_up_silu", "mlp_q", "quantized_size", "quantized_size_2d", "matmul_workspace_size", "lib", "lib_path",
     "Communicator", "allgather_", "matmul_sharded", "row_bytes", "shard_bounds", "shard_rows",
 ]

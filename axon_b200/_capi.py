@@ -72,6 +72,9 @@ SIGNATURES = {
     "axq_matmul": (ctypes.c_int, [ctypes.c_int, _vp, _vp, _vp, _i64, _i64, _i64, ctypes.c_uint, _vp, _sz, _vp]),
     "axq_workspace_status": (ctypes.c_int, [_vp, _vp]),
     "axq_matmul_noalloc": (ctypes.c_int, [ctypes.c_int, _vp, _vp, _vp, _i64, _i64, _i64, ctypes.c_uint, _vp]),
+    "axq_gate_up_workspace_size": (_sz, [ctypes.c_int, _i64, _i64, _i64]),
+    "axq_gate_up_silu": (ctypes.c_int, [ctypes.c_int, _vp, _vp, _vp, _vp, _i64, _i64, _i64, ctypes.c_uint, _vp, _sz,
+                                        _vp]),
     "axq_comm_unique_id": (ctypes.c_int, [_vp, _sz]),
     "axq_comm_init": (ctypes.c_int, [ctypes.POINTER(_vp), _vp, _sz, ctypes.c_int, ctypes.c_int]),
     "axq_comm_init_all": (ctypes.c_int, [ctypes.POINTER(_vp), ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),

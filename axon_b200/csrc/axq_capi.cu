@@ -169,8 +169,68 @@ int axq_matmul(int fmt, const void* a_q, const float* b, float* out, int64_t M, 
     cudaError_t e = (N > kGemvMaxN)
                         ? gemm_dispatch(fmt, a_q, b, out, M, K, N, static_cast<int>(flags), ws + kStatusBytes,
                                         workspace_bytes - kStatusBytes, err, s)
-                        : gemv_dispatch(fmt, a_q, b, out, M, K, N, static_cast<int>(flags), ws + kStatusBytes,
+                        : gemv_dispatch(fmt, a_q, nullptr, b, out, M, K, N, static_cast<int>(flags), ws + kStatusBytes,
                                         workspace_bytes - kStatusBytes, err, s);
+    if (e != cudaSuccess) return cuda_fail(e, fn);
+    return AXQ_OK;
+}
+
+size_t axq_gate_up_workspace_size(int fmt, int64_t M, int64_t K, int64_t N) {
+    int be = host_block_elems(fmt);
+    if (!be || K < 0 || N < 0 || M < 0) return 0;
+    if (N <= kGemvMaxN) return axq_matmul_workspace_size(fmt, M, K, N);
+    const size_t tmp = (static_cast<size_t>(M) * static_cast<size_t>(N) * 4 + 255) / 256 * 256;
+    return axq_matmul_workspace_size(fmt, M, K, N) + 2 * tmp;
+}
+
+int axq_gate_up_silu(int fmt, const void* w_gate, const void* w_up, const float* x, float* h, int64_t M, int64_t K,
+                     int64_t N, unsigned flags, void* workspace, size_t workspace_bytes, axq_stream_t stream) {
+    const char* fn = "axq_gate_up_silu";
+    if (!known_fmt(fmt)) return fail(AXQ_ERR_UNSUPPORTED, std::string(fn) + ": unsupported format " + std::to_string(fmt));
+    if (M < 0 || K < 0 || N < 0) return fail(AXQ_ERR_INVALID, std::string(fn) + ": negative shape");
+    if (flags & ~(AXQ_FLAG_B_TOKMAJOR | AXQ_FLAG_OUT_TOKMAJOR))
+        return fail(AXQ_ERR_INVALID, std::string(fn) + ": unknown flag bits");
+    if (M == 0 || N == 0) return AXQ_OK;
+    if (N > (int64_t(1) << 24) || M > (int64_t(1) << 31) || K > (int64_t(1) << 30))
+        return fail(AXQ_ERR_INVALID, std::string(fn) + ": shape too large");
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (int r = check_ptr(h, "h", fn)) return r;
+    if (K == 0) {  // silu(0) * 0
+        cudaError_t e = cudaMemsetAsync(h, 0, static_cast<size_t>(M * N) * 4, s);
+        return e == cudaSuccess ? AXQ_OK : cuda_fail(e, fn);
+    }
+    if (int r = check_ptr(w_gate, "w_gate", fn)) return r;
+    if (int r = check_ptr(w_up, "w_up", fn)) return r;
+    if (int r = check_ptr(x, "x", fn)) return r;
+    if (reinterpret_cast<uintptr_t>(x) % 4 || reinterpret_cast<uintptr_t>(h) % 4)
+        return fail(AXQ_ERR_INVALID, std::string(fn) + ": x and h must be 4-byte aligned");
+    const size_t need = axq_gate_up_workspace_size(fmt, M, K, N);
+    if (!workspace || workspace_bytes < need)
+        return fail(AXQ_ERR_WORKSPACE, std::string(fn) + ": workspace of " + std::to_string(need) +
+                                           " bytes required (" + fmt_name(fmt) + ")");
+    if (int r = check_ptr(workspace, "workspace", fn)) return r;
+    if (reinterpret_cast<uintptr_t>(workspace) % 256)
+        return fail(AXQ_ERR_INVALID, std::string(fn) + ": workspace must be 256-byte aligned");
+    auto* ws = static_cast<uint8_t*>(workspace);
+    int* err = reinterpret_cast<int*>(ws);
+    cudaError_t e;
+    if (N <= kGemvMaxN) {
+        // one pass: every unit decodes 8 rows of W_gate and the same 8 of W_up
+        e = gemv_dispatch(fmt, w_gate, w_up, x, h, M, K, N, static_cast<int>(flags), ws + kStatusBytes,
+                          workspace_bytes - kStatusBytes, err, s);
+    } else {
+        // two tensor-core GEMMs into scratch, then h = silu(gate) * up
+        const size_t mm = axq_matmul_workspace_size(fmt, M, K, N);
+        const size_t tmp = (static_cast<size_t>(M) * static_cast<size_t>(N) * 4 + 255) / 256 * 256;
+        float* g = reinterpret_cast<float*>(ws + mm);
+        float* u = reinterpret_cast<float*>(ws + mm + tmp);
+        e = gemm_dispatch(fmt, w_gate, x, g, M, K, N, static_cast<int>(flags), ws + kStatusBytes, mm - kStatusBytes,
+                          err, s);
+        if (e == cudaSuccess)
+            e = gemm_dispatch(fmt, w_up, x, u, M, K, N, static_cast<int>(flags), ws + kStatusBytes, mm - kStatusBytes,
+                              err, s);
+        if (e == cudaSuccess) e = silu_mul_dispatch(g, u, h, M * N, s);
+    }
     if (e != cudaSuccess) return cuda_fail(e, fn);
     return AXQ_OK;
 }

@@ -800,7 +800,24 @@ cudaError_t launch_gemm(const void* w, const float* x, float* out, int64_t M, in
     return e;
 }
 
+__global__ void silu_mul_kernel(const float* __restrict__ g, const float* __restrict__ u, float* __restrict__ h,
+                                int64_t n) {
+    pdl_wait();  // both GEMM outputs are complete
+    pdl_launch_dependents();
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) {
+        const float v = g[i];
+        h[i] = v / (1.0f + expf(-v)) * u[i];
+    }
+}
+
 }  // namespace
+
+cudaError_t silu_mul_dispatch(const float* g, const float* u, float* h, int64_t n, cudaStream_t s) {
+    if (n <= 0) return cudaSuccess;
+    cudaError_t e = launch_pdl(silu_mul_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, s, g, u, h, n);
+    return e == cudaSuccess ? cudaGetLastError() : e;
+}
 
 size_t gemm_workspace_bytes(int fmt, int64_t M, int64_t K, int64_t N) {
     switch (fmt) {

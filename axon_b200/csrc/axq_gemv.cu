@@ -562,6 +562,11 @@ struct GemvArgs {
     int64_t out_ld;          // row stride of out ([M x ld] or [ntok x ld] when token-major)
     int out_tokmajor;
     int* err;
+    // fused gate/up mode (pair = 1): w is W_gate, w2 is W_up, a unit is 8
+    // output rows, stage slot r < 8 holds row 8u+r of W_gate and slot r + 8
+    // the same row of W_up, and out = silu(W_gate.x) * (W_up.x)
+    const uint8_t* w2;
+    int pair;
 };
 
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
@@ -570,6 +575,14 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
         if (*abort_flag) return false;
     }
     return false;
+}
+
+// Source row and buffer of stage slot `slot` of unit u.
+__device__ __forceinline__ int64_t slot_row(const GemvArgs& a, int64_t u, int slot) {
+    return a.pair ? u * 8 + (slot & 7) : u * kUnitRows + slot;
+}
+__device__ __forceinline__ uintptr_t slot_base(const GemvArgs& a, int slot) {
+    return reinterpret_cast<uintptr_t>((a.pair && slot >= 8) ? a.w2 : a.w);
 }
 
 template <int F, int NT, int AL>
@@ -596,8 +609,6 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
     }
     __syncthreads();
 
-    const uintptr_t wbase = reinterpret_cast<uintptr_t>(a.w);
-    const uintptr_t wend = wbase + static_cast<uintptr_t>(a.rows * a.rb);
     const int64_t step_bytes = static_cast<int64_t>(kStageCG) * L::CGB;
 
     if (warp == kConsumerWarps) {
@@ -617,7 +628,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
                 uint8_t* st = stages + s * a.stage_bytes;
                 const int64_t off = static_cast<int64_t>(ks) * step_bytes;
                 const int64_t seg = min64(step_bytes, a.rb - off);
-                const int64_t row = u * kUnitRows + lane;
+                const int64_t row = slot_row(a, u, lane);
+                const uintptr_t wbase = slot_base(a, lane);
+                const uintptr_t wend = wbase + static_cast<uintptr_t>(a.rows * a.rb);
                 uint32_t my_tx = 0;
                 bool bulk = false;
                 uintptr_t lo = 0;
@@ -666,7 +679,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
     int s = 0, unit_par = 0;
     uint32_t phase = 0;
     for (int64_t u = blockIdx.x; u < a.units; u += gridDim.x, unit_par ^= 1) {
-        const int64_t row0 = u * kUnitRows + pr, row1 = row0 + 8;
+        const int64_t row0 = slot_row(a, u, pr), row1 = slot_row(a, u, pr + 8);
+        const uintptr_t base0 = slot_base(a, pr), base1 = slot_base(a, pr + 8);
         const bool ok0 = row0 < a.rows, ok1 = row1 < a.rows;
         for (int ks = 0; ks < a.nks; ++ks) {
             if (!wait_or_abort(&full[s], phase, abort_flag)) {
@@ -679,10 +693,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
             if (ok0 && cg < a.ncg && !*abort_flag) {
                 const int64_t off = static_cast<int64_t>(ks) * step_bytes;
                 const uint8_t* st = stages + s * a.stage_bytes + cgl * L::CGB;
-                const uint8_t* c0 = st + pr * a.rs + ((wbase + static_cast<uintptr_t>(row0 * a.rb + off)) & 15);
+                const uint8_t* c0 = st + pr * a.rs + ((base0 + static_cast<uintptr_t>(row0 * a.rb + off)) & 15);
                 // a row past the end decodes row0 again; its sum is never written
                 const uint8_t* c1 =
-                    ok1 ? st + (pr + 8) * a.rs + ((wbase + static_cast<uintptr_t>(row1 * a.rb + off)) & 15) : c0;
+                    ok1 ? st + (pr + 8) * a.rs + ((base1 + static_cast<uintptr_t>(row1 * a.rb + off)) & 15) : c0;
                 const ActCG X{a.act + static_cast<int64_t>(cg) * a.act_cg_stride};
                 const int nbv = a.nblk_row - cg * 8;
                 if (h == 0) L::template half<0, AL, NT>(c0, c1, nbv, X, a.ntok, acc);
@@ -709,14 +723,20 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
             }
         }
         asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
-        const int64_t orow = u * kUnitRows + lane;
-        if (warp == 0 && lane < 16 && orow < a.rows) {
+        const int64_t orow = a.pair ? u * 8 + lane : u * kUnitRows + lane;
+        if (warp == 0 && lane < (a.pair ? 8 : 16) && orow < a.rows) {
 #pragma unroll
             for (int t = 0; t < NT; ++t) {
                 if (t < a.ntok) {
                     float v = 0.0f;
 #pragma unroll
                     for (int w2 = 0; w2 < kConsumerWarps; ++w2) v += rp[(w2 * kUnitRows + lane) * NT + t];
+                    if (a.pair) {  // v = gate row; combine with the same row of W_up
+                        float up = 0.0f;
+#pragma unroll
+                        for (int w2 = 0; w2 < kConsumerWarps; ++w2) up += rp[(w2 * kUnitRows + lane + 8) * NT + t];
+                        v = v / (1.0f + expf(-v)) * up;
+                    }
                     if (a.out_tokmajor) a.out[t * a.out_ld + orow] = v;
                     else a.out[orow * a.out_ld + t] = v;
                 }
@@ -779,8 +799,8 @@ cudaError_t launch_al(const GemvPlan& p, const GemvArgs& a, int nt, cudaStream_t
 }
 
 template <int F>
-cudaError_t launch_gemv(const void* w, const float* x, float* out, int64_t M, int64_t K, int64_t N, int flags,
-                        void* ws, size_t ws_bytes, int* err, cudaStream_t s) {
+cudaError_t launch_gemv(const void* w, const void* w2, const float* x, float* out, int64_t M, int64_t K, int64_t N,
+                        int flags, void* ws, size_t ws_bytes, int* err, cudaStream_t s) {
     using L = Lane<F>;
     constexpr int BE = Traits<F>::BE, BB = Traits<F>::BB;
     const int64_t bpr = (K + BE - 1) / BE;
@@ -803,14 +823,17 @@ cudaError_t launch_gemv(const void* w, const float* x, float* out, int64_t M, in
     a.nblk_row = static_cast<int>(bpr);
     a.ncg = static_cast<int>((bpr * BB + L::CGB - 1) / L::CGB);
     a.nks = (a.ncg + kStageCG - 1) / kStageCG;
-    a.units = (M + kUnitRows - 1) / kUnitRows;
+    a.w2 = static_cast<const uint8_t*>(w2);
+    a.pair = (w2 != nullptr) ? 1 : 0;
+    a.units = a.pair ? (M + 7) / 8 : (M + kUnitRows - 1) / kUnitRows;
     a.act_cg_stride = N * kActRec;
     a.out_tokmajor = (flags & AXQ_FLAG_OUT_TOKMAJOR) ? 1 : 0;
     a.out_ld = a.out_tokmajor ? M : N;
     a.err = err;
     // Natural alignment holds when the buffer and every row start are
     // 16-byte aligned; otherwise every format takes the any-alignment loads.
-    const bool aligned = (reinterpret_cast<uintptr_t>(w) % 16 == 0) && (a.rb % 16 == 0);
+    const bool aligned = (reinterpret_cast<uintptr_t>(w) % 16 == 0) && (a.rb % 16 == 0) &&
+                         (reinterpret_cast<uintptr_t>(w2) % 16 == 0);
     const int sms = device_sm_count();
     for (int64_t t0 = 0; t0 < N; t0 += 8) {
         const int nt_run = static_cast<int>(std::min<int64_t>(8, N - t0));
@@ -836,16 +859,16 @@ size_t gemv_workspace_bytes(int64_t Kp, int64_t ntok) {
     return (static_cast<size_t>(nch * ntok) * kActRec + 255) / 256 * 256;
 }
 
-cudaError_t gemv_dispatch(int fmt, const void* w, const float* x, float* out, int64_t M, int64_t K, int64_t N, int flags,
-                          void* ws, size_t ws_bytes, int* err, cudaStream_t s) {
+cudaError_t gemv_dispatch(int fmt, const void* w, const void* w2, const float* x, float* out, int64_t M, int64_t K,
+                          int64_t N, int flags, void* ws, size_t ws_bytes, int* err, cudaStream_t s) {
     switch (fmt) {
-        case F_Q8_0: return launch_gemv<F_Q8_0>(w, x, out, M, K, N, flags, ws, ws_bytes, err, s);
-        case F_Q4_0: return launch_gemv<F_Q4_0>(w, x, out, M, K, N, flags, ws, ws_bytes, err, s);
-        case F_Q2_K: return launch_gemv<F_Q2_K>(w, x, out, M, K, N, flags, ws, ws_bytes, err, s);
-        case F_Q3_K: return launch_gemv<F_Q3_K>(w, x, out, M, K, N, flags, ws, ws_bytes, err, s);
-        case F_Q4_K: return launch_gemv<F_Q4_K>(w, x, out, M, K, N, flags, ws, ws_bytes, err, s);
-        case F_Q5_K: return launch_gemv<F_Q5_K>(w, x, out, M, K, N, flags, ws, ws_bytes, err, s);
-        case F_Q6_K: return launch_gemv<F_Q6_K>(w, x, out, M, K, N, flags, ws, ws_bytes, err, s);
+        case F_Q8_0: return launch_gemv<F_Q8_0>(w, w2, x, out, M, K, N, flags, ws, ws_bytes, err, s);
+        case F_Q4_0: return launch_gemv<F_Q4_0>(w, w2, x, out, M, K, N, flags, ws, ws_bytes, err, s);
+        case F_Q2_K: return launch_gemv<F_Q2_K>(w, w2, x, out, M, K, N, flags, ws, ws_bytes, err, s);
+        case F_Q3_K: return launch_gemv<F_Q3_K>(w, w2, x, out, M, K, N, flags, ws, ws_bytes, err, s);
+        case F_Q4_K: return launch_gemv<F_Q4_K>(w, w2, x, out, M, K, N, flags, ws, ws_bytes, err, s);
+        case F_Q5_K: return launch_gemv<F_Q5_K>(w, w2, x, out, M, K, N, flags, ws, ws_bytes, err, s);
+        case F_Q6_K: return launch_gemv<F_Q6_K>(w, w2, x, out, M, K, N, flags, ws, ws_bytes, err, s);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -25,8 +25,10 @@ cudaError_t dequant_dispatch(int fmt, const void* src, float* dst, int64_t rows,
 // matmul (Kp = K rounded up to the format's block).
 size_t gemv_workspace_bytes(int64_t Kp, int64_t ntok);
 
-cudaError_t gemv_dispatch(int fmt, const void* w, const float* x, float* out, int64_t M, int64_t K, int64_t N, int flags,
-                          void* ws, size_t ws_bytes, int* err, cudaStream_t s);
+// w2 == nullptr: out = W.X.  w2 != nullptr: fused gate/up, out =
+// silu(W.X) * (W2.X) elementwise (both [M x K] in the same format).
+cudaError_t gemv_dispatch(int fmt, const void* w, const void* w2, const float* x, float* out, int64_t M, int64_t K,
+                          int64_t N, int flags, void* ws, size_t ws_bytes, int* err, cudaStream_t s);
 
 // Tensor-core GEMM for N > 8 activation columns.
 size_t gemm_workspace_bytes(int fmt, int64_t M, int64_t K, int64_t N);
@@ -51,6 +53,9 @@ cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t 
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
+
+// h[i] = silu(g[i]) * u[i] for n elements (the fused MLP's GEMM path).
+cudaError_t silu_mul_dispatch(const float* g, const float* u, float* h, int64_t n, cudaStream_t s);
 
 // Largest N served by the GEMV kernel; larger batches use the GEMM.
 constexpr int64_t kGemvMaxN = 8;

@@ -16,6 +16,7 @@ from typing import Dict, Optional, Tuple
 import torch
 
 from ._capi import (
+    BLOCK_BYTES,
     BLOCK_ELEMS,
     FLAG_B_TOKMAJOR,
     FLAG_OUT_TOKMAJOR,
@@ -28,9 +29,29 @@ from ._capi import (
 )
 
 
-def _stream_handle(stream: Optional[torch.cuda.Stream]) -> int:
-    s = stream if stream is not None else torch.cuda.current_stream()
-    return int(s.cuda_stream)
+def _stream_handle(stream: Optional[torch.cuda.Stream], device: Optional[torch.device] = None) -> int:
+    if stream is not None:
+        return int(stream.cuda_stream)
+    idx = device.index if device is not None and device.index is not None else torch.cuda.current_device()
+    return int(torch._C._cuda_getCurrentRawStream(idx))  # the current stream, without a Stream object
+
+
+_ws_size_cache: Dict[Tuple[int, int, int, int], int] = {}
+
+
+def _ws_size(fmt: int, M: int, K: int, N: int) -> int:
+    key = (fmt, M, K, N)
+    v = _ws_size_cache.get(key)
+    if v is None:
+        v = int(lib().axq_matmul_workspace_size(fmt, M, K, N))
+        if len(_ws_size_cache) < 4096:
+            _ws_size_cache[key] = v
+    return v
+
+
+def _packed_bytes(M: int, K: int, fmt: QuantFormat) -> int:
+    be = BLOCK_ELEMS[fmt]
+    return M * ((K + be - 1) // be) * BLOCK_BYTES[fmt]
 
 
 def _req_cuda(t: torch.Tensor, name: str, dtype: torch.dtype) -> None:
@@ -165,14 +186,14 @@ def matmul_q(out: torch.Tensor, a, b: torch.Tensor, fmt: Optional[QuantFormat] =
     want = (N, M) if out_tokmajor else (M, N)
     if tuple(out.shape) != want:
         raise AxqError(Status.ERR_INVALID, f"matmul_q: output shape {tuple(out.shape)} != {want}")
-    if buf.numel() < quantized_size_2d(M, K, fmt):
+    if buf.numel() < _packed_bytes(M, K, fmt):
         raise AxqError(Status.ERR_INVALID, "matmul_q: quantized operand is smaller than its shape")
     flags = (FLAG_B_TOKMAJOR if b_tokmajor else 0) | (FLAG_OUT_TOKMAJOR if out_tokmajor else 0)
-    need = int(lib().axq_matmul_workspace_size(int(fmt), M, K, N))
+    need = _ws_size(int(fmt), M, K, N)
     ws = (workspace or _default_ws).get(need + 256, out.device)
     wp, wbytes = _aligned_ptr(ws)
     check(lib().axq_matmul(int(fmt), buf.data_ptr(), b.data_ptr(), out.data_ptr(), M, K, N, flags, wp, wbytes,
-                           _stream_handle(stream)))
+                           _stream_handle(stream, out.device)))
     return out
 
 
@@ -206,3 +227,40 @@ def linear_q(x: torch.Tensor, w: QTensor, out: Optional[torch.Tensor] = None, **
     if out is None:
         out = torch.empty((x.shape[0], M), dtype=torch.float32, device=x.device)
     return matmul_q(out, w, x, b_tokmajor=True, out_tokmajor=True, **kw)
+
+
+def gate_up_silu(x: torch.Tensor, w_gate: QTensor, w_up: QTensor, out: Optional[torch.Tensor] = None,
+                 workspace: Optional[Workspace] = None, stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """Fused front half of a gated MLP: h[N, M] = silu(x . W_gate^T) * (x . W_up^T),
+    silu(v) = v / (1 + e^-v).  The reference has neither SiLU nor a quantized
+    Linear (its Linear, src/nn/linear.cpp:19-27, is fp32); this composes its
+    quantized matmul.  Up to 8 rows of x run as a single GEMV pass over both
+    packed matrices (one activation prep, SiLU and product in the epilogue)."""
+    if w_gate.fmt != w_up.fmt or tuple(w_gate.shape) != tuple(w_up.shape):
+        raise AxqError(Status.ERR_INVALID, "gate_up_silu: W_gate and W_up must have the same shape and format")
+    M, K = w_gate.shape
+    fmt = int(w_gate.fmt)
+    _req_cuda(x, "x", torch.float32)
+    _req_cuda(w_gate.data, "w_gate", torch.uint8)
+    _req_cuda(w_up.data, "w_up", torch.uint8)
+    if x.dim() != 2 or x.shape[1] != K:
+        raise AxqError(Status.ERR_INVALID, f"gate_up_silu: x must be [N x {K}]")
+    N = x.shape[0]
+    if out is None:
+        out = torch.empty((N, M), dtype=torch.float32, device=x.device)
+    _req_cuda(out, "out", torch.float32)
+    if tuple(out.shape) != (N, M):
+        raise AxqError(Status.ERR_INVALID, f"gate_up_silu: out must be [{N} x {M}]")
+    need = int(lib().axq_gate_up_workspace_size(fmt, M, K, N))
+    wp, wbytes = _aligned_ptr((workspace or _default_ws).get(need + 256, out.device))
+    check(lib().axq_gate_up_silu(fmt, w_gate.data.data_ptr(), w_up.data.data_ptr(), x.data_ptr(), out.data_ptr(), M, K,
+                                 N, FLAG_B_TOKMAJOR | FLAG_OUT_TOKMAJOR, wp, wbytes, _stream_handle(stream, out.device)))
+    return out
+
+
+def mlp_q(x: torch.Tensor, w_gate: QTensor, w_up: QTensor, w_down: QTensor, out: Optional[torch.Tensor] = None,
+          workspace: Optional[Workspace] = None, stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """Gated MLP block y = (silu(x W_gate^T) * (x W_up^T)) W_down^T with packed
+    weights: the fused gate/up pass, then the down projection."""
+    h = gate_up_silu(x, w_gate, w_up, workspace=workspace, stream=stream)
+    return linear_q(h, w_down, out=out, workspace=workspace, stream=stream)

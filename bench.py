@@ -540,15 +540,11 @@ def run_suite(args):
     down = copies(4096, 11008, "Q6_K")
     for M in (1, 32):
         x = torch.randn(M, 4096, device=dev, generator=g)
-        hu = torch.empty(M, 11008, device=dev)
-        hg = torch.empty(M, 11008, device=dev)
         yo = torch.empty(M, 4096, device=dev)
 
-        def mlp(i, x=x, hg=hg, hu=hu, yo=yo):
-            ax.linear_q(x, gate[i % len(gate)], out=hg, workspace=ws)
-            ax.linear_q(x, up[i % len(up)], out=hu, workspace=ws)
-            h = torch.nn.functional.silu(hg) * hu
-            ax.linear_q(h, down[i % len(down)], out=yo, workspace=ws)
+        def mlp(i, x=x, yo=yo):
+            # fused gate/up pass (silu * product in the epilogue), then W_down
+            ax.mlp_q(x, gate[i % len(gate)], up[i % len(up)], down[i % len(down)], out=yo, workspace=ws)
 
         ms_eager = time_calls(mlp, 20)
         ms_graph = time_graph(mlp, 20)

@@ -90,6 +90,17 @@ size_t axq_matmul_workspace_size(int fmt, int64_t M, int64_t K, int64_t N);
 int axq_matmul(int fmt, const void* a_q, const float* b, float* out, int64_t M, int64_t K, int64_t N,
                unsigned flags, void* workspace, size_t workspace_bytes, axq_stream_t stream);
 
+/* Fused MLP front half (the reference has no SiLU and no quantized Linear;
+ * this is the composition SiLU(X W_gate^T) * (X W_up^T) of its matmul):
+ *   h = silu(W_gate . B) * (W_up . B)  elementwise, silu(v) = v / (1 + e^-v),
+ * W_gate and W_up packed [M x K] in the same format, layouts and flags as
+ * axq_matmul (h is [M x N], or [N x M] with AXQ_FLAG_OUT_TOKMAJOR).  Up to 8
+ * columns run as one GEMV pass over both matrices; more use two tensor-core
+ * GEMMs and an elementwise kernel (scratch included in the workspace). */
+size_t axq_gate_up_workspace_size(int fmt, int64_t M, int64_t K, int64_t N);
+int axq_gate_up_silu(int fmt, const void* w_gate, const void* w_up, const float* b, float* h, int64_t M, int64_t K,
+                     int64_t N, unsigned flags, void* workspace, size_t workspace_bytes, axq_stream_t stream);
+
 /* Bytes of the scratch array built into the library for
  * axq_matmul_noalloc (16 MiB, held by every GPU that loads the library). */
 #define AXQ_NOALLOC_SCRATCH_BYTES (16u << 20)
