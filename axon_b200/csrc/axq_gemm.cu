@@ -1,4 +1,4 @@
-// Quantized GEMM for batches of activation columns (N >= 9 "tokens") on the
+// Quantized GEMM for batches of activation columns (N >= 5 "tokens") on the
 // 5th-generation tensor cores: out[M x N] = W_q[M x K] . X[K x N].
 //
 // Tile: 128 weight rows x BN tokens (BN <= 256, multiple of 16), fp32

@@ -1,5 +1,5 @@
 // Quantized GEMV / small-batch matmul: out[M x N] = W_q[M x K] . X[K x N]
-// for N (activation columns, "tokens") of 1..8, HBM-bound on the packed
+// for N (activation columns, "tokens") of 1..4, HBM-bound on the packed
 // weights.
 //
 // Design (B200-first):
@@ -793,8 +793,7 @@ cudaError_t launch_al(const GemvPlan& p, const GemvArgs& a, int nt, cudaStream_t
     switch (nt) {
         case 1: return launch_nt<F, 1, AL>(p, a, s);
         case 2: return launch_nt<F, 2, AL>(p, a, s);
-        case 4: return launch_nt<F, 4, AL>(p, a, s);
-        default: return launch_nt<F, 8, AL>(p, a, s);
+        default: return launch_nt<F, 4, AL>(p, a, s);
     }
 }
 
@@ -835,9 +834,9 @@ cudaError_t launch_gemv(const void* w, const void* w2, const float* x, float* ou
     const bool aligned = (reinterpret_cast<uintptr_t>(w) % 16 == 0) && (a.rb % 16 == 0) &&
                          (reinterpret_cast<uintptr_t>(w2) % 16 == 0);
     const int sms = device_sm_count();
-    for (int64_t t0 = 0; t0 < N; t0 += 8) {
-        const int nt_run = static_cast<int>(std::min<int64_t>(8, N - t0));
-        const int nt = nt_run == 1 ? 1 : nt_run == 2 ? 2 : nt_run <= 4 ? 4 : 8;
+    for (int64_t t0 = 0; t0 < N; t0 += kGemvMaxN) {
+        const int nt_run = static_cast<int>(std::min<int64_t>(kGemvMaxN, N - t0));
+        const int nt = nt_run == 1 ? 1 : nt_run == 2 ? 2 : 4;
         GemvPlan p = plan_gemv<F>(nt);
         p.grid = static_cast<int>(std::min<int64_t>(a.units, static_cast<int64_t>(sms) * p.ctas_per_sm));
         a.rs = p.rs;

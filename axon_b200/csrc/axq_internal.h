@@ -57,7 +57,8 @@ cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t 
 // h[i] = silu(g[i]) * u[i] for n elements (the fused MLP's GEMM path).
 cudaError_t silu_mul_dispatch(const float* g, const float* u, float* h, int64_t n, cudaStream_t s);
 
-// Largest N served by the GEMV kernel; larger batches use the GEMM.
-constexpr int64_t kGemvMaxN = 8;
+// Largest N served by the GEMV kernel; larger batches use the GEMM (whose
+// cost barely depends on N below 128, while the GEMV's per-token work grows).
+constexpr int64_t kGemvMaxN = 4;
 
 }  // namespace axq

@@ -94,7 +94,7 @@ int axq_matmul(int fmt, const void* a_q, const float* b, float* out, int64_t M, 
  * this is the composition SiLU(X W_gate^T) * (X W_up^T) of its matmul):
  *   h = silu(W_gate . B) * (W_up . B)  elementwise, silu(v) = v / (1 + e^-v),
  * W_gate and W_up packed [M x K] in the same format, layouts and flags as
- * axq_matmul (h is [M x N], or [N x M] with AXQ_FLAG_OUT_TOKMAJOR).  Up to 8
+ * axq_matmul (h is [M x N], or [N x M] with AXQ_FLAG_OUT_TOKMAJOR).  Up to 4
  * columns run as one GEMV pass over both matrices; more use two tensor-core
  * GEMMs and an elementwise kernel (scratch included in the workspace). */
 size_t axq_gate_up_workspace_size(int fmt, int64_t M, int64_t K, int64_t N);

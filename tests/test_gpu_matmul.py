@@ -136,7 +136,7 @@ def test_matmul_unaligned_weight_buffer(cuda, orc, fmt, offset):
         assert rel_err(out.cpu().numpy(), orc.matmul(fmt, q, B, M, K)) <= TOL, (fmt, offset, M, K)
 
 
-# ---- batched path (N > 8 activation columns: tcgen05 tensor-core GEMM) ----
+# ---- batched path (N > 4 activation columns: tcgen05 tensor-core GEMM) ----
 
 @pytest.mark.parametrize("fmt", FORMATS)
 @pytest.mark.parametrize("M,K,N", [(128, 4096, 16), (200, 1000, 9), (256, 4096, 64), (130, 11008, 32),
