@@ -87,6 +87,13 @@ SIGNATURES = {
     "axq_allgather": (ctypes.c_int, [_vp, _vp, _sz, _vp]),
     "axq_matmul_sharded": (ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, _vp, _i64, _i64, _i64, ctypes.c_uint, _vp,
                                           _sz, _vp]),
+    "axq_symm_create": (ctypes.c_int, [_vp, _sz, ctypes.POINTER(_vp), ctypes.POINTER(_vp)]),
+    "axq_symm_destroy": (ctypes.c_int, [_vp]),
+    "axq_matmul_sharded_p2p": (ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, _i64, _i64, _i64, ctypes.c_uint, _vp, _sz,
+                                              _vp]),
+    "axq_matmul_sharded_p2p_async": (ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, _i64, _i64, _i64, ctypes.c_uint, _vp,
+                                                    _sz, _vp]),
+    "axq_symm_wait": (ctypes.c_int, [_vp, _vp]),
 }
 
 COMM_ID_BYTES = 128  # AXQ_COMM_ID_BYTES

@@ -66,6 +66,16 @@ constexpr size_t kStatusBytes = 256;  // status words at the front of a workspac
 
 }  // namespace
 
+int validate_matmul_ptrs(int fmt, const void* a_q, const void* b, const void* out, const char* fn) {
+    if (!known_fmt(fmt)) return fail(AXQ_ERR_UNSUPPORTED, std::string(fn) + ": unsupported format " + std::to_string(fmt));
+    if (int r = check_ptr(a_q, "a_q", fn)) return r;
+    if (int r = check_ptr(b, "b", fn)) return r;
+    if (int r = check_ptr(out, "out", fn)) return r;
+    if (reinterpret_cast<uintptr_t>(b) % 4 || reinterpret_cast<uintptr_t>(out) % 4)
+        return fail(AXQ_ERR_INVALID, std::string(fn) + ": b and out must be 4-byte aligned");
+    return AXQ_OK;
+}
+
 void set_last_error(const std::string& msg) { g_last_error = msg; }
 
 int device_sm_count() {

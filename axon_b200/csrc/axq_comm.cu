@@ -23,6 +23,7 @@
 
 #include "axq_common.cuh"
 #include "axq_internal.h"
+#include "axq_ptx.cuh"
 
 namespace axq {
 namespace {
@@ -77,6 +78,7 @@ NcclApi& nccl() {
 struct Comm {
     ncclComm_t nc = nullptr;
     int nranks = 0, rank = 0, device = 0;
+    bool single_process = false;  // made by axq_comm_init_all
     int64_t calls = 0;
     int64_t fail_at = -1;  // host-side failure injection: fail collective #fail_at
 };
@@ -112,6 +114,58 @@ int allgather_inplace(Comm* c, float* buf, size_t count, cudaStream_t s, const c
     ncclResult_t r = nccl().all_gather(buf + static_cast<size_t>(c->rank) * count, buf, count, ncclFloat32, c->nc, s);
     if (r != ncclSuccess) return nccl_fail(r, fn);
     return AXQ_OK;
+}
+
+// ---- symmetric buffers (CUDA IPC) and the peer-store barrier ---------------
+
+// Layout of one rank's allocation: [data: bytes, rounded to 256] then the
+// control block, one 128-byte line per counter: the completion counter and
+// the entry counter (every rank adds 1 to each per call), this rank's
+// finished-CTA counter and its call count (epoch).
+constexpr size_t kSymmCtrlBytes = 512;
+constexpr int kMaxRanks = 64;  // the GEMV epilogue stores to every rank in turn
+
+struct Symm {
+    Comm* c = nullptr;
+    size_t bytes = 0, data_bytes = 0;
+    uint8_t* local = nullptr;
+    std::vector<uint8_t*> peer;       // every rank's allocation (peer[rank] = local)
+    float** d_out = nullptr;          // device: data pointer of every rank
+    unsigned** d_comp = nullptr;      // device: completion counter of every rank
+    unsigned** d_entry = nullptr;     // device: entry counter of every rank
+    bool pending = false;             // a peer-store call awaits its axq_symm_wait
+    int* pending_err = nullptr;       // status word of that call's workspace
+    static unsigned* ctrl(uint8_t* base, size_t data_bytes, int line) {
+        return reinterpret_cast<unsigned*>(base + data_bytes + 128 * line);
+    }
+    unsigned* comp() const { return ctrl(local, data_bytes, 0); }
+    unsigned* entry() const { return ctrl(local, data_bytes, 1); }
+    unsigned* done() const { return ctrl(local, data_bytes, 2); }
+    unsigned* epoch() const { return ctrl(local, data_bytes, 3); }
+};
+
+// Waits until every rank has signalled this rank for the next epoch (their
+// peer stores of the output are then visible here), then advances the epoch.
+// Bounded: a rank that never signals sets *err and the wait gives up.  It
+// first waits for the stream's earlier kernels, so epochs advance in call
+// order even when several buffers have calls outstanding.
+__global__ void peer_wait_kernel(const unsigned* comp, unsigned* epoch, int nranks, int* err) {
+    pdl_wait();  // every earlier kernel of the stream (and its epoch update) is complete
+    pdl_launch_dependents();
+    if (threadIdx.x != 0) return;
+    const unsigned e = *epoch + 1;
+    // every rank adds 1 per call, and no rank can signal call e + 1 before
+    // this rank's wait for call e is over, so the sum reaches e * nranks only
+    // once every rank has signalled call e
+    const unsigned target = e * static_cast<unsigned>(nranks);
+    uint32_t spins = 0;
+    while (static_cast<int>(ld_acquire_sys_u32(comp) - target) < 0) {
+        if (++spins > (1u << 23)) {  // a second or two of polling
+            atomicExch(err, 1);
+            break;
+        }
+    }
+    *epoch = e;
 }
 
 }  // namespace
@@ -184,6 +238,7 @@ int axq_comm_init_all(void** comms_out, int ndev, const int* devs) {
         c->nranks = ndev;
         c->rank = i;
         c->device = devs[i];
+        c->single_process = true;
         comms_out[i] = c;
     }
     return AXQ_OK;
@@ -248,6 +303,202 @@ int axq_allgather(void* comm, float* buf, size_t count_per_rank, axq_stream_t st
     if (int e = check_comm(c, "axq_allgather")) return e;
     if (count_per_rank == 0) return AXQ_OK;
     return allgather_inplace(c, buf, count_per_rank, reinterpret_cast<cudaStream_t>(stream), "axq_allgather");
+}
+
+int axq_symm_create(void* comm, size_t bytes, void** symm_out, void** local_out) {
+    const char* fn = "axq_symm_create";
+    auto* c = static_cast<Comm*>(comm);
+    if (int e = check_comm(c, fn)) return e;
+    if (!symm_out || !local_out || bytes == 0) {
+        set_last_error(std::string(fn) + ": invalid arguments");
+        return AXQ_ERR_INVALID;
+    }
+    if (c->nranks > kMaxRanks || c->single_process) {
+        set_last_error(std::string(fn) + ": needs one process per GPU and at most 64 ranks");
+        return AXQ_ERR_UNSUPPORTED;
+    }
+    *symm_out = nullptr;
+    *local_out = nullptr;
+    auto* y = new Symm();
+    y->c = c;
+    y->bytes = bytes;
+    y->data_bytes = (bytes + 255) / 256 * 256;
+    const int G = c->nranks;
+    auto cuda_err = [&](cudaError_t e, const char* what) {
+        set_last_error(std::string(fn) + ": " + what + ": " + cudaGetErrorString(e));
+        return AXQ_ERR_CUDA;
+    };
+    cudaError_t e = cudaMalloc(&y->local, y->data_bytes + kSymmCtrlBytes);
+    if (e != cudaSuccess) {
+        delete y;
+        return cuda_err(e, "cudaMalloc");
+    }
+    cudaMemset(y->local + y->data_bytes, 0, kSymmCtrlBytes);
+    cudaIpcMemHandle_t h;
+    e = cudaIpcGetMemHandle(&h, y->local);
+    // exchange the handles: an all-gather of G x 64 bytes on the communicator
+    uint8_t* d_h = nullptr;
+    std::vector<cudaIpcMemHandle_t> hs(G);
+    cudaStream_t st = nullptr;
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaMalloc(&d_h, static_cast<size_t>(G) * sizeof(h));
+    if (e == cudaSuccess) e = cudaMemcpy(d_h + c->rank * sizeof(h), &h, sizeof(h), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        if (st) cudaStreamDestroy(st);
+        if (d_h) cudaFree(d_h);
+        cudaFree(y->local);
+        delete y;
+        return cuda_err(e, "handle exchange setup");
+    }
+    ncclResult_t r = nccl().all_gather(d_h + c->rank * sizeof(h), d_h, sizeof(h), ncclUint8, c->nc, st);
+    if (r == ncclSuccess) e = cudaStreamSynchronize(st);
+    if (r == ncclSuccess && e == cudaSuccess)
+        e = cudaMemcpy(hs.data(), d_h, static_cast<size_t>(G) * sizeof(h), cudaMemcpyDeviceToHost);
+    cudaFree(d_h);
+    cudaStreamDestroy(st);
+    if (r != ncclSuccess) {
+        cudaFree(y->local);
+        delete y;
+        return nccl_fail(r, fn);
+    }
+    y->peer.assign(G, nullptr);
+    y->peer[c->rank] = y->local;
+    for (int g = 0; g < G && e == cudaSuccess; ++g) {
+        if (g == c->rank) continue;
+        void* p = nullptr;
+        e = cudaIpcOpenMemHandle(&p, hs[g], cudaIpcMemLazyEnablePeerAccess);
+        y->peer[g] = static_cast<uint8_t*>(p);
+    }
+    std::vector<float*> outs(G);
+    std::vector<unsigned*> cmp(G), ent(G);
+    for (int g = 0; g < G; ++g) {
+        outs[g] = reinterpret_cast<float*>(y->peer[g]);
+        cmp[g] = y->peer[g] ? Symm::ctrl(y->peer[g], y->data_bytes, 0) : nullptr;
+        ent[g] = y->peer[g] ? Symm::ctrl(y->peer[g], y->data_bytes, 1) : nullptr;
+    }
+    if (e == cudaSuccess) e = cudaMalloc(&y->d_out, G * sizeof(float*));
+    if (e == cudaSuccess) e = cudaMalloc(&y->d_comp, G * sizeof(unsigned*));
+    if (e == cudaSuccess) e = cudaMalloc(&y->d_entry, G * sizeof(unsigned*));
+    if (e == cudaSuccess) e = cudaMemcpy(y->d_out, outs.data(), G * sizeof(float*), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(y->d_comp, cmp.data(), G * sizeof(unsigned*), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(y->d_entry, ent.data(), G * sizeof(unsigned*), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        axq_symm_destroy(y);
+        return cuda_err(e, "peer mapping");
+    }
+    *symm_out = y;
+    *local_out = y->local;
+    return AXQ_OK;
+}
+
+int axq_symm_destroy(void* symm) {
+    auto* y = static_cast<Symm*>(symm);
+    if (!y) return AXQ_OK;
+    cudaDeviceSynchronize();
+    for (size_t g = 0; g < y->peer.size(); ++g)
+        if (static_cast<int>(g) != y->c->rank && y->peer[g]) cudaIpcCloseMemHandle(y->peer[g]);
+    if (y->d_out) cudaFree(y->d_out);
+    if (y->d_comp) cudaFree(y->d_comp);
+    if (y->d_entry) cudaFree(y->d_entry);
+    if (y->local) cudaFree(y->local);
+    delete y;
+    return AXQ_OK;
+}
+
+int axq_symm_wait(void* symm, axq_stream_t stream) {
+    auto* y = static_cast<Symm*>(symm);
+    if (!y) {
+        set_last_error("axq_symm_wait: symmetric buffer is NULL");
+        return AXQ_ERR_INVALID;
+    }
+    if (int e = check_comm(y->c, "axq_symm_wait")) return e;
+    if (!y->pending) return AXQ_OK;  // the last call already completed in stream order
+    y->pending = false;
+    cudaError_t e = launch_pdl(peer_wait_kernel, dim3(1), dim3(32), 0, reinterpret_cast<cudaStream_t>(stream),
+                               static_cast<const unsigned*>(y->comp()), y->epoch(), y->c->nranks, y->pending_err);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        set_last_error(std::string("axq_symm_wait: ") + cudaGetErrorString(e));
+        return AXQ_ERR_CUDA;
+    }
+    return AXQ_OK;
+}
+
+int axq_matmul_sharded_p2p(void* symm, int fmt, const void* a_q_local, const float* b, int64_t M, int64_t K, int64_t N,
+                           unsigned flags, void* workspace, size_t workspace_bytes, axq_stream_t stream) {
+    if (int st = axq_matmul_sharded_p2p_async(symm, fmt, a_q_local, b, M, K, N, flags, workspace, workspace_bytes,
+                                              stream))
+        return st;
+    return axq_symm_wait(symm, stream);
+}
+
+int axq_matmul_sharded_p2p_async(void* symm, int fmt, const void* a_q_local, const float* b, int64_t M, int64_t K,
+                                 int64_t N, unsigned flags, void* workspace, size_t workspace_bytes,
+                                 axq_stream_t stream) {
+    const char* fn = "axq_matmul_sharded_p2p";
+    auto* y = static_cast<Symm*>(symm);
+    if (!y) {
+        set_last_error(std::string(fn) + ": symmetric buffer is NULL");
+        return AXQ_ERR_INVALID;
+    }
+    Comm* c = y->c;
+    if (int e = check_comm(c, fn)) return e;
+    if (flags & AXQ_FLAG_OUT_TOKMAJOR) {
+        set_last_error(std::string(fn) + ": the sharded output is row-major [M x N] (no AXQ_FLAG_OUT_TOKMAJOR)");
+        return AXQ_ERR_UNSUPPORTED;
+    }
+    if (M < 0 || K < 0 || N < 0 || M % c->nranks) {
+        set_last_error(std::string(fn) + ": M=" + std::to_string(M) + " must be >= 0 and divisible by " +
+                       std::to_string(c->nranks) + " ranks");
+        return AXQ_ERR_INVALID;
+    }
+    if (static_cast<size_t>(M) * static_cast<size_t>(N) * 4 > y->bytes) {
+        set_last_error(std::string(fn) + ": output [M x N] does not fit the symmetric buffer");
+        return AXQ_ERR_INVALID;
+    }
+    const int64_t rows = M / c->nranks;
+    float* out = reinterpret_cast<float*>(y->local);
+    float* mine = out + static_cast<size_t>(c->rank) * rows * N;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (y->pending) {
+        set_last_error(std::string(fn) + ": the buffer's previous call needs axq_symm_wait first");
+        return AXQ_ERR_INVALID;
+    }
+    if (N > kGemvMaxN || K == 0 || rows == 0 || N == 0) {
+        // tensor-core path (or an empty problem): local rows in place, then the
+        // NCCL all-gather (complete in stream order: nothing to wait for)
+        int st = axq_matmul(fmt, a_q_local, b, mine, rows, K, N, flags, workspace, workspace_bytes, stream);
+        if (st) return st;
+        if (rows == 0 || N == 0) return AXQ_OK;
+        return allgather_inplace(c, out, static_cast<size_t>(rows * N), s, fn);
+    }
+    // checks as axq_matmul, then the peer-store GEMV and the wait
+    if (int st = validate_matmul_ptrs(fmt, a_q_local, b, mine, fn)) return st;
+    const size_t need = axq_matmul_workspace_size(fmt, rows, K, N);
+    if (!workspace || workspace_bytes < need || reinterpret_cast<uintptr_t>(workspace) % 256) {
+        set_last_error(std::string(fn) + ": a 256-byte aligned workspace of " + std::to_string(need) +
+                       " bytes is required");
+        return AXQ_ERR_WORKSPACE;
+    }
+    const int64_t call = c->calls++;
+    if (c->fail_at >= 0 && call == c->fail_at) {
+        set_last_error(std::string(fn) + ": injected communicator failure at collective " + std::to_string(call));
+        return AXQ_ERR_COMM;
+    }
+    int* err = static_cast<int*>(workspace);
+    GemvPeers peers{y->d_out, y->d_comp, y->done(), y->d_entry, y->entry(), y->epoch(),
+                    c->rank * rows,  c->nranks, c->rank};
+    cudaError_t e = gemv_dispatch(fmt, a_q_local, nullptr, b, mine, rows, K, N, static_cast<int>(flags),
+                                  static_cast<uint8_t*>(workspace) + 256, workspace_bytes - 256, err, s, &peers);
+    if (e == cudaSuccess) {
+        y->pending = true;
+        y->pending_err = err;
+    }
+    if (e != cudaSuccess) {
+        set_last_error(std::string(fn) + ": " + cudaGetErrorString(e));
+        return AXQ_ERR_CUDA;
+    }
+    return AXQ_OK;
 }
 
 int axq_matmul_sharded(void* comm, int fmt, const void* a_q_local, const float* b, float* out, int64_t M, int64_t K,

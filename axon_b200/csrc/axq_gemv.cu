@@ -44,7 +44,7 @@ constexpr int kUnitRows = 16;
 constexpr int kMaxStages = 8;
 constexpr int kStageCG = 2 * kConsumerWarps;  // column groups per stage (two per warp)
 // Shared-memory header: full[kMaxStages], empty[kMaxStages] mbarriers, abort flag.
-constexpr int kHeaderBytes = ((2 * kMaxStages * 8 + 4 + 127) / 128) * 128;
+constexpr int kHeaderBytes = ((2 * kMaxStages * 8 + 8 + 127) / 128) * 128;  // barriers, abort and entry flags
 
 // n 32-bit words from shared address p with static alignment A (16, 4, or 1
 // for "any").  The generic form reads one extra word past the data.
@@ -567,6 +567,25 @@ struct GemvArgs {
     // the same row of W_up, and out = silu(W_gate.x) * (W_up.x)
     const uint8_t* w2;
     int pair;
+    // peer-store epilogue (npeers > 0, row-major out only): each output value
+    // is stored at row row_offset + row of every rank's copy of the output
+    // (peer_out[g], mapped over NVLink; a.out is unused), and the grid's last
+    // CTA then adds 1 to every rank's completion counter peer_comp[g]
+    float* const* peer_out;
+    unsigned* const* peer_comp;
+    unsigned* done;  // finished-CTA count of this grid (reset by the last CTA)
+    // entry handshake: the last CTA adds 1 to every rank's entry counter
+    // peer_entry[g] as the grid starts; before its first peer store each CTA
+    // waits until every rank has entered this call (*my_entry >= (*epoch + 1)
+    // * npeers), so no rank overwrites a copy its owner may still be reading.
+    // Counters are sums over ranks: a rank enters call e + 1 only after its
+    // wait for call e, which needs every rank to have entered call e, so the
+    // sum reaches (e + 1) * npeers only once every rank has entered call e + 1.
+    unsigned* const* peer_entry;
+    const unsigned* my_entry;
+    const unsigned* epoch;
+    int64_t row_offset;
+    int npeers, rank;
 };
 
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
@@ -592,6 +611,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + kMaxStages;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kMaxStages);
+    // peer-store calls: 1 once every rank has entered this call, 2 if the
+    // producer's wait for that gave up (set by the producer warp)
+    unsigned* entry_flag = reinterpret_cast<unsigned*>(empty + kMaxStages) + 1;
     float* red = reinterpret_cast<float*>(smem + kHeaderBytes);  // [2][warps][16][NT]
     uint8_t* stages = smem + kHeaderBytes + ((2 * kConsumerWarps * kUnitRows * NT * 4 + 127) / 128) * 128;
 
@@ -605,6 +627,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
             mbar_init(&empty[s], kConsumerWarps);
         }
         *abort_flag = 0;
+        *entry_flag = 0;
         fence_mbar_init();
     }
     __syncthreads();
@@ -613,16 +636,44 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
 
     if (warp == kConsumerWarps) {
         // ---------------- producer warp: lane r copies row r of each stage ----
+        // Peer-store calls: the entry signal comes from the last CTA (one with
+        // the fewest units), and every CTA's producer waits for the other
+        // ranks' entry before its first wait for a free slot (consumers never
+        // hold it up), handing the result to the consumers in entry_flag.
+        // This grid started after every earlier kernel of the stream
+        // completed (the activation prep waited for them before it let this
+        // grid launch), so this rank's reads of the old output are done.
+        if (a.npeers > 0 && lane == 0 && blockIdx.x == gridDim.x - 1)
+            for (int g = 0; g < a.npeers; ++g) red_add_sys_u32(a.peer_entry[g], 1u);
+        bool polled = (a.npeers == 0);
+        auto poll_entry = [&]() {
+            if (lane == 0) {
+                const unsigned target = (*a.epoch + 1) * static_cast<unsigned>(a.npeers);
+                unsigned ok = 1;
+                uint32_t spins = 0;
+                while (static_cast<int>(ld_acquire_sys_u32(a.my_entry) - target) < 0) {
+                    if (++spins > (1u << 23)) {  // a second or two: give up, report
+                        atomicExch(a.err, 1);
+                        ok = 2;
+                        break;
+                    }
+                }
+                st_release_cta_shared_u32(entry_flag, ok);
+            }
+            __syncwarp();
+            polled = true;
+        };
         int s = 0, pass = 0;  // ring slot and how many times the ring was filled
         for (int64_t u = blockIdx.x; u < a.units; u += gridDim.x) {
             for (int ks = 0; ks < a.nks; ++ks) {
                 if (pass > 0) {
+                    if (!polled) poll_entry();
                     if (!wait_or_abort(&empty[s], (pass - 1) & 1, abort_flag)) {
                         if (lane == 0) {
                             *abort_flag = 1;
                             atomicExch(a.err, 1);
                         }
-                        return;
+                        return;  // (the entry was polled before this wait)
                     }
                 }
                 uint8_t* st = stages + s * a.stage_bytes;
@@ -662,6 +713,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
                 }
             }
         }
+        if (!polled) poll_entry();
         return;
     }
 
@@ -678,6 +730,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
     for (int t = 0; t < NT; ++t) acc[0][t] = acc[1][t] = 0.0f;
     int s = 0, unit_par = 0;
     uint32_t phase = 0;
+    bool entered = (a.npeers == 0);  // every rank has entered this call
     for (int64_t u = blockIdx.x; u < a.units; u += gridDim.x, unit_par ^= 1) {
         const int64_t row0 = slot_row(a, u, pr), row1 = slot_row(a, u, pr + 8);
         const uintptr_t base0 = slot_base(a, pr), base1 = slot_base(a, pr + 8);
@@ -723,6 +776,19 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
             }
         }
         asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+        if (!entered && warp == 0) {
+            if (lane == 0) {  // the producer's entry wait (normally long done)
+                uint32_t spins = 0;
+                while (ld_acquire_cta_shared_u32(entry_flag) == 0) {
+                    if (++spins > (1u << 28)) {  // outlasts the producer's own bounded wait
+                        atomicExch(a.err, 1);
+                        break;
+                    }
+                }
+            }
+            __syncwarp();
+            entered = true;
+        }
         const int64_t orow = a.pair ? u * 8 + lane : u * kUnitRows + lane;
         if (warp == 0 && lane < (a.pair ? 8 : 16) && orow < a.rows) {
 #pragma unroll
@@ -737,10 +803,29 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
                         for (int w2 = 0; w2 < kConsumerWarps; ++w2) up += rp[(w2 * kUnitRows + lane + 8) * NT + t];
                         v = v / (1.0f + expf(-v)) * up;
                     }
-                    if (a.out_tokmajor) a.out[t * a.out_ld + orow] = v;
-                    else a.out[orow * a.out_ld + t] = v;
+                    if (a.npeers > 0) {
+                        const int64_t gi = (a.row_offset + orow) * a.out_ld + t;
+                        for (int g = 0; g < a.npeers; ++g) a.peer_out[g][gi] = v;
+                    } else if (a.out_tokmajor) {
+                        a.out[t * a.out_ld + orow] = v;
+                    } else {
+                        a.out[orow * a.out_ld + t] = v;
+                    }
                 }
             }
+        }
+    }
+    if (a.npeers > 0 && warp == 0) {
+        // The warp's peer stores are ordered before the CTA counts itself
+        // (a GPU-scope release, cumulative over the warp barrier); the last
+        // CTA acquires every count, and one system-scope release fence (its
+        // cumulativity covers all the stores it has observed) precedes its
+        // signal to each rank.  A system fence in every CTA costs far more.
+        __syncwarp();
+        if (lane == 0 && atom_add_acq_rel_gpu_u32(a.done, 1u) == gridDim.x - 1) {
+            *a.done = 0u;  // the next call's CTAs count only after this grid completes
+            fence_acq_rel_sys();
+            for (int g = 0; g < a.npeers; ++g) red_add_sys_u32(a.peer_comp[g], 1u);
         }
     }
 }
@@ -799,7 +884,7 @@ cudaError_t launch_al(const GemvPlan& p, const GemvArgs& a, int nt, cudaStream_t
 
 template <int F>
 cudaError_t launch_gemv(const void* w, const void* w2, const float* x, float* out, int64_t M, int64_t K, int64_t N,
-                        int flags, void* ws, size_t ws_bytes, int* err, cudaStream_t s) {
+                        int flags, void* ws, size_t ws_bytes, int* err, cudaStream_t s, const GemvPeers* peers) {
     using L = Lane<F>;
     constexpr int BE = Traits<F>::BE, BB = Traits<F>::BB;
     const int64_t bpr = (K + BE - 1) / BE;
@@ -822,6 +907,18 @@ cudaError_t launch_gemv(const void* w, const void* w2, const float* x, float* ou
     a.nblk_row = static_cast<int>(bpr);
     a.ncg = static_cast<int>((bpr * BB + L::CGB - 1) / L::CGB);
     a.nks = (a.ncg + kStageCG - 1) / kStageCG;
+    if (peers) {
+        if (N > kGemvMaxN || (flags & AXQ_FLAG_OUT_TOKMAJOR)) return cudaErrorInvalidValue;
+        a.peer_out = peers->out;
+        a.peer_comp = peers->comp;
+        a.done = peers->done;
+        a.peer_entry = peers->entry;
+        a.my_entry = peers->my_entry;
+        a.epoch = peers->epoch;
+        a.row_offset = peers->row_offset;
+        a.npeers = peers->n;
+        a.rank = peers->rank;
+    }
     a.w2 = static_cast<const uint8_t*>(w2);
     a.pair = (w2 != nullptr) ? 1 : 0;
     a.units = a.pair ? (M + 7) / 8 : (M + kUnitRows - 1) / kUnitRows;
@@ -859,15 +956,16 @@ size_t gemv_workspace_bytes(int64_t Kp, int64_t ntok) {
 }
 
 cudaError_t gemv_dispatch(int fmt, const void* w, const void* w2, const float* x, float* out, int64_t M, int64_t K,
-                          int64_t N, int flags, void* ws, size_t ws_bytes, int* err, cudaStream_t s) {
+                          int64_t N, int flags, void* ws, size_t ws_bytes, int* err, cudaStream_t s,
+                          const GemvPeers* peers) {
     switch (fmt) {
-        case F_Q8_0: return launch_gemv<F_Q8_0>(w, w2, x, out, M, K, N, flags, ws, ws_bytes, err, s);
-        case F_Q4_0: return launch_gemv<F_Q4_0>(w, w2, x, out, M, K, N, flags, ws, ws_bytes, err, s);
-        case F_Q2_K: return launch_gemv<F_Q2_K>(w, w2, x, out, M, K, N, flags, ws, ws_bytes, err, s);
-        case F_Q3_K: return launch_gemv<F_Q3_K>(w, w2, x, out, M, K, N, flags, ws, ws_bytes, err, s);
-        case F_Q4_K: return launch_gemv<F_Q4_K>(w, w2, x, out, M, K, N, flags, ws, ws_bytes, err, s);
-        case F_Q5_K: return launch_gemv<F_Q5_K>(w, w2, x, out, M, K, N, flags, ws, ws_bytes, err, s);
-        case F_Q6_K: return launch_gemv<F_Q6_K>(w, w2, x, out, M, K, N, flags, ws, ws_bytes, err, s);
+        case F_Q8_0: return launch_gemv<F_Q8_0>(w, w2, x, out, M, K, N, flags, ws, ws_bytes, err, s, peers);
+        case F_Q4_0: return launch_gemv<F_Q4_0>(w, w2, x, out, M, K, N, flags, ws, ws_bytes, err, s, peers);
+        case F_Q2_K: return launch_gemv<F_Q2_K>(w, w2, x, out, M, K, N, flags, ws, ws_bytes, err, s, peers);
+        case F_Q3_K: return launch_gemv<F_Q3_K>(w, w2, x, out, M, K, N, flags, ws, ws_bytes, err, s, peers);
+        case F_Q4_K: return launch_gemv<F_Q4_K>(w, w2, x, out, M, K, N, flags, ws, ws_bytes, err, s, peers);
+        case F_Q5_K: return launch_gemv<F_Q5_K>(w, w2, x, out, M, K, N, flags, ws, ws_bytes, err, s, peers);
+        case F_Q6_K: return launch_gemv<F_Q6_K>(w, w2, x, out, M, K, N, flags, ws, ws_bytes, err, s, peers);
         default: return cudaErrorInvalidValue;
     }
 }

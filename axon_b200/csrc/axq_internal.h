@@ -18,6 +18,10 @@ int device_sm_count();
 // Sets the calling thread's axq_last_error() message.
 void set_last_error(const std::string& msg);
 
+// The pointer and format checks of axq_matmul (status 0 or an AXQ_ERR_*
+// code with the message set).
+int validate_matmul_ptrs(int fmt, const void* a_q, const void* b, const void* out, const char* fn);
+
 cudaError_t pack_dispatch(int fmt, const float* src, void* dst, int64_t rows, int64_t cols, cudaStream_t s);
 cudaError_t dequant_dispatch(int fmt, const void* src, float* dst, int64_t rows, int64_t cols, cudaStream_t s);
 
@@ -25,10 +29,31 @@ cudaError_t dequant_dispatch(int fmt, const void* src, float* dst, int64_t rows,
 // matmul (Kp = K rounded up to the format's block).
 size_t gemv_workspace_bytes(int64_t Kp, int64_t ntok);
 
+// Peer-store epilogue of a row-sharded GEMV: device arrays of the n ranks'
+// output copies, of their completion and entry counters, this rank's
+// finished-CTA counter, entry counters and call epoch, and the global row of
+// local row 0.
+// Peer-store GEMV epilogue of a row-sharded matmul: out[g] is rank g's
+// copy of the full output (this rank's rows start at row_offset), comp[g]
+// and entry[g] its completion and entry counters; my_entry, epoch and done
+// are this rank's entry counter, call count and finished-CTA counter.
+struct GemvPeers {
+    float* const* out;
+    unsigned* const* comp;
+    unsigned* done;
+    unsigned* const* entry;
+    const unsigned* my_entry;
+    const unsigned* epoch;
+    int64_t row_offset;
+    int n, rank;
+};
+
 // w2 == nullptr: out = W.X.  w2 != nullptr: fused gate/up, out =
 // silu(W.X) * (W2.X) elementwise (both [M x K] in the same format).
+// peers != nullptr: the outputs go to every rank (see GemvPeers), row-major.
 cudaError_t gemv_dispatch(int fmt, const void* w, const void* w2, const float* x, float* out, int64_t M, int64_t K,
-                          int64_t N, int flags, void* ws, size_t ws_bytes, int* err, cudaStream_t s);
+                          int64_t N, int flags, void* ws, size_t ws_bytes, int* err, cudaStream_t s,
+                          const GemvPeers* peers = nullptr);
 
 // Tensor-core GEMM for N > 8 activation columns.
 size_t gemm_workspace_bytes(int fmt, int64_t M, int64_t K, int64_t N);

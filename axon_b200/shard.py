@@ -173,3 +173,72 @@ def matmul_sharded(out: torch.Tensor, a_local: QTensor, b: torch.Tensor, comm: C
     check(lib().axq_matmul_sharded(comm.handle, fmt, a_local.data.data_ptr(), b.data_ptr(), out.data_ptr(), M, K, N,
                                    flags, ptr, nbytes, _stream_handle(stream)))
     return out
+
+
+class _CudaArray:
+    """__cuda_array_interface__ view of library-owned device memory."""
+
+    def __init__(self, ptr: int, shape, typestr: str = "<f4"):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 2, "strides": None}
+
+
+class SymmetricBuffer:
+    """Device memory that every rank of a communicator allocates and maps
+    from every other rank (CUDA IPC over NVLink).  Collective to create and
+    to destroy; `tensor(shape)` views this rank's copy as fp32."""
+
+    def __init__(self, comm: Communicator, nbytes: int):
+        h, p = ctypes.c_void_p(), ctypes.c_void_p()
+        check(lib().axq_symm_create(comm.handle, nbytes, ctypes.byref(h), ctypes.byref(p)))
+        self._h, self.ptr, self.nbytes, self.comm = h, p.value, nbytes, comm
+
+    @property
+    def handle(self) -> ctypes.c_void_p:
+        if not self._h.value:
+            raise AxqError(Status.ERR_INVALID, "symmetric buffer was destroyed")
+        return self._h
+
+    def tensor(self, shape) -> torch.Tensor:
+        n = 1
+        for d in shape:
+            n *= int(d)
+        if 4 * n > self.nbytes:
+            raise AxqError(Status.ERR_INVALID, f"view of {n} floats exceeds the buffer's {self.nbytes} bytes")
+        return torch.as_tensor(_CudaArray(self.ptr, shape), device=f"cuda:{torch.cuda.current_device()}")
+
+    def wait(self, stream: Optional[torch.cuda.Stream] = None) -> None:
+        """Enqueue the wait for this buffer's outstanding peer-store call."""
+        check(lib().axq_symm_wait(self.handle, _stream_handle(stream)))
+
+    def destroy(self) -> None:
+        if self._h.value:
+            h, self._h = self._h, ctypes.c_void_p()
+            check(lib().axq_symm_destroy(h))
+
+
+def matmul_sharded_p2p(out: SymmetricBuffer, a_local: QTensor, b: torch.Tensor, M: int, b_tokmajor: bool = False,
+                       workspace: Optional[Workspace] = None, stream: Optional[torch.cuda.Stream] = None,
+                       wait: bool = True) -> torch.Tensor:
+    """As matmul_sharded, into a symmetric buffer: up to 4 columns store every
+    output value straight into each rank's copy from the GEMV epilogue (no
+    separate collective).  Returns this rank's full [M x N] copy.  wait=False
+    leaves the completion wait to `out.wait()`, so calls on several buffers
+    can be issued back to back."""
+    _req_cuda(a_local.data, "a_local.data", torch.uint8)
+    _req_cuda(b, "b", torch.float32)
+    comm = out.comm
+    rows, K = a_local.shape
+    if rows * comm.world != M:
+        raise AxqError(Status.ERR_INVALID, f"local shard has {rows} rows; {comm.world} ranks need M/{comm.world}")
+    if b.dim() != 2 or (b.shape[1] if b_tokmajor else b.shape[0]) != K:
+        raise AxqError(Status.ERR_INVALID, f"b must be 2-D with K={K}")
+    N = b.shape[0] if b_tokmajor else b.shape[1]
+    fmt = int(a_local.fmt)
+    need = int(lib().axq_matmul_workspace_size(fmt, rows, K, N))
+    ptr, nbytes = _aligned_ptr((workspace or _default_ws).get(need + 256, b.device))
+    flags = FLAG_B_TOKMAJOR if b_tokmajor else 0
+    fn = lib().axq_matmul_sharded_p2p if wait else lib().axq_matmul_sharded_p2p_async
+    check(fn(out.handle, fmt, a_local.data.data_ptr(), b.data_ptr(), M, K, N, flags, ptr, nbytes,
+             _stream_handle(stream, b.device)))
+    return out.tensor((M, N))

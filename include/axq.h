@@ -169,6 +169,36 @@ int axq_comm_inject_failure(void* comm, int64_t collective_index);
  * buf + r*count_per_rank; on completion every rank holds all of them. */
 int axq_allgather(void* comm, float* buf, size_t count_per_rank, axq_stream_t stream);
 
+/* Symmetric buffer: every rank allocates `bytes` of device memory (plus a
+ * small signal area) and maps every other rank's allocation over NVLink
+ * (CUDA IPC).  Collective over the communicator's ranks (one process per
+ * GPU).  *local_out is this rank's copy; destroy is collective too and must
+ * follow the last use on every rank. */
+int axq_symm_create(void* comm, size_t bytes, void** symm_out, void** local_out);
+int axq_symm_destroy(void* symm);
+
+/* As axq_matmul_sharded, with the output in a symmetric buffer (full
+ * [M x N] row-major copy on every rank): for up to 4 columns the GEMV's
+ * epilogue stores every output value into each rank's copy over NVLink and
+ * its last CTA signals the ranks; a one-thread kernel then waits (bounded)
+ * until every rank has signalled — no separate collective.  More columns run
+ * the tensor-core path and the in-place NCCL all-gather.  A wait that gives
+ * up sets the workspace status (axq_workspace_status). */
+int axq_matmul_sharded_p2p(void* symm, int fmt, const void* a_q_local, const float* b, int64_t M, int64_t K,
+                           int64_t N, unsigned flags, void* workspace, size_t workspace_bytes, axq_stream_t stream);
+
+/* axq_matmul_sharded_p2p split in two: the _async call enqueues the
+ * peer-store GEMV only; axq_symm_wait(symm, stream) enqueues the wait that
+ * makes the full output visible on this rank (a no-op when the call took the
+ * NCCL path).  Calls on different buffers may be issued back to back and
+ * waited for together; each buffer takes one outstanding call (a second
+ * _async on it before its wait returns AXQ_ERR_INVALID).  The status word of
+ * the call's workspace reports a wait that gave up. */
+int axq_matmul_sharded_p2p_async(void* symm, int fmt, const void* a_q_local, const float* b, int64_t M, int64_t K,
+                                 int64_t N, unsigned flags, void* workspace, size_t workspace_bytes,
+                                 axq_stream_t stream);
+int axq_symm_wait(void* symm, axq_stream_t stream);
+
 /* out[M x N] (row-major, full size on every rank) = A_q . B where this rank
  * passes only its row shard a_q_local (M/G packed rows of K elements).  The
  * local rows are computed in place into out and then all-gathered on

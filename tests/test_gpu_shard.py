@@ -74,6 +74,41 @@ def test_sharded_argument_errors(comm1):
         ax.matmul_sharded(torch.empty(16, 1, device="cuda"), a, torch.empty(256, 1, device="cuda"), comm1, 16)
 
 
+def test_one_rank_peer_store_async_and_wait(orc, comm1):
+    """The peer-store path on one rank (its only peer is itself): calls on two
+    buffers issued back to back, then both waits, three times over; a second
+    call on a buffer whose wait is outstanding is refused on the host."""
+    import torch
+    import axon_b200 as ax
+    rng = np.random.default_rng(5)
+    cases = []
+    for fmt, M, K, N in [("Q2_K", 272, 2048, 1), ("Q6_K", 96, 1024, 4)]:
+        q = orc.quantize(fmt, gen(rng, (M, K), "randn"))
+        b = rng.standard_normal((K, N)).astype(np.float32)
+        a = ax.QTensor(torch.from_numpy(q).cuda(), (M, K), ax.QuantFormat[fmt])
+        cases.append((a, torch.from_numpy(b).cuda(), M, N, orc.matmul(fmt, q, b, M, K)))
+    bufs = [ax.SymmetricBuffer(comm1, 4 * M * N) for _, _, M, N, _ in cases]
+    try:
+        for _ in range(3):
+            for (a, bd, M, N, _), buf in zip(cases, bufs):
+                buf.tensor((M, N)).fill_(float("nan"))
+                ax.matmul_sharded_p2p(buf, a, bd, M, wait=False)
+            a, bd, M, _, _ = cases[0]
+            with pytest.raises(ax.AxqError, match="axq_symm_wait first") as e:
+                ax.matmul_sharded_p2p(bufs[0], a, bd, M, wait=False)
+            assert e.value.status == ax.Status.ERR_INVALID
+            for buf in bufs:
+                buf.wait()
+                buf.wait()  # nothing outstanding: a no-op
+            torch.cuda.synchronize()
+            for (_, _, M, N, y_ref), buf in zip(cases, bufs):
+                assert rel_err(buf.tensor((M, N)).cpu().numpy(), y_ref) <= TOL
+    finally:
+        torch.cuda.synchronize()
+        for buf in bufs:
+            buf.destroy()
+
+
 def test_destroyed_communicator_is_refused(cuda):
     import axon_b200 as ax
     c = ax.Communicator.create(ax.Communicator.unique_id(), 1, 0)
@@ -103,6 +138,11 @@ def test_multi_gpu_sharded_parity(cuda, tmp_path, ranks):
         rep = json.load(open(tmp_path / f"rank{rank}.json"))
         for c in rep["cases"]:
             assert c["err"] <= TOL and c["err_tokmajor"] <= TOL, c
+        assert len(rep["p2p"]) == 7
+        for c in rep["p2p"]:
+            assert all(e <= TOL for e in c["errs"]), c
+        assert len(rep["p2p_async"]) == 2 and all(e <= TOL for errs in rep["p2p_async"] for e in errs), rep
+        assert rep["p2p_refused"] == ax.Status.ERR_INVALID
         assert rep["injected"][0] == ax.Status.ERR_COMM, rep["injected"]
         assert rep["allgather_ok"] and rep["check_ok"]
         assert rep.get("wrong_device_status") == ax.Status.ERR_INVALID
