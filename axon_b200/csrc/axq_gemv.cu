@@ -219,45 +219,70 @@ template <int H, int AL> struct RowQ2K {
     __device__ __forceinline__ float mscale() const { return h2f_ref(hd >> 16); }
 };
 
+// Bit select: bits of x where m is set, bits of y elsewhere (one LOP3).
+__device__ __forceinline__ uint32_t bsel(uint32_t m, uint32_t x, uint32_t y) { return (x & m) | (y & ~m); }
+
+// Byte j of w sign-extended to 32 bits (prmt with the sign-replicate flag).
+template <int J>
+__device__ __forceinline__ int sext_byte(uint32_t w) {
+    constexpr uint32_t sel = J | ((8 | J) << 4) | ((8 | J) << 8) | ((8 | J) << 12);
+    uint32_t r;
+    asm("prmt.b32 %0, %1, 0, %2;" : "=r"(r) : "r"(w), "n"(sel));
+    return static_cast<int>(r);
+}
+
 // Q3_K {hmask[32], qs[64], scales[12], d}: half H = qs[32H..]; run J = 2s+lh,
 // code = 2-bit field (shift 2s of qs[32H + 16lh + l]) + 4 * bit (4H+s) of
-// hmask[16lh + l]; value = d * (6-bit scale - 32) * (code - 4).  The code is
-// assembled in place at bit p = min(2s, 4) (x2^p), the scale multiplied by
-// 2^(4-p): |HS| <= 16 * 32*16 * 16*7*127 < 1.2e8; |MS| <= 16*32*16*32385.
+// hmask[16lh + l]; value = d * (6-bit scale - 32) * (code - 4).  Once per
+// half CG, each qs word w and hmask word hm become two words holding the
+// 3-bit codes of two sub-blocks per byte: a = codes of s = 0 (bits 0-2) and
+// s = 2 (bits 4-6), b = codes of s = 1 and s = 3 (bits 3 and 7 are don't-care),
+// so a run is one mask.  Scales are kept as 4 * (scale - 32) in signed bytes;
+// codes at bit 4 (x16) take scale 4m, codes at bit 0 take 64m:
+// |HS|, |LS| <= 8 * 2048 * 16*7*127 < 2.4e8; |MS| <= 8 * 128 * 16*32385.
 template <int H, int AL> struct RowQ3K {
     static constexpr int RL = 16;
-    uint32_t hd, sv[2], hm[8], w[8];  // sv: the half's eight 6-bit scales, one per byte
+    uint32_t hd, sv[2], a[8], b[8];  // sv: 4 * (scale - 32) of the half's eight runs, one signed byte each
     __device__ __forceinline__ void load(const uint8_t* cg) {
-        uint32_t h[1], s12[3];
+        uint32_t h[1], s12[3], hm[8], w[8];
         ld_words<1>(cg + 108, h);
         hd = h[0];
         ld_words<3>(cg + 96, s12);
         // scale IS = 8H + J: low 4 bits from nibble H of byte (IS & 7) of the
         // first 8 scale bytes, high 2 bits from bits 2*(IS >> 2) of byte 8 + (IS & 3)
+        uint32_t s6[2];
         if constexpr (H == 0) {
-            sv[0] = (s12[0] & 0x0F0F0F0Fu) | ((s12[2] << 4) & 0x30303030u);
-            sv[1] = (s12[1] & 0x0F0F0F0Fu) | ((s12[2] << 2) & 0x30303030u);
+            s6[0] = (s12[0] & 0x0F0F0F0Fu) | ((s12[2] << 4) & 0x30303030u);
+            s6[1] = (s12[1] & 0x0F0F0F0Fu) | ((s12[2] << 2) & 0x30303030u);
         } else {
-            sv[0] = ((s12[0] >> 4) & 0x0F0F0F0Fu) | (s12[2] & 0x30303030u);
-            sv[1] = ((s12[1] >> 4) & 0x0F0F0F0Fu) | ((s12[2] >> 2) & 0x30303030u);
+            s6[0] = ((s12[0] >> 4) & 0x0F0F0F0Fu) | (s12[2] & 0x30303030u);
+            s6[1] = ((s12[1] >> 4) & 0x0F0F0F0Fu) | ((s12[2] >> 2) & 0x30303030u);
         }
+        // v - 32 for a 6-bit v is v ^ 32 read as a signed 6-bit number; shifted
+        // to the top of its byte it is 4 * (v - 32) as a signed byte
+#pragma unroll
+        for (int i = 0; i < 2; ++i) sv[i] = (s6[i] ^ 0x20202020u) << 2;
         ld_words<8>(cg, hm);
         ld_words<8>(cg + 32 + 32 * H, w);
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+            // high bit of s = 0 / 2 (bits 4H, 4H+2 of each hmask byte) to bits 2 / 6
+            a[v] = bsel(0x33333333u, w[v], bsel(0x0F0F0F0Fu, shl<2 - 4 * H>(hm[v]), shl<4 - 4 * H>(hm[v])));
+            // s = 1 / 3: fields at bits 2-3 / 6-7 moved down by 2; high bits 4H+1, 4H+3
+            b[v] = bsel(0x33333333u, w[v] >> 2, bsel(0x0F0F0F0Fu, shl<1 - 4 * H>(hm[v]), shl<3 - 4 * H>(hm[v])));
+        }
     }
     template <int J>
     __device__ __forceinline__ void run(uint32_t* q, int& sc, int& m) const {
         constexpr int s = J >> 1, lh = J & 1;
-        constexpr int PB = (2 * s < 4) ? 2 * s : 4;  // in-place bit of the 2-bit field
-        constexpr int WS = 2 * s - PB;               // right shift of the qs word
-        constexpr int HSH = (PB + 2) - (4 * H + s);  // left shift of the hmask word
+        constexpr uint32_t MASK = (s >= 2) ? 0x70707070u : 0x07070707u;
 #pragma unroll
-        for (int v = 0; v < 4; ++v)
-            q[v] = ((w[4 * lh + v] >> WS) & (0x03030303u << PB)) | (shl<HSH>(hm[4 * lh + v]) & (0x04040404u << PB));
-        m = static_cast<int>(__byte_perm(sv[J >> 2], 0u, 0x4440u | (J & 3))) - 32;
-        sc = m * (1 << (4 - PB));
+        for (int v = 0; v < 4; ++v) q[v] = ((s & 1) ? b[4 * lh + v] : a[4 * lh + v]) & MASK;
+        m = sext_byte<J & 3>(sv[J >> 2]);  // 4 * (scale - 32)
+        sc = (s < 2) ? (m << 4) : m;
     }
-    __device__ __forceinline__ float dscale() const { return h2f_ref(hd & 0xFFFFu) * 0.0625f; }
-    __device__ __forceinline__ float mscale() const { return h2f_ref(hd & 0xFFFFu) * 4.0f; }
+    __device__ __forceinline__ float dscale() const { return h2f_ref(hd & 0xFFFFu) * (1.0f / 64.0f); }
+    __device__ __forceinline__ float mscale() const { return h2f_ref(hd & 0xFFFFu); }
 };
 
 // Q4_K {d, dmin, scales[12], qs[128]}: group G = 4H + J covers nibble G&1 of
