@@ -123,7 +123,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("ranks", [2])
+@pytest.mark.parametrize("ranks", [2, 4, 8])
 def test_multi_gpu_sharded_parity(cuda, tmp_path, ranks):
     import torch
     if torch.cuda.device_count() < ranks:
