@@ -524,25 +524,37 @@ template <int F> struct Lane {
 __global__ void act_prep_kernel(const float* __restrict__ x, int64_t K, int64_t ntok, int x_tokmajor, int perm,
                                 int64_t nch, uint8_t* __restrict__ rec, int* __restrict__ err) {
     const int lane = threadIdx.x & 31;
-    // x may come from the previous kernel; only after it has finished may the
-    // matmul kernel (launched early) start streaming weights.
-    pdl_wait();
+    // The matmul kernel may launch at once: it streams weights (complete
+    // before this call) and reads the records only after this grid is done.
+    // x may come from the previous kernel, so it is read after pdl_wait.
     pdl_launch_dependents();
+    pdl_wait();
     if (blockIdx.x == 0 && threadIdx.x == 0) *err = 0;  // status word of this call
     const int64_t wid = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (wid >= nch * ntok) return;
     const int64_t ch = wid / ntok, tok = wid - ch * ntok;
     float v[8];
     float amax = 0.0f;
+    const int64_t k0 = ch * 256 + 32 * (lane >> 2) + 8 * (lane & 3);  // first element of the lane's 8
+    const float* xt = x + tok * K + k0;
+    if (x_tokmajor && !perm && k0 + 8 <= K && (reinterpret_cast<uintptr_t>(xt) & 15) == 0) {
+        // the lane's 8 consecutive elements as two 16-byte loads
+        const float4 a = *reinterpret_cast<const float4*>(xt);
+        const float4 b = *reinterpret_cast<const float4*>(xt + 4);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const int p = 8 * (lane & 3) + i;  // position within the 32-block
-        const int e = perm ? ((p < 16) ? 2 * p : 2 * (p - 16) + 1) : p;
-        const int64_t k = ch * 256 + 32 * (lane >> 2) + e;
-        v[i] = 0.0f;
-        if (k < K) v[i] = x_tokmajor ? x[tok * K + k] : x[k * ntok + tok];
-        amax = fmaxf(amax, fabsf(v[i]));
+        for (int i = 0; i < 8; ++i) {
+            const int p = 8 * (lane & 3) + i;  // position within the 32-block
+            const int e = perm ? ((p < 16) ? 2 * p : 2 * (p - 16) + 1) : p;
+            const int64_t k = ch * 256 + 32 * (lane >> 2) + e;
+            v[i] = 0.0f;
+            if (k < K) v[i] = x_tokmajor ? x[tok * K + k] : x[k * ntok + tok];
+        }
     }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     float u = 0.0f;
@@ -551,11 +563,15 @@ __global__ void act_prep_kernel(const float* __restrict__ x, int64_t K, int64_t 
     if (amax > 0.0f && amax <= 3.0e38f) {
         u = amax * (1.0f / 32258.0f);  // 127 * 254
         const float shi = u * 254.0f;
+        // reciprocals instead of divisions: the product is within an ulp or
+        // so of the quotient, which can flip hi only at a rounding tie; the
+        // remainder then exceeds shi/2 by that much and lo (clamped) absorbs it
+        const float rshi = 1.0f / shi, ru = 1.0f / u;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            const int hi = max(-127, min(127, __float2int_rn(v[i] / shi)));
+            const int hi = max(-127, min(127, __float2int_rn(v[i] * rshi)));
             const float r = fmaf(-static_cast<float>(hi), shi, v[i]);
-            const int lo = max(-127, min(127, __float2int_rn(r / u)));
+            const int lo = max(-127, min(127, __float2int_rn(r * ru)));
             hw[i >> 2] |= (static_cast<uint32_t>(hi) & 0xFFu) << (8 * (i & 3));
             lw[i >> 2] |= (static_cast<uint32_t>(lo) & 0xFFu) << (8 * (i & 3));
             s += 254 * hi + lo;
@@ -688,6 +704,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
             __syncwarp();
             polled = true;
         };
+        const uint64_t wpol = l2_evict_first_policy();  // weights are read once
         int s = 0, pass = 0;  // ring slot and how many times the ring was filled
         for (int64_t u = blockIdx.x; u < a.units; u += gridDim.x) {
             for (int ks = 0; ks < a.nks; ++ks) {
@@ -731,7 +748,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
                     else mbar_arrive(&full[s]);
                 }
                 __syncwarp();
-                if (bulk) bulk_g2s(st + lane * a.rs, reinterpret_cast<const void*>(lo), my_tx, &full[s]);
+                if (bulk) bulk_g2s_hint(st + lane * a.rs, reinterpret_cast<const void*>(lo), my_tx, &full[s], wpol);
                 if (++s == a.nstages) {
                     s = 0;
                     ++pass;
