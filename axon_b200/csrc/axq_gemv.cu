@@ -616,7 +616,7 @@ struct GemvArgs {
     unsigned* const* peer_comp;
     unsigned* done;  // finished-CTA count of this grid (reset by the last CTA)
     // entry handshake: the last CTA adds 1 to every rank's entry counter
-    // peer_entry[g] as the grid starts; before its first peer store each CTA
+    // peer_entry[g] once the call's inputs are ready; before its first peer store each CTA
     // waits until every rank has entered this call (*my_entry >= (*epoch + 1)
     // * npeers), so no rank overwrites a copy its owner may still be reading.
     // Counters are sums over ranks: a rank enters call e + 1 only after its
@@ -659,8 +659,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
     uint8_t* stages = smem + kHeaderBytes + ((2 * kConsumerWarps * kUnitRows * NT * 4 + 127) / 128) * 128;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    // The weights were complete before the activation prep started; only the
-    // consumers read its records, after pdl_wait below.
+    // The next kernel may launch at once: every kernel of this library waits
+    // for its predecessor (pdl_wait) before it touches what that one writes.
     pdl_launch_dependents();
     if (tid == 0) {
         for (int s = 0; s < kMaxStages; ++s) {
@@ -677,15 +677,11 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
 
     if (warp == kConsumerWarps) {
         // ---------------- producer warp: lane r copies row r of each stage ----
-        // Peer-store calls: the entry signal comes from the last CTA (one with
-        // the fewest units), and every CTA's producer waits for the other
-        // ranks' entry before its first wait for a free slot (consumers never
-        // hold it up), handing the result to the consumers in entry_flag.
-        // This grid started after every earlier kernel of the stream
-        // completed (the activation prep waited for them before it let this
-        // grid launch), so this rank's reads of the old output are done.
-        if (a.npeers > 0 && lane == 0 && blockIdx.x == gridDim.x - 1)
-            for (int g = 0; g < a.npeers; ++g) red_add_sys_u32(a.peer_entry[g], 1u);
+        // The weights were complete before this call was enqueued (no kernel
+        // of this library writes them), so streaming starts at once.
+        // Peer-store calls: every CTA's producer waits for the other ranks'
+        // entry before its first wait for a free slot (consumers never hold
+        // it up) and hands the result to the consumers in entry_flag.
         bool polled = (a.npeers == 0);
         auto poll_entry = [&]() {
             if (lane == 0) {
@@ -764,6 +760,12 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
     // takes CG 4(w%4) + l/8 for rows l%8 and l%8 + 8 of the unit, so every
     // activation run it loads serves two rows.
     pdl_wait();  // activation records of this call are complete
+    // Peer-store calls: every earlier kernel of the stream has completed now
+    // (the activation prep waited for its predecessor before finishing), so
+    // this rank's reads of the old output are done: the last CTA (one with
+    // the fewest units) counts this rank as entered at every rank.
+    if (a.npeers > 0 && tid == 0 && blockIdx.x == gridDim.x - 1)
+        for (int g = 0; g < a.npeers; ++g) red_add_sys_u32(a.peer_entry[g], 1u);
     const int h = warp >> 2;
     const int cgl = 4 * (warp & 3) + (lane >> 3);  // CG slot in the stage
     const int pr = lane & 7;                        // rows pr and pr + 8 of the unit
