@@ -166,48 +166,67 @@ __device__ __forceinline__ void ldg_w(const uint8_t* p, uint32_t* out) {
     }
 }
 
-template <int I>
-__device__ __forceinline__ uint32_t byte_i(const uint32_t* w) { return (w[I >> 2] >> (8 * (I & 3))) & 0xFFu; }
+// fp16 bits -> float with subnormals flushed to (signed) zero, as the
+// reference's decoder does (a scale that decodes to zero must give exact
+// zeros); normal, infinite and NaN values convert as the hardware does.
+__device__ __forceinline__ float h2f_flush(uint32_t h) {
+    return (h & 0x7C00u) ? __half2float(__ushort_as_half(static_cast<unsigned short>(h & 0xFFFFu)))
+                         : __uint_as_float((h & 0x8000u) << 16);
+}
 
-template <int G>
-__device__ __forceinline__ void k4_sm(const uint32_t* hw, int& sc, int& m) {
-    if constexpr (G < 4) {
-        sc = byte_i<4 + G>(hw) & 63;
-        m = byte_i<8 + G>(hw) & 63;
+// Byte j (0..7, run time) of the little-endian pair (lo, hi).
+__device__ __forceinline__ uint32_t byte_rt(uint32_t lo, uint32_t hi, int j) {
+    return prmt(lo, hi, static_cast<uint32_t>(j)) & 0xFFu;
+}
+
+// get_scale_min_k4 (cpu_backend.cpp:681-689) for a run-time sub-block g of
+// the 12 scale bytes q0|q1|q2.
+__device__ __forceinline__ void k4_sm_rt(uint32_t q0, uint32_t q1, uint32_t q2, int g, int& sc, int& m) {
+    const uint32_t a = byte_rt(q0, q1, g);      // q[g]
+    const uint32_t b = byte_rt(q1, q2, g);      // q[g + 4]
+    if (g < 4) {
+        sc = static_cast<int>(a & 63);
+        m = static_cast<int>(b & 63);
     } else {
-        sc = (byte_i<8 + G>(hw) & 0xF) | ((byte_i<G>(hw) >> 6) << 4);
-        m = (byte_i<8 + G>(hw) >> 4) | ((byte_i<4 + G>(hw) >> 6) << 4);
+        const uint32_t c = byte_rt(q0, q0, g & 3);  // q[g - 4]
+        sc = static_cast<int>((b & 0xF) | ((c >> 6) << 4));
+        m = static_cast<int>((b >> 4) | ((a >> 6) << 4));
     }
 }
 
-// Dq<F>::kstep<KS, A>(row, out, H): half H (0/1, warp-uniform at run time)
-// of K-step KS (elements 64KS..64KS+63 of the column group at `row`, shared
-// memory with alignment A) into out[4] = fp16 chunks 4H..4H+3 of that
-// K-step.  Every format splits a K-step into two halves that share no scale
-// (nibble, 2-bit shift, or block); H selects with register shifts and
-// selects, not branches, so all dequant warps run the same code.
+// Dq<F>: header<AL>(cg) decodes what a column group's K-steps share (fp16
+// scales, scale bytes) once; kstep<AL>(cg, hdr, out, H, KS) writes half H
+// (0/1) of K-step KS (elements 64KS..64KS+63 of the column group, both run
+// time) as out[4] = fp16 chunks 4H..4H+3 of that K-step.  Every format
+// splits a K-step into two halves that share no scale (nibble, 2-bit shift,
+// or block).  One loop body serves all four K-steps (run-time KS keeps the
+// kernel's code small enough for the instruction cache).  `cg` is shared
+// memory with alignment AL.
 template <int F> struct Dq;
 
 __device__ __forceinline__ uint32_t sel(int h, uint32_t a, uint32_t b) { return h ? b : a; }
 
+// Q4_K {d, dmin, scales[12], qs[128]}: K-step KS = qs[32KS..+31], low
+// nibbles sub-block 2KS, high nibbles 2KS+1.
 template <> struct Dq<F_Q4_K> {
     static constexpr int A = 16;
-    template <int KS, int AL>
-    __device__ static void kstep(const uint8_t* row, uint4* out, int H) {
-        uint32_t hw[4], w[8];
+    struct Hdr {
+        float d, mn;
+        uint32_t q0, q1, q2;
+    };
+    template <int AL>
+    __device__ static Hdr header(const uint8_t* row) {
+        uint32_t hw[4];
         ldg_w<4, AL>(row, hw);
+        return Hdr{h2f_flush(hw[0]), h2f_flush(hw[0] >> 16), hw[1], hw[2], hw[3]};
+    }
+    template <int AL>
+    __device__ static void kstep(const uint8_t* row, const Hdr& hd, uint4* out, int H, int KS) {
+        uint32_t w[8];
         ldg_w<8, AL>(row + 16 + 32 * KS, w);
-        const float d = h2f_ref(hw[0] & 0xFFFFu), mn = h2f_ref(hw[0] >> 16);
         int sc, m;
-        if constexpr (KS < 2) {  // group 2KS+H < 4
-            sc = sel(H, byte_i<4 + 2 * KS>(hw), byte_i<5 + 2 * KS>(hw)) & 63;
-            m = sel(H, byte_i<8 + 2 * KS>(hw), byte_i<9 + 2 * KS>(hw)) & 63;
-        } else {
-            const uint32_t b8 = sel(H, byte_i<8 + 2 * KS>(hw), byte_i<9 + 2 * KS>(hw));
-            sc = (b8 & 0xF) | ((sel(H, byte_i<2 * KS>(hw), byte_i<2 * KS + 1>(hw)) >> 6) << 4);
-            m = (b8 >> 4) | ((sel(H, byte_i<4 + 2 * KS>(hw), byte_i<5 + 2 * KS>(hw)) >> 6) << 4);
-        }
-        const Sm g = scale_min(d * sc, mn * m);
+        k4_sm_rt(hd.q0, hd.q1, hd.q2, 2 * KS + H, sc, m);
+        const Sm g = scale_min(hd.d * sc, hd.mn * m);
         const uint32_t sh = 4 * H;
 #pragma unroll
         for (int c = 0; c < 4; ++c)
@@ -215,26 +234,25 @@ template <> struct Dq<F_Q4_K> {
     }
 };
 
+// Q5_K {d, dmin, scales[12], qh[32], qs[128]}: as Q4_K plus bit g of qh[l]
+// as bit 4 of the code of sub-block g.
 template <> struct Dq<F_Q5_K> {
     static constexpr int A = 16;
-    template <int KS, int AL>
-    __device__ static void kstep(const uint8_t* row, uint4* out, int H) {
-        uint32_t hw[4], w[8], qh[8];
-        ldg_w<4, AL>(row, hw);
+    using Hdr = Dq<F_Q4_K>::Hdr;
+    template <int AL>
+    __device__ static Hdr header(const uint8_t* row) {
+        return Dq<F_Q4_K>::header<AL>(row);
+    }
+    template <int AL>
+    __device__ static void kstep(const uint8_t* row, const Hdr& hd, uint4* out, int H, int KS) {
+        uint32_t w[8], qh[8];
         ldg_w<8, AL>(row + 48 + 32 * KS, w);
         ldg_w<8, AL>(row + 16, qh);
-        const float d = h2f_ref(hw[0] & 0xFFFFu), mn = h2f_ref(hw[0] >> 16);
+        const int g = 2 * KS + H;
         int sc, m;
-        if constexpr (KS < 2) {
-            sc = sel(H, byte_i<4 + 2 * KS>(hw), byte_i<5 + 2 * KS>(hw)) & 63;
-            m = sel(H, byte_i<8 + 2 * KS>(hw), byte_i<9 + 2 * KS>(hw)) & 63;
-        } else {
-            const uint32_t b8 = sel(H, byte_i<8 + 2 * KS>(hw), byte_i<9 + 2 * KS>(hw));
-            sc = (b8 & 0xF) | ((sel(H, byte_i<2 * KS>(hw), byte_i<2 * KS + 1>(hw)) >> 6) << 4);
-            m = (b8 >> 4) | ((sel(H, byte_i<4 + 2 * KS>(hw), byte_i<5 + 2 * KS>(hw)) >> 6) << 4);
-        }
-        const Sm s = scale_min(d * sc, mn * m);
-        const uint32_t sh = 4 * H, g = 2 * KS + H;
+        k4_sm_rt(hd.q0, hd.q1, hd.q2, g, sc, m);
+        const Sm s = scale_min(hd.d * sc, hd.mn * m);
+        const uint32_t sh = 4 * H;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
             uint32_t cw[2];
@@ -246,23 +264,30 @@ template <> struct Dq<F_Q5_K> {
     }
 };
 
+// Q2_K {d, dmin, scales[16], qs[64]}: K-step KS = half n = KS/2 of the
+// block, 2-bit fields s = 2(KS%2) + H of qs[32n..+31]; sub-block 8n + 2s + lh
+// for the first / second 16 elements (lh).
 template <> struct Dq<F_Q2_K> {
     static constexpr int A = 4;
-    template <int KS, int AL>
-    __device__ static void kstep(const uint8_t* row, uint4* out, int H) {
-        constexpr int n = KS >> 1, s0 = 2 * (KS & 1);
-        uint32_t hd[1], sc[2], w[8];
+    struct Hdr {
+        float d, mn;
+    };
+    template <int AL>
+    __device__ static Hdr header(const uint8_t* row) {
+        uint32_t hd[1];
         ldg_w<1, AL>(row, hd);
+        return Hdr{h2f_flush(hd[0]), h2f_flush(hd[0] >> 16)};
+    }
+    template <int AL>
+    __device__ static void kstep(const uint8_t* row, const Hdr& hd, uint4* out, int H, int KS) {
+        const int n = KS >> 1, s = 2 * (KS & 1) + H;
+        uint32_t sc[2], w[8];
         ldg_w<2, AL>(row + 4 + 8 * n, sc);
         ldg_w<8, AL>(row + 20 + 32 * n, w);
-        const float d = h2f_ref(hd[0] & 0xFFFFu), mn = h2f_ref(hd[0] >> 16);
-        const uint32_t s = s0 + H;
 #pragma unroll
         for (int lh = 0; lh < 2; ++lh) {
-            // scale byte of sub-block 8n + 2s + lh (bytes 2s0+lh or 2s0+2+lh)
-            const uint32_t b = sel(H, (sc[(2 * s0 + lh) >> 2] >> (8 * ((2 * s0 + lh) & 3))) & 0xFFu,
-                                   (sc[(2 * s0 + 2 + lh) >> 2] >> (8 * ((2 * s0 + 2 + lh) & 3))) & 0xFFu);
-            const Sm g = scale_min(d * static_cast<float>(b & 0xF), mn * static_cast<float>(b >> 4));
+            const uint32_t b = byte_rt(sc[0], sc[1], 2 * s + lh);
+            const Sm g = scale_min(hd.d * static_cast<float>(b & 0xF), hd.mn * static_cast<float>(b >> 4));
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
                 const int wi = 4 * lh + 2 * c;
@@ -273,31 +298,36 @@ template <> struct Dq<F_Q2_K> {
     }
 };
 
+// Q3_K {hmask[32], qs[64], scales[12], d}: K-step KS = half n = KS/2, field
+// s = 2(KS%2) + H of qs[32 + 32n..], high bit 4n + s of hmask; sub-block
+// IS = 8n + 2s + lh with scale (6 bits) - 32; value = D * (code - 4).
 template <> struct Dq<F_Q3_K> {
     static constexpr int A = 1;
-    template <int IS>
-    __device__ static float subscale(const uint32_t* s12, float d) {
-        constexpr int lo_byte = (IS < 8) ? IS : IS - 8, lo_sh = (IS < 8) ? 0 : 4;
-        const int lo4 = (s12[lo_byte >> 2] >> (8 * (lo_byte & 3) + lo_sh)) & 0xF;
-        const int hi2 = (s12[2] >> (8 * (IS & 3) + 2 * (IS >> 2))) & 3;
-        return d * static_cast<float>((lo4 | (hi2 << 4)) - 32);
-    }
-    template <int KS, int AL>
-    __device__ static void kstep(const uint8_t* row, uint4* out, int H) {
-        constexpr int n = KS >> 1, s0 = 2 * (KS & 1);
-        uint32_t hd[1], s12[3], w[8], hm[8];
+    struct Hdr {
+        float d;
+        uint32_t s0, s1, s2;
+    };
+    template <int AL>
+    __device__ static Hdr header(const uint8_t* row) {
+        uint32_t hd[1], s12[3];
         ld_words<1>(row + 108, hd);
         ld_words<3>(row + 96, s12);
+        return Hdr{h2f_flush(hd[0]), s12[0], s12[1], s12[2]};
+    }
+    __device__ static float subscale(const Hdr& hd, int IS) {
+        const uint32_t lo4 = (byte_rt(hd.s0, hd.s1, IS & 7) >> (4 * (IS >> 3))) & 0xFu;
+        const uint32_t hi2 = (hd.s2 >> (8 * (IS & 3) + 2 * (IS >> 2))) & 3u;
+        return hd.d * static_cast<float>(static_cast<int>(lo4 | (hi2 << 4)) - 32);
+    }
+    template <int AL>
+    __device__ static void kstep(const uint8_t* row, const Hdr& hd, uint4* out, int H, int KS) {
+        const int n = KS >> 1, s = 2 * (KS & 1) + H, hb = 4 * n + s;
+        uint32_t w[8], hm[8];
         ld_words<8>(row + 32 + 32 * n, w);
         ld_words<8>(row, hm);
-        const float d = h2f_ref(hd[0] & 0xFFFFu);
-        const float D0 = H ? subscale<8 * n + 2 * s0 + 2>(s12, d) : subscale<8 * n + 2 * s0>(s12, d);
-        const float D1 = H ? subscale<8 * n + 2 * s0 + 3>(s12, d) : subscale<8 * n + 2 * s0 + 1>(s12, d);
-        const Sm g0 = scale_off(D0, 4.0f), g1 = scale_off(D1, 4.0f);
-        const uint32_t s = s0 + H, hb = 4 * n + s;
 #pragma unroll
         for (int lh = 0; lh < 2; ++lh) {
-            const Sm& g = lh ? g1 : g0;
+            const Sm g = scale_off(subscale(hd, 8 * n + 2 * s + lh), 4.0f);
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
                 const int wi = 4 * lh + 2 * c;
@@ -309,30 +339,40 @@ template <> struct Dq<F_Q3_K> {
     }
 };
 
+// Q6_K {ql[128], qh[64], scales[16] (int8), d}: K-step KS = half n = KS/2,
+// nibble KS%2 of ql[64n + 32H..], 2-bit field t = 2(KS%2) + H of
+// qh[32n..]; sub-block 8n + 2t + lh; value = d * scale * (code - 32).
 template <> struct Dq<F_Q6_K> {
     static constexpr int A = 1;
-    template <int KS, int AL>
-    __device__ static void kstep(const uint8_t* row, uint4* out, int H) {
-        constexpr int n = KS >> 1, hi_nib = KS & 1;  // t = 2*(KS&1) + H
-        uint32_t hd[1], sc[4], qh[8], ql[8];
+    struct Hdr {
+        float d;
+        uint32_t sc[4];
+    };
+    template <int AL>
+    __device__ static Hdr header(const uint8_t* row) {
+        uint32_t hd[1];
+        Hdr r;
         ld_words<1>(row + 208, hd);
-        ld_words<4>(row + 192, sc);
+        ld_words<4>(row + 192, r.sc);
+        r.d = h2f_flush(hd[0]);
+        return r;
+    }
+    template <int AL>
+    __device__ static void kstep(const uint8_t* row, const Hdr& hd, uint4* out, int H, int KS) {
+        const int n = KS >> 1, hi_nib = KS & 1, t = 2 * hi_nib + H;
+        uint32_t qh[8], ql[8];
         ld_words<8>(row + 128 + 32 * n, qh);
         ld_words<8>(row + 64 * n + 32 * H, ql);
-        const float d = h2f_ref(hd[0] & 0xFFFFu);
-        const uint32_t t = 2 * hi_nib + H;
+        const uint32_t sa = sel(n, hd.sc[0], hd.sc[2]), sb = sel(n, hd.sc[1], hd.sc[3]);
 #pragma unroll
         for (int lh = 0; lh < 2; ++lh) {
-            constexpr int jb = 8 * n + 4 * hi_nib;  // sub-block 8n + 2t + lh
-            const uint32_t sb = sel(H, (sc[(jb + lh) >> 2] >> (8 * ((jb + lh) & 3))) & 0xFFu,
-                                    (sc[(jb + 2 + lh) >> 2] >> (8 * ((jb + 2 + lh) & 3))) & 0xFFu);
-            const float Dv = d * static_cast<float>(static_cast<int8_t>(sb));
-            const Sm g = scale_off(Dv, 32.0f);
+            const uint32_t b = byte_rt(sa, sb, 2 * t + lh);
+            const Sm g = scale_off(hd.d * static_cast<float>(static_cast<int8_t>(b)), 32.0f);
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
                 const int wi = 4 * lh + 2 * c;
-                const uint32_t n0 = (hi_nib ? (ql[wi] >> 4) : ql[wi]) & 0x0F0F0F0Fu;
-                const uint32_t n1 = (hi_nib ? (ql[wi + 1] >> 4) : ql[wi + 1]) & 0x0F0F0F0Fu;
+                const uint32_t n0 = (ql[wi] >> (4 * hi_nib)) & 0x0F0F0F0Fu;
+                const uint32_t n1 = (ql[wi + 1] >> (4 * hi_nib)) & 0x0F0F0F0Fu;
                 const uint32_t c0 = n0 | (((qh[wi] >> (2 * t)) & 0x03030303u) << 4);
                 const uint32_t c1 = n1 | (((qh[wi + 1] >> (2 * t)) & 0x03030303u) << 4);
                 out[2 * lh + c] = chunk8(c0, c1, g.sub, g.D, g.Mneg);
@@ -344,13 +384,16 @@ template <> struct Dq<F_Q6_K> {
 // Q8_0: half H = block 2KS+H of the column group; signed codes biased by 128.
 template <> struct Dq<F_Q8_0> {
     static constexpr int A = 1;
-    template <int KS, int AL>
-    __device__ static void kstep(const uint8_t* row, uint4* out, int H) {
+    struct Hdr {};
+    template <int AL>
+    __device__ static Hdr header(const uint8_t*) { return Hdr{}; }
+    template <int AL>
+    __device__ static void kstep(const uint8_t* row, const Hdr&, uint4* out, int H, int KS) {
         const uint8_t* blk = row + 34 * (2 * KS + H);
         uint32_t hd[1], w[8];
         ld_words<1>(blk, hd);
         ld_words<8>(blk + 2, w);
-        const Sm g = scale_off(h2f_ref(hd[0] & 0xFFFFu), 128.0f);
+        const Sm g = scale_off(h2f_flush(hd[0]), 128.0f);
 #pragma unroll
         for (int c = 0; c < 4; ++c)
             out[c] = chunk8(w[2 * c] ^ 0x80808080u, w[2 * c + 1] ^ 0x80808080u, g.sub, g.D, g.Mneg);
@@ -360,13 +403,16 @@ template <> struct Dq<F_Q8_0> {
 // Q4_0: half H = block 2KS+H; byte i holds elements 2i (low) and 2i+1 (high).
 template <> struct Dq<F_Q4_0> {
     static constexpr int A = 1;
-    template <int KS, int AL>
-    __device__ static void kstep(const uint8_t* row, uint4* out, int H) {
+    struct Hdr {};
+    template <int AL>
+    __device__ static Hdr header(const uint8_t*) { return Hdr{}; }
+    template <int AL>
+    __device__ static void kstep(const uint8_t* row, const Hdr&, uint4* out, int H, int KS) {
         const uint8_t* blk = row + 18 * (2 * KS + H);
         uint32_t hd[1], w[4];
         ld_words<1>(blk, hd);
         ld_words<4>(blk + 2, w);
-        const Sm g = scale_off(h2f_ref(hd[0] & 0xFFFFu), 8.0f);
+        const Sm g = scale_off(h2f_flush(hd[0]), 8.0f);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
             const uint32_t lo = w[c] & 0x0F0F0F0Fu, hi = (w[c] >> 4) & 0x0F0F0F0Fu;
@@ -526,15 +572,14 @@ __global__ void __launch_bounds__(kThreadsGemm, 2) gemm_kernel(GemmArgs a) {
             const uintptr_t ga = wbase + static_cast<uintptr_t>(row * a.rb + static_cast<int64_t>(cg) * C::BYTES);
             const uint8_t* rowp = pk_ring + p * a.pk_bytes + r * a.rs + (ga & 15);
             const bool tail = (static_cast<int64_t>(cg + 1) * 256 > a.K) || ((cg + 1) * C::BLK > a.nblk_row);
-#pragma unroll
+            typename Dq<F>::Hdr hdr{};
+            if (row_ok) hdr = Dq<F>::template header<AL>(rowp);
+#pragma unroll 1
             for (int k = 0; k < kKStepsPerCG; ++k) {
                 if (pass > 0 && !gwait(&bars->ab_empty[s], (pass - 1) & 1, abort_flag, a.err)) break;
                 uint4 o[4];
                 if (row_ok) {
-                    if (k == 0) Dq<F>::template kstep<0, AL>(rowp, o, h);
-                    else if (k == 1) Dq<F>::template kstep<1, AL>(rowp, o, h);
-                    else if (k == 2) Dq<F>::template kstep<2, AL>(rowp, o, h);
-                    else Dq<F>::template kstep<3, AL>(rowp, o, h);
+                    Dq<F>::template kstep<AL>(rowp, hdr, o, h, k);
                     if (tail) {
                         // zero the elements past K (and blocks past the row's end)
 #pragma unroll
