@@ -110,8 +110,10 @@ __device__ __forceinline__ float xsub(float a, float b) { return x86_nan(__fsub_
 // Little-endian 16-bit read from a byte pointer with any alignment.
 __device__ __forceinline__ uint32_t ld_u16(const uint8_t* p) { return p[0] | (static_cast<uint32_t>(p[1]) << 8); }
 
-// Bounded spin limit for mbarrier waits (iterations of try_wait, each of
-// which already suspends for a hardware-defined interval).
-constexpr uint32_t kSpinLimit = 1u << 26;
+// mbarrier waits: each try suspends the thread for up to kSuspendNs (it is
+// woken when the phase completes); a wait gives up after kWaitLimitNs of
+// global time and the caller reports an error status.
+constexpr uint32_t kSuspendNs = 20000;
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
 }  // namespace axq

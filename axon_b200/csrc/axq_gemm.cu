@@ -80,12 +80,11 @@ struct Bars {
 };
 
 __device__ __forceinline__ bool gwait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err) {
-    for (uint32_t i = 0; i < kSpinLimit; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if (*abort_flag) return false;
+    if (mbar_wait_bounded(bar, parity, abort_flag)) return true;
+    if (!*abort_flag) {  // this thread's wait ran out: stop the other roles
+        *abort_flag = 1;
+        atomicExch(err, 1);
     }
-    *abort_flag = 1;
-    atomicExch(err, 1);
     return false;
 }
 

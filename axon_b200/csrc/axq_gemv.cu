@@ -630,11 +630,7 @@ struct GemvArgs {
 };
 
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
-    for (uint32_t i = 0; i < kSpinLimit; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if (*abort_flag) return false;
-    }
-    return false;
+    return mbar_wait_bounded(bar, parity, abort_flag);
 }
 
 // Source row and buffer of stage slot `slot` of unit u.

@@ -42,12 +42,41 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Waits for the phase with the given parity to complete; gives up after
-// kSpinLimit polls and returns false (the caller reports an error status).
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
-    for (uint32_t i = 0; i < kSpinLimit; ++i)
-        if (mbar_try_wait(bar, parity)) return true;
-    return false;
+// try_wait that may suspend the thread for up to `ns` nanoseconds; the
+// thread resumes as soon as the phase completes.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+        : "memory");
+    return ok != 0;
+}
+
+// Global nanosecond timer.
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Waits for the phase with the given parity to complete.  Returns false if
+// *abort_flag (shared memory, may be null) becomes set or kWaitLimitNs pass;
+// the caller then reports an error status.  Waiting threads sleep in
+// try_wait instead of polling, so they take no issue slots from the warps
+// doing the work.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  const volatile int* abort_flag = nullptr) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+        if (mbar_try_wait_sleep(bar, parity, kSuspendNs)) return true;
+        if (abort_flag && *abort_flag) return false;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    }
 }
 
 // 1-D bulk copy global -> shared, completion counted on `bar` in bytes.
