@@ -248,7 +248,10 @@ def run_gpu(args):
     # in place by the matmul and the rest brought by the library's in-place
     # NCCL all-gather (axq_allgather / axq_matmul_sharded).
     comm = ax.Communicator.from_process_group() if world > 1 else None
-    ys = {f: torch.empty(M_TOK, ROWS, device=dev) for f in FORMATS}
+    # one contiguous buffer holds the three outputs, so the end-to-end step
+    # reads them back with a single copy
+    y_all = torch.empty(len(FORMATS), M_TOK, ROWS, device=dev)
+    ys = {f: y_all[i] for i, f in enumerate(FORMATS)}
     # with several ranks each output lives in a symmetric buffer: the GEMV's
     # epilogue stores every value into each rank's copy over NVLink
     symm = {f: ax.SymmetricBuffer(comm, 4 * world * ROWS * M_TOK) for f in FORMATS} if world > 1 else None
@@ -336,20 +339,28 @@ def run_gpu(args):
         fmt_ms = {f: float(t[1 + i]) for i, f in enumerate(FORMATS)}
 
     # End to end through the public API with host buffers: pinned x -> device,
-    # the three matmuls (+ all-gathers), full outputs -> pinned host.
+    # the three matmuls back to back (with several ranks: issued, then waited
+    # for), then every full output -> pinned host.  Copies sit outside the
+    # chain of matmul kernels: a copy between two kernels would stop the next
+    # one from launching while the previous one drains.
     xh = torch.randn(M_TOK, K_DIM).pin_memory()
     yh = {f: torch.empty(world * M_TOK * ROWS).pin_memory() for f in FORMATS}
+    yh_all = torch.empty(len(FORMATS) * M_TOK * ROWS).pin_memory()
     xd = torch.empty_like(x)
 
     def e2e_step():
         xd.copy_(xh, non_blocking=True)
-        for fmt in FORMATS:
-            if world > 1:
-                y = ax.matmul_sharded_p2p(symm[fmt], qs[fmt], xd, world * ROWS, b_tokmajor=True, workspace=ws)
-                yh[fmt].copy_(y.view(-1), non_blocking=True)  # after the call's wait
-            else:
+        if world > 1:
+            outs = [ax.matmul_sharded_p2p(symm[f], qs[f], xd, world * ROWS, b_tokmajor=True, workspace=ws,
+                                          wait=False) for f in FORMATS]
+            for f in FORMATS:
+                symm[f].wait()
+            for f, y in zip(FORMATS, outs):
+                yh[f].copy_(y.view(-1), non_blocking=True)
+        else:
+            for fmt in FORMATS:
                 ax.linear_q(xd, qs[fmt], out=ys[fmt], workspace=ws)
-                yh[fmt].copy_(ys[fmt].view(-1), non_blocking=True)
+            yh_all.copy_(y_all.view(-1), non_blocking=True)
 
     for _ in range(3):
         e2e_step()
@@ -402,7 +413,8 @@ def run_gpu(args):
                          "by_format": by_fmt},
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * K_DIM * M_TOK,
                     "d2h_bytes_per_step": 4 * world * M_TOK * ROWS * len(FORMATS)},
-            "gpu_launches": 2 * len(FORMATS) * args.steps,
+            # per matmul: activation prep + GEMV (+ the peer wait with several ranks)
+            "gpu_launches": (3 if world > 1 else 2) * len(FORMATS) * args.steps,
             "clocks": clocks,
         }
         if cpu is not None:
