@@ -158,13 +158,7 @@ __global__ void peer_wait_kernel(const unsigned* comp, unsigned* epoch, int nran
     // this rank's wait for call e is over, so the sum reaches e * nranks only
     // once every rank has signalled call e
     const unsigned target = e * static_cast<unsigned>(nranks);
-    uint32_t spins = 0;
-    while (static_cast<int>(ld_acquire_sys_u32(comp) - target) < 0) {
-        if (++spins > (1u << 23)) {  // a second or two of polling
-            atomicExch(err, 1);
-            break;
-        }
-    }
+    if (!poll_counter_sys(comp, target, kPeerWaitNs)) atomicExch(err, 1);  // a rank never signalled
     *epoch = e;
 }
 

@@ -115,5 +115,7 @@ __device__ __forceinline__ uint32_t ld_u16(const uint8_t* p) { return p[0] | (st
 // global time and the caller reports an error status.
 constexpr uint32_t kSuspendNs = 20000;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
+// Waits on other ranks (multi-GPU peer stores) give up after this long.
+constexpr uint64_t kPeerWaitNs = 1000000000ull;
 
 }  // namespace axq

@@ -683,13 +683,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
             if (lane == 0) {
                 const unsigned target = (*a.epoch + 1) * static_cast<unsigned>(a.npeers);
                 unsigned ok = 1;
-                uint32_t spins = 0;
-                while (static_cast<int>(ld_acquire_sys_u32(a.my_entry) - target) < 0) {
-                    if (++spins > (1u << 23)) {  // a second or two: give up, report
-                        atomicExch(a.err, 1);
-                        ok = 2;
-                        break;
-                    }
+                if (!poll_counter_sys(a.my_entry, target, kPeerWaitNs)) {  // give up, report
+                    atomicExch(a.err, 1);
+                    ok = 2;
                 }
                 st_release_cta_shared_u32(entry_flag, ok);
             }
@@ -817,13 +813,16 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
         }
         asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
         if (!entered && warp == 0) {
-            if (lane == 0) {  // the producer's entry wait (normally long done)
-                uint32_t spins = 0;
+            if (lane == 0 && ld_acquire_cta_shared_u32(entry_flag) == 0) {
+                // the producer's entry wait (normally long done); this bound
+                // outlasts the producer's own
+                const uint64_t t0 = globaltimer_ns();
                 while (ld_acquire_cta_shared_u32(entry_flag) == 0) {
-                    if (++spins > (1u << 28)) {  // outlasts the producer's own bounded wait
+                    if (globaltimer_ns() - t0 > 2 * kPeerWaitNs) {
                         atomicExch(a.err, 1);
                         break;
                     }
+                    __nanosleep(100);
                 }
             }
             __syncwarp();

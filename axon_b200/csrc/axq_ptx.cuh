@@ -182,6 +182,18 @@ __device__ __forceinline__ unsigned ld_acquire_cta_shared_u32(const unsigned* p)
     return v;
 }
 
+// Polls *p (acquire, system scope) until the counter has reached `target`
+// ((int)(*p - target) >= 0, wrap-safe); false after limit_ns of global time.
+__device__ __forceinline__ bool poll_counter_sys(const unsigned* p, unsigned target, uint64_t limit_ns) {
+    if (static_cast<int>(ld_acquire_sys_u32(p) - target) >= 0) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (static_cast<int>(ld_acquire_sys_u32(p) - target) < 0) {
+        if (globaltimer_ns() - t0 > limit_ns) return false;
+        __nanosleep(100);
+    }
+    return true;
+}
+
 __device__ __forceinline__ uint32_t byte_of(const uint32_t* w, int i) { return (w[i >> 2] >> (8 * (i & 3))) & 0xFFu; }
 
 }  // namespace axq

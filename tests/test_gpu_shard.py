@@ -109,6 +109,59 @@ def test_one_rank_peer_store_async_and_wait(orc, comm1):
             buf.destroy()
 
 
+def test_one_rank_peer_waits_run_out_and_context_survives(orc, comm1):
+    """Failure detection without a GPU fault: the buffer's call count is
+    advanced by hand (a count no rank will ever reach), so the next call's
+    entry wait (every CTA's producer) and completion wait (peer_wait_kernel)
+    both give up on their own one-second bounds and report through the call's
+    workspace status word.  The context stays usable: a plain matmul and a
+    fresh symmetric buffer still give the oracle's result."""
+    import time
+    import torch
+    import axon_b200 as ax
+    from axon_b200.shard import _CudaArray
+    fmt, M, K, N = "Q4_K", 64, 1024, 1
+    rng = np.random.default_rng(17)
+    q = orc.quantize(fmt, gen(rng, (M, K), "randn"))
+    b = rng.standard_normal((K, N)).astype(np.float32)
+    y_ref = orc.matmul(fmt, q, b, M, K)
+    a = ax.QTensor(torch.from_numpy(q).cuda(), (M, K), ax.QuantFormat[fmt])
+    bd = torch.from_numpy(b).cuda()
+    ws = ax.Workspace()
+    buf = ax.SymmetricBuffer(comm1, 4 * M * N)
+    try:
+        assert rel_err(ax.matmul_sharded_p2p(buf, a, bd, M, workspace=ws).cpu().numpy(), y_ref) <= TOL
+        # control block after the data (rounded up to 256 bytes), one 128-byte
+        # line each: completion count, entry count, finished CTAs, call count
+        data_bytes = -(-buf.nbytes // 256) * 256
+        calls = torch.as_tensor(_CudaArray(buf.ptr + data_bytes + 3 * 128, (1,), "<i4"), device="cuda")
+        calls += 1
+        torch.cuda.synchronize()
+        t0 = time.time()
+        ax.matmul_sharded_p2p(buf, a, bd, M, workspace=ws)
+        wp = ws.get(1, bd.device).data_ptr()
+        wp += (-wp) % 256
+        with pytest.raises(ax.AxqError) as e:
+            ax.workspace_status(wp)
+        elapsed = time.time() - t0
+        assert e.value.status == ax.Status.ERR_TIMEOUT
+        assert 1.0 <= elapsed < 60.0, elapsed
+    finally:
+        torch.cuda.synchronize()
+        buf.destroy()
+    out = torch.full((M, N), float("nan"), device="cuda")
+    ax.matmul_q(out, a, bd)
+    torch.cuda.synchronize()
+    assert rel_err(out.cpu().numpy(), y_ref) <= TOL
+    fresh = ax.SymmetricBuffer(comm1, 4 * M * N)
+    try:
+        assert rel_err(ax.matmul_sharded_p2p(fresh, a, bd, M, workspace=ws).cpu().numpy(), y_ref) <= TOL
+        ax.workspace_status(wp)
+    finally:
+        torch.cuda.synchronize()
+        fresh.destroy()
+
+
 def test_destroyed_communicator_is_refused(cuda):
     import axon_b200 as ax
     c = ax.Communicator.create(ax.Communicator.unique_id(), 1, 0)
