@@ -55,7 +55,7 @@ cudaError_t gemv_dispatch(int fmt, const void* w, const void* w2, const float* x
                           int64_t N, int flags, void* ws, size_t ws_bytes, int* err, cudaStream_t s,
                           const GemvPeers* peers = nullptr);
 
-// Tensor-core GEMM for N > 8 activation columns.
+// Tensor-core GEMM for N > kGemvMaxN activation columns.
 size_t gemm_workspace_bytes(int fmt, int64_t M, int64_t K, int64_t N);
 cudaError_t gemm_dispatch(int fmt, const void* w, const float* x, float* out, int64_t M, int64_t K, int64_t N, int flags,
                           void* ws, size_t ws_bytes, int* err, cudaStream_t s);
