@@ -47,6 +47,14 @@ from .ops import (  # noqa: F401
     gate_up_silu,
     mlp_q,
 )
+from .axon_file import (  # noqa: F401
+    AxonRecord,
+    axon_records,
+    load_axon,
+    load_tensor,
+    save_axon,
+    save_tensor,
+)
 from .shard import (  # noqa: F401
     Communicator,
     SymmetricBuffer,

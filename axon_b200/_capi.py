@@ -94,7 +94,24 @@ SIGNATURES = {
     "axq_matmul_sharded_p2p_async": (ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, _i64, _i64, _i64, ctypes.c_uint, _vp,
                                                     _sz, _vp]),
     "axq_symm_wait": (ctypes.c_int, [_vp, _vp]),
+    "axq_axon_open": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(_vp), ctypes.POINTER(ctypes.c_uint32)]),
+    "axq_axon_info": (ctypes.c_int, [_vp, ctypes.c_uint32, _vp]),
+    "axq_axon_read": (ctypes.c_int, [_vp, ctypes.c_uint32, _vp, _sz, _vp]),
+    "axq_axon_close": (ctypes.c_int, [_vp]),
+    "axq_axon_save": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_uint32, _vp, _vp, _vp]),
 }
+
+AXON_MAX_DIMS = 8
+AXON_NAME_BYTES = 256
+AXON_PLAIN, AXON_ROWS, AXON_FLAT = 0, 1, 2
+
+
+class AxonTensorInfo(ctypes.Structure):
+    """axq_axon_tensor (include/axq.h): one record of an .axon file."""
+
+    _fields_ = [("name", ctypes.c_char * AXON_NAME_BYTES), ("dtype", ctypes.c_uint32), ("quant", ctypes.c_uint32),
+                ("ndims", ctypes.c_uint32), ("layout", ctypes.c_uint32), ("shape", ctypes.c_int64 * AXON_MAX_DIMS),
+                ("data_bytes", ctypes.c_uint64), ("offset", ctypes.c_uint64)]
 
 COMM_ID_BYTES = 128  # AXQ_COMM_ID_BYTES
 

@@ -636,6 +636,66 @@ def run_case(args):
     return 0
 
 
+def run_axon(args):
+    """Loading weights from an .axon file (the reference's format) into
+    device memory: the headline workload's three packed matrices (340 MB,
+    Q2_K / Q3_K / Q5_K [28672 x 8192]) saved with save_axon, then loaded with
+    load_axon (file -> pinned staging -> device).  The file is read back from
+    the page cache (it was just written), so this measures the loader, not a
+    disk.  Beside it: the reference's own load_tensor (serialize.cpp:98-123,
+    oracle/_ref) on an fp32 file of the same size into host memory (it cannot
+    load packed tensors at all).  One JSON line."""
+    import torch
+    import axon_b200 as ax
+    import oracle
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(11)
+    ws = {}
+    for fmt in FORMATS:
+        q = ax.QTensor.empty(ROWS, K_DIM, ax.QuantFormat[fmt], device=dev)
+        ax.quantize(q, torch.randn(ROWS, K_DIM, device=dev, generator=g) * 0.02, ax.QuantFormat[fmt])
+        ws[fmt] = q
+    total = sum(packed_bytes(f) for f in FORMATS)
+    tmp = tempfile.mkdtemp(prefix="axq_axon_")
+    path = os.path.join(tmp, "c4.axon")
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    ax.save_axon(path, ws)
+    save_s = time.perf_counter() - t0
+    loads = []
+    for _ in range(max(3, min(args.steps, 5))):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        back = ax.load_axon(path)
+        torch.cuda.synchronize()
+        loads.append(time.perf_counter() - t0)
+        del back
+    for fmt in FORMATS:  # loaded bytes equal the saved ones
+        b = ax.load_axon(path)[fmt]
+        if not torch.equal(b.data[:packed_bytes(fmt)], ws[fmt].data[:packed_bytes(fmt)]):
+            raise RuntimeError(f"{fmt}: loaded bytes differ")
+        del b
+    line = {"config": "C6 .axon weights -> device", "bytes": total, "load_GBps": round(total / min(loads) / 1e9, 2),
+            "load_ms": round(min(loads) * 1e3, 2), "save_GBps": round(total / save_s / 1e9, 2),
+            "source": "page cache (file just written)"}
+    ref = oracle.ref()
+    if ref is not None:
+        fpath = os.path.join(tmp, "f32.axon")
+        n = total // 4
+        ref.save_tensor(fpath, [n], 0, 0, np.zeros(n, dtype=np.float32))
+        ref.load_tensor(fpath, cap=16)  # warm the page cache
+        t0 = time.perf_counter()
+        _, err = ref.load_tensor(fpath, cap=16)
+        dt = time.perf_counter() - t0
+        line["reference_load_tensor_fp32_host_GBps"] = round(total / dt / 1e9, 2) if err is None else err
+        os.remove(fpath)
+    os.remove(path)
+    os.rmdir(tmp)
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -645,7 +705,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--suite", action="store_true", help="time every configuration (one JSON line each)")
     ap.add_argument("--case", default=None, help="time one matmul, FMT:ROWS:K:TOKENS")
+    ap.add_argument("--axon", action="store_true", help="time loading the packed weights from an .axon file")
     args = ap.parse_args()
+    if args.axon:
+        return run_axon(args)
     if args.suite:
         return run_suite(args)
     if args.case:

@@ -208,6 +208,48 @@ int axq_symm_wait(void* symm, axq_stream_t stream);
 int axq_matmul_sharded(void* comm, int fmt, const void* a_q_local, const float* b, float* out, int64_t M, int64_t K,
                        int64_t N, unsigned flags, void* workspace, size_t workspace_bytes, axq_stream_t stream);
 
+/* ---- .axon tensor files ---------------------------------------------------
+ * Replace save_tensor / load_tensor / save_checkpoint / load_checkpoint
+ * (src/core/serialize.cpp:84-203) for device buffers.  The byte format is
+ * the reference's (serialize.cpp:10-70): files written by either side read on
+ * the other.  Unlike the reference's loaders, which ignore quant_type and so
+ * cannot load a packed tensor, the quant_type of each record selects its
+ * packed layout (`layout` below) and the data goes straight into device
+ * memory. */
+#define AXQ_AXON_MAX_DIMS 8
+#define AXQ_AXON_NAME_BYTES 256
+#define AXQ_AXON_PLAIN 0u /* unquantized: numel * sizeof(dtype) bytes */
+#define AXQ_AXON_ROWS 1u  /* packed, rows of whole blocks: axq_quantized_size_2d(rows, last dim) */
+#define AXQ_AXON_FLAT 2u  /* packed over the flattened tensor: axq_quantized_size(numel); rows not whole blocks */
+
+typedef struct axq_axon_tensor {
+    char name[AXQ_AXON_NAME_BYTES]; /* NUL-terminated */
+    uint32_t dtype;                 /* the reference's DType ordinal (0 Float32, 1 Float64, 2 Int32, 3 Int64, 4 Int16, 5 Int8, 6 UInt8) */
+    uint32_t quant;                 /* QuantFormat ordinal: 0 none, else an AXQ format id */
+    uint32_t ndims;                 /* <= AXQ_AXON_MAX_DIMS */
+    uint32_t layout;                /* AXQ_AXON_*; set by the library */
+    int64_t shape[AXQ_AXON_MAX_DIMS];
+    uint64_t data_bytes;            /* bytes of the tensor's data */
+    uint64_t offset;                /* file offset of the data (set on open) */
+} axq_axon_tensor;
+
+/* Open an .axon file and check every record (magic, version, sizes against
+ * shape, dtype and quant_type); *count_out = number of tensors. */
+int axq_axon_open(const char* path, void** file_out, uint32_t* count_out);
+/* Metadata of tensor `index` (file order). */
+int axq_axon_info(void* file, uint32_t index, axq_axon_tensor* info_out);
+/* Copy tensor `index`'s data into dst (device memory: through pinned staging
+ * buffers on `stream`, file reads overlapping the copies; host memory: read
+ * directly).  Returns once the data is in dst.  One thread per file handle. */
+int axq_axon_read(void* file, uint32_t index, void* dst, size_t dst_bytes, axq_stream_t stream);
+int axq_axon_close(void* file);
+/* Write `count` tensors (metadata infos[i], data[i] in host or device
+ * memory, data_bytes each) in the reference's format; offset and layout are
+ * ignored on input.  count == 1 with the name "data" is what save_tensor
+ * writes. */
+int axq_axon_save(const char* path, uint32_t count, const axq_axon_tensor* infos, const void* const* data,
+                  axq_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -144,6 +144,49 @@ class Reference(_Lib):
     def has_avx2(self) -> bool:
         return bool(self.lib.ref_has_avx2())
 
+    # ---- .axon files through the reference's serializer (src/core/serialize.cpp)
+
+    def save_tensor(self, path: str, shape, dtype: int, quant: int, data: np.ndarray) -> None:
+        """save_tensor (serialize.cpp:84-96) of one tensor named "data"."""
+        sh = np.ascontiguousarray(shape, dtype=np.int64)
+        d = np.ascontiguousarray(data).view(np.uint8).ravel()
+        L = self.lib
+        L.ref_save_tensor.argtypes = [ctypes.c_char_p, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp,
+                                      ctypes.c_size_t]
+        if L.ref_save_tensor(path.encode(), _ptr(sh), len(shape), dtype, quant, _ptr(d), d.size) != 0:
+            raise RuntimeError("ref_save_tensor failed")
+
+    def save_checkpoint(self, path: str, tensors) -> None:
+        """save_checkpoint (serialize.cpp:125-148); tensors: list of
+        (name, shape, dtype, quant, data)."""
+        n = len(tensors)
+        names = (ctypes.c_char_p * n)(*[t[0].encode() for t in tensors])
+        shapes = np.concatenate([np.asarray(t[1], dtype=np.int64) for t in tensors])
+        ndims = np.asarray([len(t[1]) for t in tensors], dtype=np.int32)
+        dtypes = np.asarray([t[2] for t in tensors], dtype=np.int32)
+        quants = np.asarray([t[3] for t in tensors], dtype=np.int32)
+        datas = [np.ascontiguousarray(t[4]).view(np.uint8).ravel() for t in tensors]
+        ptrs = (_vp * n)(*[_ptr(d) for d in datas])
+        sizes = (ctypes.c_size_t * n)(*[d.size for d in datas])
+        L = self.lib
+        L.ref_save_checkpoint.argtypes = [ctypes.c_char_p, ctypes.c_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp]
+        rc = L.ref_save_checkpoint(path.encode(), n, ctypes.cast(names, _vp), _ptr(shapes), _ptr(ndims),
+                                   _ptr(dtypes), _ptr(quants), ctypes.cast(ptrs, _vp), ctypes.cast(sizes, _vp))
+        if rc != 0:
+            raise RuntimeError("ref_save_checkpoint failed")
+
+    def load_tensor(self, path: str, cap: int = 1 << 20):
+        """load_tensor (serialize.cpp:98-123): (data bytes, None) or (None, error)."""
+        out = np.zeros(cap, dtype=np.uint8)
+        got = ctypes.c_size_t(0)
+        err = ctypes.create_string_buffer(512)
+        L = self.lib
+        L.ref_load_tensor.argtypes = [ctypes.c_char_p, _vp, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t),
+                                      ctypes.c_char_p, ctypes.c_size_t]
+        if L.ref_load_tensor(path.encode(), _ptr(out), cap, ctypes.byref(got), err, 512) != 0:
+            return None, err.value.decode()
+        return out[:got.value].copy(), None
+
     def quantize_1d(self, fmt: str, x: np.ndarray) -> np.ndarray:
         """The reference's flat (1-D tensor) pack path."""
         x = np.ascontiguousarray(x, dtype=np.float32).ravel()

@@ -13,12 +13,17 @@
 //   cpu::matmul_q2_K/_q3_K/_q6_K  :1862/:1924/:1805 (scalar only)
 //   cpu::matmul (fp32)       :116, used for Q8_0 after dequantize because
 //       the reference has no Q8_0 quantized matmul.
+//   save_tensor / load_tensor / save_checkpoint  src/core/serialize.cpp:84/:98/:125
+//       (.axon files: golden fixtures for the device loader)
 #include <chrono>
+#include <cstdio>
 #include <cstring>
 #include <memory>
 #include <thread>
 #include <vector>
 
+#include "axon/core/serialize.h"
+#include "axon/nn/module.h"
 #include "axon/backend/cpu_backend.h"
 #include "axon/backend/cpuid.h"
 #include "axon/backend/registry.h"
@@ -70,6 +75,24 @@ Expected<void> run_matmul(QuantFormat f, Tensor& out, const Tensor& a_q, const T
         default: return Error{"unsupported format"};
     }
 }
+
+// A tensor with the given metadata (quant != None: a packed tensor whose
+// storage holds `bytes` of blocks) over a copy of `data`.
+Tensor make_any(const int64_t* shape, int ndims, int dtype, int quant, const void* data, size_t bytes) {
+    std::vector<int64_t> sh(shape, shape + ndims);
+    auto c = TensorMetadata::contiguous(sh, static_cast<DType>(dtype));
+    TensorMetadata md(c.shape(), c.strides(), static_cast<DType>(dtype), Device::CPU, to_fmt(quant));
+    auto st = std::make_shared<Storage>(bytes);
+    if (quant) st->quant = QuantizationDescriptor{to_fmt(quant), static_cast<size_t>(is_kquant(to_fmt(quant)) ? 256 : 32)};
+    if (bytes) std::memcpy(st->data, data, bytes);
+    return Tensor(md, st, false);
+}
+
+// Holds parameters for save_checkpoint (which walks a Module's parameters).
+struct Holder : Module {
+    std::vector<std::unique_ptr<Parameter>> owned;
+    Expected<Tensor> forward(Runtime&, const Tensor& x) override { return x; }
+};
 
 struct Job {
     QuantFormat fmt;
@@ -206,6 +229,42 @@ int ref_quantize_threads(int fmt, const float* src, int64_t rows, int64_t cols, 
     for (auto& th : threads) th.join();
     for (int s : status)
         if (s) return -1;
+    return 0;
+}
+
+// save_tensor (serialize.cpp:84-96) of one tensor; 0 on success.
+int ref_save_tensor(const char* path, const int64_t* shape, int ndims, int dtype, int quant, const void* data,
+                    size_t bytes) {
+    Tensor t = make_any(shape, ndims, dtype, quant, data, bytes);
+    return save_tensor(t, path) ? 0 : 1;
+}
+
+// save_checkpoint (serialize.cpp:125-148) of n tensors, in order, under the
+// given names; shapes are packed back to back (ndims[i] entries each).
+int ref_save_checkpoint(const char* path, int n, const char* const* names, const int64_t* shapes, const int* ndims,
+                        const int* dtypes, const int* quants, const void* const* data, const size_t* bytes) {
+    Holder h;
+    const int64_t* sp = shapes;
+    for (int i = 0; i < n; ++i) {
+        h.owned.push_back(std::make_unique<Parameter>(make_any(sp, ndims[i], dtypes[i], quants[i], data[i], bytes[i])));
+        h.register_parameter(names[i], h.owned.back().get());
+        sp += ndims[i];
+    }
+    return save_checkpoint(h, path) ? 0 : 1;
+}
+
+// load_tensor (serialize.cpp:98-123): 0 and the data (up to cap bytes) on
+// success, else 1 and the reference's error message in err.
+int ref_load_tensor(const char* path, void* out, size_t cap, size_t* got, char* err, size_t err_len) {
+    Runtime rt;
+    auto r = load_tensor(rt, path);
+    if (!r) {
+        std::snprintf(err, err_len, "%s", r.error().message.c_str());
+        return 1;
+    }
+    const size_t n = (*r).storage()->size_bytes;
+    *got = n;
+    std::memcpy(out, (*r).storage()->data, n < cap ? n : cap);
     return 0;
 }
 
