@@ -17,13 +17,24 @@
 // quantized_size(numel) bytes whose rows are not whole blocks is the flat
 // layout (TensorMetadata::size_bytes, tensor_metadata.h:45-62).
 //
-// Reads into device memory go through two pinned staging buffers, so the
-// file read of one chunk overlaps the host-to-device copy of the previous
-// one; reads into host memory go straight from the file.
+// Reads into device memory are split into 8 MiB chunks over up to
+// kReaders threads; each reads its chunks (pread) into its own two pinned
+// staging buffers, so its file read of one chunk overlaps the host-to-device
+// copy of the previous one, and the threads' reads overlap each other.  The
+// staging buffers (64 MiB of pinned host memory) are allocated on the first
+// device read or write of the process and kept until it exits; device reads
+// and writes from several host threads take turns on them.  Reads into host
+// memory go straight from the file.
+#include <fcntl.h>
+#include <unistd.h>
+
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
+#include <mutex>
 #include <cstring>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "axq_internal.h"
@@ -34,6 +45,7 @@ namespace {
 constexpr uint32_t kAxonMagic = 0x4E4F5841u;  // "AXON" little-endian
 constexpr uint32_t kAxonVersion = 1;
 constexpr size_t kStageBytes = size_t{8} << 20;
+constexpr int kReaders = 4;
 
 // Bytes per element of the reference's DType (include/axon/core/types.h:9-30); 0 if unknown.
 size_t dtype_bytes(uint32_t dtype) {
@@ -49,18 +61,28 @@ size_t dtype_bytes(uint32_t dtype) {
     }
 }
 
+constexpr int kStages = 2 * kReaders;  // two staging buffers per reader
+
+constexpr int kMaxDev = 64;
+
+// Pinned staging shared by every file handle (see the header comment).
+struct StagePool {
+    std::mutex mu;
+    void* stage[kStages] = {};
+    cudaEvent_t ev[kMaxDev][kStages] = {};  // events belong to a device
+};
+StagePool& stage_pool() {
+    static StagePool* p = new StagePool();  // lives as long as the process
+    return *p;
+}
+
 struct AxonFile {
     FILE* f = nullptr;
+    int fd = -1;  // for the readers' pread
     std::string path;
     std::vector<axq_axon_tensor> t;
-    void* stage[2] = {nullptr, nullptr};  // pinned, allocated on the first device read
-    cudaEvent_t ev[2] = {nullptr, nullptr};
-    int stage_dev = -1;
     ~AxonFile() {
-        for (int i = 0; i < 2; ++i) {
-            if (ev[i]) cudaEventDestroy(ev[i]);
-            if (stage[i]) cudaFreeHost(stage[i]);
-        }
+        if (fd >= 0) ::close(fd);
         if (f) std::fclose(f);
     }
 };
@@ -109,22 +131,18 @@ bool is_device_ptr(const void* p) {
     return at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged;
 }
 
-int ensure_stage(AxonFile* af, const char* fn) {
+// Makes the first `nstage` staging buffers and their events on the current
+// device ready (call with the pool locked); *dev_out = that device.
+int ensure_stage(StagePool& sp, const char* fn, int nstage, int* dev_out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
-    if (e == cudaSuccess && af->stage[0] && af->stage_dev != dev) {
-        // the events belong to the device they were made on
-        for (int i = 0; i < 2; ++i) {
-            cudaEventDestroy(af->ev[i]);
-            af->ev[i] = nullptr;
-        }
-    }
-    for (int i = 0; i < 2 && e == cudaSuccess; ++i) {
-        if (!af->stage[i]) e = cudaHostAlloc(&af->stage[i], kStageBytes, cudaHostAllocPortable);
-        if (e == cudaSuccess && !af->ev[i]) e = cudaEventCreateWithFlags(&af->ev[i], cudaEventDisableTiming);
+    if (e == cudaSuccess && (dev < 0 || dev >= kMaxDev)) e = cudaErrorInvalidDevice;
+    for (int i = 0; i < nstage && e == cudaSuccess; ++i) {
+        if (!sp.stage[i]) e = cudaHostAlloc(&sp.stage[i], kStageBytes, cudaHostAllocPortable);
+        if (e == cudaSuccess && !sp.ev[dev][i]) e = cudaEventCreateWithFlags(&sp.ev[dev][i], cudaEventDisableTiming);
     }
     if (e != cudaSuccess) return io_fail(AXQ_ERR_CUDA, std::string(fn) + ": staging set-up: " + cudaGetErrorString(e));
-    af->stage_dev = dev;
+    *dev_out = dev;
     return AXQ_OK;
 }
 
@@ -223,29 +241,70 @@ int axq_axon_read(void* file, uint32_t index, void* dst, size_t dst_bytes, axq_s
         if (t.data_bytes && std::fread(dst, 1, t.data_bytes, af->f) != t.data_bytes) return short_read();
         return AXQ_OK;
     }
-    if (int st = ensure_stage(af, fn)) return st;
+    const uint64_t nchunks = (t.data_bytes + kStageBytes - 1) / kStageBytes;
+    const int readers = static_cast<int>(std::min<uint64_t>(kReaders, nchunks));
+    if (readers == 0) return AXQ_OK;
+    if (af->fd < 0) af->fd = ::open(af->path.c_str(), O_RDONLY);
+    if (af->fd < 0) return io_fail(AXQ_ERR_INVALID, std::string(fn) + ": cannot reopen " + af->path);
+    StagePool& sp = stage_pool();
+    std::lock_guard<std::mutex> lock(sp.mu);
+    int dev = 0;
+    if (int st = ensure_stage(sp, fn, 2 * readers, &dev)) return st;
+    cudaEvent_t* ev = sp.ev[dev];
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    uint64_t off = 0;
-    int b = 0;
-    bool used[2] = {false, false};
-    cudaError_t e = cudaSuccess;
-    while (off < t.data_bytes && e == cudaSuccess) {
-        const size_t n = static_cast<size_t>(std::min<uint64_t>(kStageBytes, t.data_bytes - off));
-        if (used[b]) e = cudaEventSynchronize(af->ev[b]);  // its previous copy has left the buffer
-        if (e != cudaSuccess) break;
-        if (std::fread(af->stage[b], 1, n, af->f) != n) {
-            cudaStreamSynchronize(s);
-            return short_read();
+    std::atomic<int> cuda_err{0};  // first CUDA error code seen by any reader
+    std::atomic<bool> short_file{false};
+    // Reader r takes chunks r, r + readers, ... through staging buffers 2r and 2r+1.
+    auto reader = [&](int r) {
+        if (cudaSetDevice(dev) != cudaSuccess) {
+            cuda_err.store(static_cast<int>(cudaErrorInvalidDevice));
+            return;
         }
-        e = cudaMemcpyAsync(static_cast<uint8_t*>(dst) + off, af->stage[b], n, cudaMemcpyHostToDevice, s);
-        if (e == cudaSuccess) e = cudaEventRecord(af->ev[b], s);
-        used[b] = true;
-        off += n;
-        b ^= 1;
-    }
-    for (int i = 0; i < 2 && e == cudaSuccess; ++i)
-        if (used[i]) e = cudaEventSynchronize(af->ev[i]);
-    if (e != cudaSuccess) return io_fail(AXQ_ERR_CUDA, std::string(fn) + ": " + cudaGetErrorString(e));
+        bool used[2] = {false, false};
+        int b = 0;
+        for (uint64_t c = static_cast<uint64_t>(r); c < nchunks; c += static_cast<uint64_t>(readers)) {
+            if (cuda_err.load() || short_file.load()) break;
+            const uint64_t off = c * kStageBytes;
+            const size_t n = static_cast<size_t>(std::min<uint64_t>(kStageBytes, t.data_bytes - off));
+            const int k = 2 * r + b;
+            cudaError_t e = used[b] ? cudaEventSynchronize(ev[k]) : cudaSuccess;  // buffer free again
+            if (e != cudaSuccess) {
+                cuda_err.store(static_cast<int>(e));
+                break;
+            }
+            size_t done = 0;
+            while (done < n) {
+                const ssize_t got = ::pread(af->fd, static_cast<uint8_t*>(sp.stage[k]) + done, n - done,
+                                            static_cast<off_t>(t.offset + off + done));
+                if (got <= 0) break;
+                done += static_cast<size_t>(got);
+            }
+            if (done != n) {
+                short_file.store(true);
+                break;
+            }
+            e = cudaMemcpyAsync(static_cast<uint8_t*>(dst) + off, sp.stage[k], n, cudaMemcpyHostToDevice, s);
+            if (e == cudaSuccess) e = cudaEventRecord(ev[k], s);
+            if (e != cudaSuccess) {
+                cuda_err.store(static_cast<int>(e));
+                break;
+            }
+            used[b] = true;
+            b ^= 1;
+        }
+        for (int i = 0; i < 2; ++i)
+            if (used[i]) {
+                const cudaError_t e = cudaEventSynchronize(ev[2 * r + i]);
+                if (e != cudaSuccess) cuda_err.store(static_cast<int>(e));
+            }
+    };
+    std::vector<std::thread> pool;
+    for (int r = 1; r < readers; ++r) pool.emplace_back(reader, r);
+    reader(0);
+    for (auto& th : pool) th.join();
+    if (short_file.load()) return short_read();
+    if (cuda_err.load())
+        return io_fail(AXQ_ERR_CUDA, std::string(fn) + ": " + cudaGetErrorString(static_cast<cudaError_t>(cuda_err.load())));
     return AXQ_OK;
 }
 
@@ -269,7 +328,8 @@ int axq_axon_save(const char* path, uint32_t count, const axq_axon_tensor* infos
     }
     FILE* f = std::fopen(path, "wb");
     if (!f) return io_fail(AXQ_ERR_INVALID, std::string(fn) + ": failed to open file for writing: " + path);
-    AxonFile af;  // staging for device sources; closes nothing (f is ours)
+    StagePool& sp = stage_pool();
+    std::unique_lock<std::mutex> lock(sp.mu, std::defer_lock);  // taken at the first device source
     auto fail_io = [&](const std::string& what) {
         std::fclose(f);
         return io_fail(AXQ_ERR_INVALID, std::string(fn) + ": " + path + ": " + what);
@@ -291,20 +351,22 @@ int axq_axon_save(const char* path, uint32_t count, const axq_axon_tensor* infos
             if (!fwrite_all(f, data[i], t[i].data_bytes)) return fail_io("write failed");
             continue;
         }
-        if (int st = ensure_stage(&af, fn)) {
+        if (!lock.owns_lock()) lock.lock();
+        int dev = 0;
+        if (int st = ensure_stage(sp, fn, 1, &dev)) {
             std::fclose(f);
             return st;
         }
         for (uint64_t off = 0; off < t[i].data_bytes;) {
             const size_t n = static_cast<size_t>(std::min<uint64_t>(kStageBytes, t[i].data_bytes - off));
-            cudaError_t e = cudaMemcpyAsync(af.stage[0], static_cast<const uint8_t*>(data[i]) + off, n,
+            cudaError_t e = cudaMemcpyAsync(sp.stage[0], static_cast<const uint8_t*>(data[i]) + off, n,
                                             cudaMemcpyDeviceToHost, s);
             if (e == cudaSuccess) e = cudaStreamSynchronize(s);
             if (e != cudaSuccess) {
                 std::fclose(f);
                 return io_fail(AXQ_ERR_CUDA, std::string(fn) + ": " + cudaGetErrorString(e));
             }
-            if (!fwrite_all(f, af.stage[0], n)) return fail_io("write failed");
+            if (!fwrite_all(f, sp.stage[0], n)) return fail_io("write failed");
             off += n;
         }
     }

@@ -238,9 +238,12 @@ typedef struct axq_axon_tensor {
 int axq_axon_open(const char* path, void** file_out, uint32_t* count_out);
 /* Metadata of tensor `index` (file order). */
 int axq_axon_info(void* file, uint32_t index, axq_axon_tensor* info_out);
-/* Copy tensor `index`'s data into dst (device memory: through pinned staging
- * buffers on `stream`, file reads overlapping the copies; host memory: read
- * directly).  Returns once the data is in dst.  One thread per file handle. */
+/* Copy tensor `index`'s data into dst (device memory: up to 4 reader threads
+ * through pinned staging buffers, copies on `stream`, file reads overlapping
+ * the copies; host memory: read directly).  Returns once the data is in dst.
+ * The staging (64 MiB pinned) is allocated on the first device read or save
+ * and kept until the process exits; concurrent device reads take turns on
+ * it.  One thread per file handle. */
 int axq_axon_read(void* file, uint32_t index, void* dst, size_t dst_bytes, axq_stream_t stream);
 int axq_axon_close(void* file);
 /* Write `count` tensors (metadata infos[i], data[i] in host or device
