@@ -35,6 +35,7 @@ from .ops import (  # noqa: F401
     Workspace,
     quantize,
     dequantize,
+    matmul,
     matmul_q,
     matmul_q8_0,
     matmul_q4,

@@ -66,6 +66,8 @@ constexpr size_t kStatusBytes = 256;  // status words at the front of a workspac
 
 }  // namespace
 
+int check_device_ptr(const void* p, const char* what, const char* fn) { return check_ptr(p, what, fn); }
+
 int validate_matmul_ptrs(int fmt, const void* a_q, const void* b, const void* out, const char* fn) {
     if (!known_fmt(fmt)) return fail(AXQ_ERR_UNSUPPORTED, std::string(fn) + ": unsupported format " + std::to_string(fmt));
     if (int r = check_ptr(a_q, "a_q", fn)) return r;

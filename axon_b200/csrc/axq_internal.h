@@ -21,6 +21,8 @@ void set_last_error(const std::string& msg);
 // The pointer and format checks of axq_matmul (status 0 or an AXQ_ERR_*
 // code with the message set).
 int validate_matmul_ptrs(int fmt, const void* a_q, const void* b, const void* out, const char* fn);
+// NULL, host-only and other-device pointers -> AXQ_ERR_INVALID with a message.
+int check_device_ptr(const void* p, const char* what, const char* fn);
 
 cudaError_t pack_dispatch(int fmt, const float* src, void* dst, int64_t rows, int64_t cols, cudaStream_t s);
 cudaError_t dequant_dispatch(int fmt, const void* src, float* dst, int64_t rows, int64_t cols, cudaStream_t s);

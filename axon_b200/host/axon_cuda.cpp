@@ -105,6 +105,28 @@ Expected<void> matmul_kernel(KernelContext& ctx) {
     return {};
 }
 
+// fp32 matmul (unquantized A), the "matmul" kernel the reference's
+// choose_gemm_strategy names for fp32 operands (strategy.cpp:35-58).
+Expected<void> matmul_f32_kernel(KernelContext& ctx) {
+    const char* fn = "matmul";
+    if (ctx.outputs.size() < 1 || ctx.inputs.size() < 2) return Error{std::string(fn) + ": expects 1 output, 2 inputs"};
+    DeviceTensor& out = ctx.outputs[0];
+    const DeviceTensor& a = ctx.inputs[0];
+    const DeviceTensor& b = ctx.inputs[1];
+    if (a.is_quantized() || b.is_quantized() || out.is_quantized() || a.dtype() != DType::Float32 ||
+        b.dtype() != DType::Float32 || out.dtype() != DType::Float32)
+        return Error{"cpu::matmul: only Float32 supported"};
+    const int64_t M = a.rows(), K = a.cols(), N = b.cols();
+    if (b.rows() != K) return Error{std::string(fn) + ": inner dimensions differ"};
+    if (out.rows() != M || out.cols() != N) return Error{std::string(fn) + ": output shape mismatch"};
+    if (auto e = check_same_device(a, b, fn); !e) return e;
+    if (auto e = check_same_device(a, out, fn); !e) return e;
+    const int st = axq_matmul_f32(static_cast<const float*>(a.data()), static_cast<const float*>(b.data()),
+                                  static_cast<float*>(out.data()), M, K, N, t_stream);
+    if (st != AXQ_OK) return last_error(fn);
+    return {};
+}
+
 Expected<void> quantize_kernel(KernelContext& ctx) {
     if (ctx.outputs.size() < 1 || ctx.inputs.size() < 1) return Error{"quantize: expects 1 output, 1 input"};
     DeviceTensor& dst = ctx.outputs[0];
@@ -327,6 +349,7 @@ void register_cuda_kernels() {
         reg.register_kernel(cuda_key(OpId::MatMulQ6_K), matmul_kernel<OpId::MatMulQ6_K>);
         reg.register_kernel(cuda_key(OpId::Quantize), quantize_kernel);
         reg.register_kernel(cuda_key(OpId::Dequantize), dequantize_kernel);
+        reg.register_kernel(cuda_key(OpId::MatMul), matmul_f32_kernel);
     }
 }
 
@@ -371,7 +394,7 @@ Expected<void> dequantize(DeviceTensor& dst, const DeviceTensor& src) {
 }
 
 Expected<void> matmul(DeviceTensor& out, const DeviceTensor& a, const DeviceTensor& b) {
-    if (!a.is_quantized()) return Error{"matmul: the CUDA backend serves quantized A only"};
+    // quantized A -> matmul_q*; fp32 A -> "matmul" (as choose_gemm_strategy routes)
     return run_named(gemm_kernel_name(a.quant().format), out, a, b);
 }
 

@@ -217,6 +217,28 @@ matmul_q5_K = _fixed(QuantFormat.Q5_K, "matmul_q5_K")
 matmul_q6_K = _fixed(QuantFormat.Q6_K, "matmul_q6_K")
 
 
+def matmul(out: torch.Tensor, a, b: torch.Tensor, stream: Optional[torch.cuda.Stream] = None, **kw) -> torch.Tensor:
+    """``out = a . b`` routed like the reference's ``cpu::matmul``
+    (src/backend/cpu_backend.cpp:116-173 with choose_gemm_strategy,
+    src/backend/cpu/strategy.cpp:5-65): a packed :class:`QTensor` A goes to
+    its format's quantized matmul, an fp32 A (all row-major [M x K] . [K x N])
+    to the fp32 GEMM (``axq_matmul_f32``, cuBLAS in pedantic fp32 mode)."""
+    if isinstance(a, QTensor):
+        return matmul_q(out, a, b, stream=stream, **kw)
+    for t, name in ((a, "a"), (b, "b"), (out, "out")):
+        _req_cuda(t, name, torch.float32)
+        if t.dim() != 2:
+            raise AxqError(Status.ERR_INVALID, "cpu::matmul: all inputs must be 2D")
+    M, K = a.shape
+    if b.shape[0] != K:
+        raise AxqError(Status.ERR_INVALID, "cpu::matmul: inner dimensions must match")
+    N = b.shape[1]
+    if tuple(out.shape) != (M, N):
+        raise AxqError(Status.ERR_INVALID, "cpu::matmul: output shape mismatch")
+    check(lib().axq_matmul_f32(a.data_ptr(), b.data_ptr(), out.data_ptr(), M, K, N, _stream_handle(stream, out.device)))
+    return out
+
+
 def linear_q(x: torch.Tensor, w: QTensor, out: Optional[torch.Tensor] = None, **kw) -> torch.Tensor:
     """Quantized Linear: y[N, M] = x[N, K] . W[M, K]^T with W packed row-wise.
 

@@ -609,8 +609,10 @@ def run_case(args):
 
     fmt, rows, K, M = args.case.split(":")
     rows, K, M = int(rows), int(K), int(M)
-    F = ax.QuantFormat[fmt]
     dev = torch.device("cuda", 0)
+    if fmt == "F32":
+        return run_case_f32(args, rows, K, M)
+    F = ax.QuantFormat[fmt]
     g = torch.Generator(device=dev).manual_seed(3)
     W = torch.randn(rows, K, device=dev, generator=g) * 0.02
     base = ax.QTensor.empty(rows, K, F, device=dev)
@@ -633,6 +635,43 @@ def run_case(args):
     ms = e0.elapsed_time(e1) / max(1, args.steps)
     print(json.dumps({"case": args.case, "ms": round(ms, 5), "TOPS": round(2.0 * rows * K * M / (ms / 1e3) / 1e12, 2),
                       "weight_GBps": round(nbytes / (ms / 1e3) / 1e9, 1)}), flush=True)
+    return 0
+
+
+def run_case_f32(args, rows, K, M):
+    """fp32 matmul for unquantized A (--case F32:M:K:N): out[M x N] = a . b
+    through axon_b200.matmul (cuBLAS SGEMM, pedantic fp32), CUDA events over
+    --steps calls; beside it the reference's cpu::matmul (oracle/_ref) on
+    all host threads' worth of one call, timed once."""
+    import torch
+    import axon_b200 as ax
+    import oracle
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(4)
+    a = torch.randn(rows, K, device=dev, generator=g)
+    b = torch.randn(K, M, device=dev, generator=g)
+    out = torch.empty(rows, M, device=dev)
+    for _ in range(max(3, args.warmup)):
+        ax.matmul(out, a, b)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        ax.matmul(out, a, b)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / max(1, args.steps)
+    flops = 2.0 * rows * K * M
+    line = {"case": args.case, "ms": round(ms, 5), "TFLOPs": round(flops / (ms / 1e3) / 1e12, 2),
+            "math": "fp32 (cuBLAS pedantic, no TF32)"}
+    ref = oracle.ref()
+    if ref is not None:
+        an, bn = a.cpu().numpy(), b.cpu().numpy()
+        t0 = time.perf_counter()
+        ref.matmul_f32(an, bn)
+        line["reference_cpu_GFLOPs"] = round(flops / (time.perf_counter() - t0) / 1e9, 2)
+    print(json.dumps(line), flush=True)
     return 0
 
 

@@ -208,6 +208,14 @@ int axq_symm_wait(void* symm, axq_stream_t stream);
 int axq_matmul_sharded(void* comm, int fmt, const void* a_q_local, const float* b, float* out, int64_t M, int64_t K,
                        int64_t N, unsigned flags, void* workspace, size_t workspace_bytes, axq_stream_t stream);
 
+/* ---- fp32 matmul (unquantized A) -------------------------------------------
+ * Replaces cpu::matmul's fp32 path (src/backend/cpu_backend.cpp:116-173, routed
+ * by choose_gemm_strategy, src/backend/cpu/strategy.cpp:35-58): row-major
+ * out[M x N] = a[M x K] . b[K x N], all fp32 device buffers, as a cuBLAS SGEMM
+ * in pedantic fp32 mode (no TF32).  cuBLAS is loaded at run time; without it
+ * the call returns AXQ_ERR_UNSUPPORTED. */
+int axq_matmul_f32(const float* a, const float* b, float* out, int64_t M, int64_t K, int64_t N, axq_stream_t stream);
+
 /* ---- .axon tensor files ---------------------------------------------------
  * Replace save_tensor / load_tensor / save_checkpoint / load_checkpoint
  * (src/core/serialize.cpp:84-203) for device buffers.  The byte format is

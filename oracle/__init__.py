@@ -144,6 +144,19 @@ class Reference(_Lib):
     def has_avx2(self) -> bool:
         return bool(self.lib.ref_has_avx2())
 
+    def matmul_f32(self, a: np.ndarray, b: np.ndarray) -> np.ndarray:
+        """cpu::matmul (cpu_backend.cpp:116-173) of fp32 [M x K] . [K x N]."""
+        a = np.ascontiguousarray(a, dtype=np.float32)
+        b = np.ascontiguousarray(b, dtype=np.float32)
+        M, K = a.shape
+        N = b.shape[1]
+        out = np.zeros((M, N), dtype=np.float32)
+        L = self.lib
+        L.ref_matmul_f32.argtypes = [_vp, _vp, _vp, _c_i64, _c_i64, _c_i64]
+        if L.ref_matmul_f32(_ptr(a), _ptr(b), _ptr(out), M, K, N) != 0:
+            raise RuntimeError("ref_matmul_f32 failed")
+        return out
+
     # ---- .axon files through the reference's serializer (src/core/serialize.cpp)
 
     def save_tensor(self, path: str, shape, dtype: int, quant: int, data: np.ndarray) -> None:

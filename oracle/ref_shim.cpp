@@ -232,6 +232,17 @@ int ref_quantize_threads(int fmt, const float* src, int64_t rows, int64_t cols, 
     return 0;
 }
 
+// cpu::matmul (cpu_backend.cpp:116-173) on fp32 row-major operands: the
+// reference's fp32 path (its registry kernel when one is registered, else
+// its scalar loop); 0 on success.
+int ref_matmul_f32(const float* a, const float* b, float* out, int64_t M, int64_t K, int64_t N) {
+    Tensor ta = make_f32({M, K}, a), tb = make_f32({K, N}, b), to = make_f32({M, N}, nullptr);
+    auto r = cpu::matmul(to, ta, tb);
+    if (!r) return 1;
+    std::memcpy(out, to.storage()->data, static_cast<size_t>(M * N) * sizeof(float));
+    return 0;
+}
+
 // save_tensor (serialize.cpp:84-96) of one tensor; 0 on success.
 int ref_save_tensor(const char* path, const int64_t* shape, int ndims, int dtype, int quant, const void* data,
                     size_t bytes) {

@@ -86,8 +86,13 @@ static void test_errors_before_any_device_call() {
     r = matmul_q5_K(out, a, b2);  // fixed-format entry rejects another format
     CHECK(!r && r.error().message.find("not Q5_K") != std::string::npos);
     DeviceTensor dense = DeviceTensor::view(fake, 64, 256, DType::Float32, QuantFormat::None, 0);
-    r = matmul(out, dense, b2);
-    CHECK(!r && r.error().message.find("quantized A") != std::string::npos);
+    // fp32 A routes to the fp32 kernel ("matmul"), which checks shapes and
+    // dtypes on the host first
+    r = matmul(out2, dense, b2);
+    CHECK(!r && r.error().message.find("output shape") != std::string::npos);
+    DeviceTensor b_u8 = DeviceTensor::view(fake, 256, 4, DType::UInt8, QuantFormat::None, 0);
+    r = matmul(out, dense, b_u8);
+    CHECK(!r && r.error().message.find("only Float32") != std::string::npos);
     DeviceTensor other_dev = DeviceTensor::view(fake, 256, 4, DType::Float32, QuantFormat::None, 1);
     r = matmul(out, a, other_dev);
     CHECK(!r && r.error().message.find("different devices") != std::string::npos);
