@@ -3,7 +3,10 @@
 
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <mutex>
+#include <random>
+#include <vector>
 
 namespace axon::cuda {
 namespace {
@@ -277,6 +280,41 @@ Expected<DeviceTensor> DeviceTensor::from_host(const float* host, int64_t rows, 
     return std::move(t.value());
 }
 
+namespace {
+std::mutex g_rand_mu;
+std::mt19937& rand_gen() {
+    static std::mt19937 gen(42);  // tensor.cpp:39
+    return gen;
+}
+}  // namespace
+
+void randn_fill(float* host, size_t n) {
+    std::lock_guard<std::mutex> lk(g_rand_mu);
+    std::normal_distribution<float> dist(0.0f, 1.0f);  // a fresh one per call, as tensor.cpp:40
+    for (size_t i = 0; i < n; ++i) host[i] = dist(rand_gen());
+}
+
+Expected<DeviceTensor> DeviceTensor::zeros(int64_t rows, int64_t cols) {
+    auto t = empty(rows, cols, QuantFormat::None);
+    if (!t) return t.error();
+    if (t.value().bytes_ && cudaMemset(t.value().data_, 0, t.value().bytes_) != cudaSuccess) {
+        cudaGetLastError();
+        return Error{"zeros: memset failed"};
+    }
+    return std::move(t.value());
+}
+
+Expected<DeviceTensor> DeviceTensor::ones(int64_t rows, int64_t cols) {
+    std::vector<float> h(static_cast<size_t>(std::max<int64_t>(rows * cols, 0)), 1.0f);
+    return from_host(h.data(), rows, cols);
+}
+
+Expected<DeviceTensor> DeviceTensor::randn(int64_t rows, int64_t cols) {
+    std::vector<float> h(static_cast<size_t>(std::max<int64_t>(rows * cols, 0)));
+    randn_fill(h.data(), h.size());
+    return from_host(h.data(), rows, cols);
+}
+
 DeviceTensor DeviceTensor::view(void* data, int64_t rows, int64_t cols, DType dtype, QuantFormat quant, int device) {
     DeviceTensor t;
     t.data_ = data;
@@ -433,3 +471,5 @@ Expected<void> synchronize() {
 }
 
 }  // namespace axon::cuda
+
+extern "C" void axon_cuda_randn_fill(float* host, size_t n) { axon::cuda::randn_fill(host, n); }

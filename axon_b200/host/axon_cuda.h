@@ -112,6 +112,13 @@ public:
     // blocks otherwise.
     static Expected<DeviceTensor> empty(int64_t rows, int64_t cols, QuantFormat quant = QuantFormat::None);
     static Expected<DeviceTensor> from_host(const float* host, int64_t rows, int64_t cols);
+    // Tensor::zeros / ones / randn (tensor.cpp:17-47) on the device, fp32.
+    // randn draws from one process-wide std::mt19937 seeded 42 through a
+    // fresh std::normal_distribution<float>(0, 1) per call, as the
+    // reference does, so a sequence of calls gives the reference's values.
+    static Expected<DeviceTensor> zeros(int64_t rows, int64_t cols);
+    static Expected<DeviceTensor> ones(int64_t rows, int64_t cols);
+    static Expected<DeviceTensor> randn(int64_t rows, int64_t cols);
     // Wraps existing device memory (not owned).
     static DeviceTensor view(void* data, int64_t rows, int64_t cols, DType dtype, QuantFormat quant, int device);
 
@@ -226,4 +233,12 @@ void set_stream(axq_stream_t stream);
 axq_stream_t current_stream();
 Expected<void> synchronize();
 
+// The next n values of DeviceTensor::randn's process-wide sequence, into
+// host memory (one call = one randn call of n elements).
+void randn_fill(float* host, size_t n);
+
 }  // namespace axon::cuda
+
+// C linkage of randn_fill, so a test can compare the sequence with the
+// reference's Tensor::randn from another language.
+extern "C" void axon_cuda_randn_fill(float* host, size_t n);

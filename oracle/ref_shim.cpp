@@ -243,6 +243,14 @@ int ref_matmul_f32(const float* a, const float* b, float* out, int64_t M, int64_
     return 0;
 }
 
+// Tensor::randn (tensor.cpp:36-47) of n fp32 elements, copied to out (the
+// reference's process-wide generator advances as in the reference).
+void ref_randn(int64_t n, float* out) {
+    Runtime rt;
+    Tensor t = Tensor::randn(rt, {n});
+    std::memcpy(out, t.storage()->data, static_cast<size_t>(n) * sizeof(float));
+}
+
 // save_tensor (serialize.cpp:84-96) of one tensor; 0 on success.
 int ref_save_tensor(const char* path, const int64_t* shape, int ndims, int dtype, int quant, const void* data,
                     size_t bytes) {

@@ -86,10 +86,46 @@ void run_format(QuantFormat f, const char* name) {
     }
 }
 
+// Tensor::zeros / ones / randn on the device, and the fp32 "matmul" kernel
+// over them (fp32 A routes there like choose_gemm_strategy's fp32 path).
+void run_factories_and_f32() {
+    auto z = DeviceTensor::zeros(3, 5);
+    auto o = DeviceTensor::ones(5, 2);
+    CHECK(static_cast<bool>(z) && static_cast<bool>(o));
+    std::vector<float> expect(20);
+    randn_fill(expect.data(), expect.size());  // the sequence the next randn continues
+    auto r = DeviceTensor::randn(4, 5);
+    CHECK(static_cast<bool>(r));
+    std::vector<float> zh(15, 1.0f), oh(10, 0.0f), rh(20), rh2(20);
+    CHECK(static_cast<bool>(z.value().to_host(zh.data(), zh.size() * 4)));
+    CHECK(static_cast<bool>(o.value().to_host(oh.data(), oh.size() * 4)));
+    CHECK(static_cast<bool>(r.value().to_host(rh.data(), rh.size() * 4)));
+    for (float v : zh) CHECK(v == 0.0f);
+    for (float v : oh) CHECK(v == 1.0f);
+    bool differs = false;  // a later call continues the generator
+    for (size_t i = 0; i < rh.size(); ++i) differs |= (rh[i] != expect[i]);
+    CHECK(differs);
+    for (float v : rh) CHECK(std::isfinite(v) && std::fabs(v) < 10.0f);
+    // out[4 x 2] = randn[4 x 5] . ones[5 x 2]: each entry is a row sum
+    auto out = DeviceTensor::empty(4, 2);
+    CHECK(static_cast<bool>(out));
+    CHECK(static_cast<bool>(matmul(out.value(), r.value(), o.value())));
+    CHECK(static_cast<bool>(synchronize()));
+    std::vector<float> y(8);
+    CHECK(static_cast<bool>(out.value().to_host(y.data(), y.size() * 4)));
+    for (int i = 0; i < 4; ++i) {
+        float sum = 0.0f;
+        for (int k = 0; k < 5; ++k) sum += rh[i * 5 + k];
+        CHECK_MSG(std::fabs(y[2 * i] - sum) <= 1e-5f * (1.0f + std::fabs(sum)) && y[2 * i] == y[2 * i + 1],
+                  "f32 matmul row " + std::to_string(i));
+    }
+}
+
 }  // namespace
 
 int main() {
     register_cuda_kernels();
+    run_factories_and_f32();
     run_format(QuantFormat::Q8_0, "Q8_0");
     run_format(QuantFormat::Q4_0, "Q4_0");
     run_format(QuantFormat::Q2_K, "Q2_K");
