@@ -4,6 +4,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <atomic>
 #include <string>
 
 #include "axq_common.cuh"
@@ -81,15 +82,15 @@ int validate_matmul_ptrs(int fmt, const void* a_q, const void* b, const void* ou
 void set_last_error(const std::string& msg) { g_last_error = msg; }
 
 int device_sm_count() {
-    static int cache[64] = {0};
+    static std::atomic<int> cache[64];  // 0 until looked up; every thread stores the same value
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-    if (cache[dev] == 0) {
-        int n = 0;
+    int n = cache[dev].load(std::memory_order_relaxed);
+    if (n == 0) {
         if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-        cache[dev] = n;
+        cache[dev].store(n, std::memory_order_relaxed);
     }
-    return cache[dev];
+    return n;
 }
 
 }  // namespace axq

@@ -817,16 +817,9 @@ cudaError_t launch_gemm(const void* w, const float* x, float* out, int64_t M, in
     }
     const int smem = 1024 + a.npk * a.pk_bytes + a.nab * a.b_bytes;
     auto kern = (a.aligned && Dq<F>::A > 1) ? gemm_kernel<F, Dq<F>::A> : gemm_kernel<F, 1>;
-    static int configured[2][64] = {{0}};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    static std::atomic<int> configured[2][64];
     const int ai = (a.aligned && Dq<F>::A > 1) ? 1 : 0;
-    if (smem > configured[ai][dev]) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e != cudaSuccess) return e;
-        configured[ai][dev] = smem;
-    }
+    if (cudaError_t e = ensure_dyn_smem(kern, smem, configured[ai]); e != cudaSuccess) return e;
     const int grid = g.nrt * g.nct * g.splits;
     {
         cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kThreadsGemm), smem, s, a);

@@ -899,15 +899,8 @@ GemvPlan plan_gemv(int nt) {
 template <int F, int NT, int AL>
 cudaError_t launch_nt(const GemvPlan& p, const GemvArgs& a, cudaStream_t s) {
     auto kern = gemv_kernel<F, NT, AL>;
-    static int configured[64] = {0};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if (p.smem > configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, p.smem);
-        if (e != cudaSuccess) return e;
-        configured[dev] = p.smem;
-    }
+    static std::atomic<int> configured[64];
+    if (cudaError_t e = ensure_dyn_smem(kern, p.smem, configured); e != cudaSuccess) return e;
     cudaError_t e = launch_pdl(kern, dim3(p.grid), dim3(kThreads), p.smem, s, a);
     return e != cudaSuccess ? e : cudaGetLastError();
 }

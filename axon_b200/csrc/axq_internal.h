@@ -8,6 +8,9 @@
 #include <utility>
 #include <cuda_runtime.h>
 
+#include <atomic>
+#include <mutex>
+
 #include "../../include/axq.h"
 
 namespace axq {
@@ -61,6 +64,26 @@ cudaError_t gemv_dispatch(int fmt, const void* w, const void* w2, const float* x
 size_t gemm_workspace_bytes(int fmt, int64_t M, int64_t K, int64_t N);
 cudaError_t gemm_dispatch(int fmt, const void* w, const float* x, float* out, int64_t M, int64_t K, int64_t N, int flags,
                           void* ws, size_t ws_bytes, int* err, cudaStream_t s);
+
+// Raises `kernel`'s dynamic shared-memory limit on the current device to at
+// least `smem`.  `cfg` (one per kernel instantiation, zero-initialised
+// static storage) records the largest limit set per device; the limit only
+// grows, under a lock, so host threads launching at once never lower it
+// below what another is about to launch with.
+template <typename Kernel>
+cudaError_t ensure_dyn_smem(Kernel kernel, int smem, std::atomic<int> (&cfg)[64]) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (smem <= cfg[dev].load(std::memory_order_acquire)) return cudaSuccess;
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lk(mu);
+    if (smem <= cfg[dev].load(std::memory_order_relaxed)) return cudaSuccess;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e == cudaSuccess) cfg[dev].store(smem, std::memory_order_release);
+    return e;
+}
 
 // Launches `kernel` on `s` with programmatic stream serialization: it may
 // be scheduled while the previous kernel of the stream is still running and
