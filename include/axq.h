@@ -3,9 +3,17 @@
  *
  * Drop-in device implementation of the reference's (ruwwww/Axon) GGML-style
  * quantize / dequantize / quantized-matmul CPU path.  Plain pointers and
- * sizes only: every pointer argument except host-side results is device
- * memory on the current CUDA device; every call is asynchronous on `stream`
- * (NULL = legacy default stream) and allocates nothing.
+ * sizes only: unless stated beside a call, pointer arguments other than
+ * host-side results are device memory on the current CUDA device, and calls
+ * are asynchronous on `stream` (NULL = legacy default stream).  quantize,
+ * dequantize and the matmuls allocate nothing (scratch is the caller's
+ * workspace, or the built-in scratch of axq_matmul_noalloc); the
+ * communicator, symmetric-buffer, fp32 (cuBLAS) and .axon entry points
+ * allocate as described beside them.
+ *
+ * Threads: any host thread may call the library, concurrently with others,
+ * except that one communicator, one symmetric buffer and one .axon file
+ * handle are each used by one thread at a time.
  *
  * Errors follow the reference's Expected<void>/Error{message} convention
  * (include/axon/core/expected.h:9-62): 0 is success, a non-zero AXQ_ERR_*
