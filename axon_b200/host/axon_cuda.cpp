@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdio>
 #include <mutex>
 #include <random>
 #include <vector>
@@ -287,6 +288,94 @@ std::mt19937& rand_gen() {
     return gen;
 }
 }  // namespace
+
+namespace {
+
+struct AxonFileHandle {
+    void* h = nullptr;
+    ~AxonFileHandle() {
+        if (h) axq_axon_close(h);
+    }
+};
+
+Expected<DeviceTensor> read_record(void* h, uint32_t i, std::string* name) {
+    axq_axon_tensor info{};
+    if (axq_axon_info(h, i, &info) != AXQ_OK) return last_error("load_tensor");
+    int64_t numel = 1;
+    for (uint32_t d = 0; d < info.ndims; ++d) numel *= info.shape[d];
+    const int64_t cols = info.ndims ? info.shape[info.ndims - 1] : 1;
+    int64_t rows = cols ? numel / cols : 0;
+    int64_t c = cols;
+    const QuantFormat q = static_cast<QuantFormat>(info.quant);
+    if (info.layout == AXQ_AXON_FLAT) {  // blocks over the flattened tensor: one row
+        rows = 1;
+        c = numel;
+    }
+    if (q == QuantFormat::None && info.dtype != 0)
+        return Error{std::string("load_tensor: '") + info.name + "' is not Float32 (dtype " +
+                     std::to_string(info.dtype) + "); DeviceTensor holds fp32 or packed data"};
+    auto t = DeviceTensor::empty(rows, c, q);
+    if (!t) return t.error();
+    if (t.value().size_bytes() && axq_axon_read(h, i, t.value().data(), t.value().size_bytes(), t_stream) != AXQ_OK)
+        return last_error("load_tensor");
+    if (name) *name = info.name;
+    return std::move(t.value());
+}
+
+axq_axon_tensor record_of(const std::string& name, const DeviceTensor& t) {
+    axq_axon_tensor info{};
+    std::snprintf(info.name, sizeof(info.name), "%s", name.c_str());
+    info.dtype = 0;  // Float32, also for packed tensors (the reference's metadata does the same)
+    info.quant = static_cast<uint32_t>(t.quant().format);
+    info.ndims = 2;
+    info.shape[0] = t.rows();
+    info.shape[1] = t.cols();
+    info.data_bytes = t.size_bytes();
+    return info;
+}
+
+}  // namespace
+
+Expected<void> save_checkpoint(const std::vector<std::pair<std::string, const DeviceTensor*>>& tensors,
+                               const std::string& path) {
+    std::vector<axq_axon_tensor> infos;
+    std::vector<const void*> data;
+    for (const auto& [name, t] : tensors) {
+        if (!t) return Error{"save_checkpoint: NULL tensor '" + name + "'"};
+        if (name.size() >= AXQ_AXON_NAME_BYTES) return Error{"save_checkpoint: name too long: " + name};
+        infos.push_back(record_of(name, *t));
+        data.push_back(t->data());
+    }
+    if (axq_axon_save(path.c_str(), static_cast<uint32_t>(infos.size()), infos.data(), data.data(), t_stream) != AXQ_OK)
+        return last_error("save_checkpoint");
+    return {};
+}
+
+Expected<void> save_tensor(const DeviceTensor& t, const std::string& path) {
+    return save_checkpoint({{"data", &t}}, path);
+}
+
+Expected<std::vector<std::pair<std::string, DeviceTensor>>> load_checkpoint(const std::string& path) {
+    AxonFileHandle f;
+    uint32_t n = 0;
+    if (axq_axon_open(path.c_str(), &f.h, &n) != AXQ_OK) return last_error("load_checkpoint");
+    std::vector<std::pair<std::string, DeviceTensor>> out;
+    for (uint32_t i = 0; i < n; ++i) {
+        std::string name;
+        auto t = read_record(f.h, i, &name);
+        if (!t) return t.error();
+        out.emplace_back(std::move(name), std::move(t.value()));
+    }
+    return out;
+}
+
+Expected<DeviceTensor> load_tensor(const std::string& path) {
+    AxonFileHandle f;
+    uint32_t n = 0;
+    if (axq_axon_open(path.c_str(), &f.h, &n) != AXQ_OK) return last_error("load_tensor");
+    if (n < 1) return Error{"No tensors in file"};  // serialize.cpp:105
+    return read_record(f.h, 0, nullptr);
+}
 
 void randn_fill(float* host, size_t n) {
     std::lock_guard<std::mutex> lk(g_rand_mu);

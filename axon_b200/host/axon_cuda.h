@@ -233,6 +233,18 @@ void set_stream(axq_stream_t stream);
 axq_stream_t current_stream();
 Expected<void> synchronize();
 
+// ---- .axon files (serialize.h / serialize.cpp:84-203) -----------------------
+// The reference's byte format, through axq_axon_* (include/axq.h).  Packed
+// records load with their QuantFormat (the reference's loaders drop it);
+// DeviceTensor holds fp32 or packed data, so other plain dtypes are refused.
+// load_checkpoint returns every record in file order (the reference's fills
+// a Module's parameters in that order).
+Expected<void> save_tensor(const DeviceTensor& t, const std::string& path);  // one record named "data"
+Expected<DeviceTensor> load_tensor(const std::string& path);                 // the first record
+Expected<void> save_checkpoint(const std::vector<std::pair<std::string, const DeviceTensor*>>& tensors,
+                               const std::string& path);
+Expected<std::vector<std::pair<std::string, DeviceTensor>>> load_checkpoint(const std::string& path);
+
 // The next n values of DeviceTensor::randn's process-wide sequence, into
 // host memory (one call = one randn call of n elements).
 void randn_fill(float* host, size_t n);

@@ -4,6 +4,8 @@
 // compare (bit-exact), and multiply through matmul() (routed by the A
 // operand's format, as choose_gemm_strategy does) for a GEMV-sized and a
 // GEMM-sized batch, within max|y - y_ref| <= 1e-3 * max|y_ref|.
+#include <algorithm>
+#include <cstdio>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
@@ -121,10 +123,65 @@ void run_factories_and_f32() {
     }
 }
 
+// .axon front doors over files written by the reference's serializer
+// (tests/golden/axon_*.axon) and a device round trip.
+void run_axon(const std::string& dir) {
+    auto q = load_tensor(dir + "/axon_q4k.axon");
+    CHECK_MSG(static_cast<bool>(q), q ? "" : q.error().message);
+    if (!q) return;
+    CHECK(q.value().quant().format == QuantFormat::Q4_K && q.value().rows() == 4 && q.value().cols() == 512);
+    std::vector<uint8_t> packed(q.value().size_bytes());
+    CHECK(static_cast<bool>(q.value().to_host(packed.data(), packed.size())));
+    std::vector<float> b(512 * 3);
+    randn_fill(b.data(), b.size());
+    auto bd = DeviceTensor::from_host(b.data(), 512, 3);
+    auto out = DeviceTensor::empty(4, 3);
+    CHECK(static_cast<bool>(bd) && static_cast<bool>(out));
+    CHECK(static_cast<bool>(matmul(out.value(), q.value(), bd.value())));
+    CHECK(static_cast<bool>(synchronize()));
+    std::vector<float> y(12), y_ref(12);
+    CHECK(static_cast<bool>(out.value().to_host(y.data(), y.size() * 4)));
+    CHECK(orc_matmul(static_cast<int>(QuantFormat::Q4_K), packed.data(), b.data(), y_ref.data(), 4, 512, 3) == 0);
+    double m = 0, e = 0;
+    for (int i = 0; i < 12; ++i) {
+        m = std::max(m, static_cast<double>(std::fabs(y_ref[i])));
+        e = std::max(e, static_cast<double>(std::fabs(y[i] - y_ref[i])));
+    }
+    CHECK_MSG(e <= 1e-3 * m, "loaded Q4_K matmul rel_err=" + std::to_string(e / m));
+    auto flat = load_tensor(dir + "/axon_q8_0_flat.axon");  // blocks over all 120 elements: one row
+    CHECK(static_cast<bool>(flat) && flat.value().rows() == 1 && flat.value().cols() == 120);
+    auto f = load_tensor(dir + "/axon_f32.axon");
+    CHECK(static_cast<bool>(f) && f.value().rows() == 2 && f.value().cols() == 3);
+    if (f) {
+        std::vector<float> fh(6);
+        CHECK(static_cast<bool>(f.value().to_host(fh.data(), 24)));
+        for (int i = 0; i < 6; ++i) CHECK(fh[i] == static_cast<float>(i));
+    }
+    auto ck = load_checkpoint(dir + "/axon_checkpoint.axon");  // holds an int32 record
+    CHECK(!ck && ck.error().message.find("not Float32") != std::string::npos);
+    // device round trip: a packed and an fp32 tensor
+    auto r = DeviceTensor::randn(3, 7);
+    CHECK(static_cast<bool>(r));
+    const std::string path = dir + "/../cpp/_build/roundtrip.axon";
+    CHECK(static_cast<bool>(save_checkpoint({{"w", &q.value()}, {"r", &r.value()}}, path)));
+    auto back = load_checkpoint(path);
+    CHECK(static_cast<bool>(back) && back.value().size() == 2);
+    if (back) {
+        std::vector<uint8_t> p2(back.value()[0].second.size_bytes());
+        CHECK(back.value()[0].first == "w" && p2.size() == packed.size());
+        CHECK(static_cast<bool>(back.value()[0].second.to_host(p2.data(), p2.size())) && p2 == packed);
+        std::vector<float> r1(21), r2(21);
+        CHECK(static_cast<bool>(r.value().to_host(r1.data(), 84)));
+        CHECK(static_cast<bool>(back.value()[1].second.to_host(r2.data(), 84)) && r1 == r2);
+    }
+    std::remove(path.c_str());
+}
+
 }  // namespace
 
-int main() {
+int main(int argc, char** argv) {
     register_cuda_kernels();
+    if (argc > 1) run_axon(argv[1]);
     run_factories_and_f32();
     run_format(QuantFormat::Q8_0, "Q8_0");
     run_format(QuantFormat::Q4_0, "Q4_0");

@@ -62,6 +62,6 @@ def test_registry_and_front_door_errors(host_lib):
 @pytest.mark.gpu
 def test_mirror_matches_oracle_on_gpu(host_lib, cuda):
     exe = _build("quant_cuda_test", with_oracle=True)
-    r = subprocess.run([exe], capture_output=True, text=True, timeout=600)
+    r = subprocess.run([exe, os.path.join(ROOT, "tests", "golden")], capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "0 failures" in r.stdout
