@@ -224,9 +224,11 @@ int axq_axon_info(void* file, uint32_t index, axq_axon_tensor* info_out) {
 int axq_axon_read(void* file, uint32_t index, void* dst, size_t dst_bytes, axq_stream_t stream) {
     const char* fn = "axq_axon_read";
     auto* af = static_cast<AxonFile*>(file);
-    if (!af || !dst) return io_fail(AXQ_ERR_INVALID, std::string(fn) + ": NULL argument");
+    if (!af) return io_fail(AXQ_ERR_INVALID, std::string(fn) + ": NULL file");
     if (index >= af->t.size()) return io_fail(AXQ_ERR_INVALID, std::string(fn) + ": index out of range");
     const axq_axon_tensor& t = af->t[index];
+    if (t.data_bytes == 0) return AXQ_OK;  // an empty tensor: nothing to read, dst may be NULL
+    if (!dst) return io_fail(AXQ_ERR_INVALID, std::string(fn) + ": NULL destination");
     if (dst_bytes < t.data_bytes)
         return io_fail(AXQ_ERR_INVALID, std::string(fn) + ": tensor '" + t.name + "' has " +
                                             std::to_string(t.data_bytes) + " bytes; the destination holds " +

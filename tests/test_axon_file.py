@@ -171,3 +171,33 @@ def test_read_argument_errors(tmp_path):
             check(L.axq_axon_read(h, 1, small.ctypes.data, small.nbytes, None))
     finally:
         L.axq_axon_close(h)
+
+
+def test_edge_records(tmp_path):
+    """A file with no tensors, a 0-d (scalar) tensor, an empty tensor and a
+    packed tensor with an empty row range, each written by the reference's
+    writer where it can express them, read back here."""
+    import oracle
+    import axon_b200 as ax
+    ref = oracle.ref()
+    p0 = str(tmp_path / "none.axon")
+    open(p0, "wb").write(struct.pack("<III", 0x4E4F5841, 1, 0))  # what save_checkpoint writes for no parameters
+    assert ax.axon_records(p0) == [] and ax.load_axon(p0, device="cpu") == {}
+    with pytest.raises(ax.AxqError, match="no tensors"):
+        ax.load_tensor(p0, device="cpu")
+    ps = str(tmp_path / "scalar.axon")
+    pe = str(tmp_path / "empty.axon")
+    if ref is not None:
+        ref.save_tensor(ps, [], 0, 0, np.array([2.5], dtype=np.float32))
+        ref.save_tensor(pe, [0, 4], 0, 0, np.zeros(0, dtype=np.float32))
+    else:
+        ax.save_tensor(torch.tensor(2.5), ps)
+        ax.save_tensor(torch.zeros(0, 4), pe)
+    s = ax.load_tensor(ps, device="cpu")
+    assert s.shape == () and float(s) == 2.5
+    e = ax.load_tensor(pe, device="cpu")
+    assert tuple(e.shape) == (0, 4)
+    pq = str(tmp_path / "q0.axon")
+    ax.save_tensor(ax.QTensor(torch.zeros(1, dtype=torch.uint8), (0, 256), ax.QuantFormat.Q4_K), pq)
+    r = ax.axon_records(pq)[0]
+    assert r.layout == "rows" and r.data_bytes == 0 and r.shape == (0, 256)
