@@ -10,6 +10,7 @@
 // process that is torch's copy), so this library has no link-time
 // dependency on it.  One handle per device, created on first use.
 #include <dlfcn.h>
+#include <cstdlib>
 
 #include <cublas_v2.h>
 
@@ -36,7 +37,10 @@ Cublas& cublas() {
     static std::once_flag once;
     std::call_once(once, [] {
         void* h = dlopen("libcublas.so.12", RTLD_NOW | RTLD_GLOBAL);
-        if (!h) h = dlopen("/usr/local/cuda/lib64/libcublas.so.12", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) {  // not on the loader's path: try the toolkit named by CUDA_HOME
+            const char* home = std::getenv("CUDA_HOME");
+            if (home && *home) h = dlopen((std::string(home) + "/lib64/libcublas.so.12").c_str(), RTLD_NOW | RTLD_GLOBAL);
+        }
         if (!h) {
             c.error = std::string("cannot load libcublas.so.12: ") + dlerror();
             return;

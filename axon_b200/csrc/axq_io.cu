@@ -95,15 +95,21 @@ int io_fail(int code, const std::string& msg) {
 // Checks one record's metadata and sets its layout; "" if consistent.
 std::string classify(axq_axon_tensor& t) {
     if (t.ndims > AXQ_AXON_MAX_DIMS) return "more than " + std::to_string(AXQ_AXON_MAX_DIMS) + " dimensions";
+    // The dims come from the file: every product is checked for overflow, and
+    // element counts are capped at 2^56 so that no byte count below can wrap.
     int64_t numel = 1;
     for (uint32_t d = 0; d < t.ndims; ++d) {
         if (t.shape[d] < 0) return "negative dimension";
-        numel *= t.shape[d];
+        if (__builtin_mul_overflow(numel, t.shape[d], &numel) || numel > (int64_t{1} << 56))
+            return "shape has too many elements";
     }
     if (t.quant == 0) {
         const size_t eb = dtype_bytes(t.dtype);
         if (!eb) return "unknown dtype " + std::to_string(t.dtype);
-        if (t.data_bytes != static_cast<uint64_t>(numel) * eb) return "data size does not match shape and dtype";
+        uint64_t bytes = 0;
+        if (__builtin_mul_overflow(static_cast<uint64_t>(numel), static_cast<uint64_t>(eb), &bytes))
+            return "shape has too many elements";
+        if (t.data_bytes != bytes) return "data size does not match shape and dtype";
         t.layout = AXQ_AXON_PLAIN;
         return "";
     }

@@ -14,8 +14,9 @@
 // Host code cannot pass the array's name to a kernel (on the host that name
 // is only a stand-in, not a device address), so the first call on each
 // device — with that device current — looks its device address up with
-// cudaGetSymbolAddress and caches it.  Nothing here calls cudaMalloc,
-// cudaFree or any allocating library routine.
+// cudaGetSymbolAddress and caches it (so cudaDeviceReset, which unloads the
+// module and with it the array, is unsupported after that first call).
+// Nothing here calls cudaMalloc, cudaFree or any allocating library routine.
 #include <mutex>
 #include <string>
 
@@ -75,4 +76,18 @@ extern "C" int axq_matmul_noalloc(int fmt, const void* a_q, const float* b, floa
         }
     }
     return axq_matmul(fmt, a_q, b, out, M, K, N, flags, scratch, AXQ_NOALLOC_SCRATCH_BYTES, stream);
+}
+
+// The built-in scratch starts with the same status word as a caller's
+// workspace: a kernel that gave up a bounded wait sets it, and the next call's
+// first kernel clears it.  Reading it therefore reports the last
+// axq_matmul_noalloc call issued on the current device.
+extern "C" int axq_noalloc_status(axq_stream_t stream) {
+    void* scratch = nullptr;
+    cudaError_t e = scratch_for_current_device(&scratch);
+    if (e != cudaSuccess) {
+        set_last_error(std::string("axq_noalloc_status: scratch lookup failed: ") + cudaGetErrorString(e));
+        return AXQ_ERR_CUDA;
+    }
+    return axq_workspace_status(scratch, stream);
 }

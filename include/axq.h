@@ -125,12 +125,24 @@ int axq_gate_up_silu(int fmt, const void* w_gate, const void* w_up, const float*
  *  - The first call on each device looks up the scratch's device address
  *    (cudaGetSymbolAddress) with that device current; make that first call
  *    before any stream capture.
+ *  - The scratch's address is cached per device, so cudaDeviceReset (which
+ *    unloads the array) is unsupported after that first call.
  *  - All calls on a device share one scratch and it keeps the last call's
  *    contents (each call clears what must start at zero): calls that may
  *    overlap on the GPU (different streams, or host threads) race — serialize
- *    them on one stream. */
+ *    them on one stream.
+ *  - A bounded wait that gave up inside the kernels does not change the
+ *    return code (the call only enqueues work); axq_noalloc_status reports it. */
 int axq_matmul_noalloc(int fmt, const void* a_q, const float* b, float* out, int64_t M, int64_t K, int64_t N,
                        unsigned flags, axq_stream_t stream);
+
+/* Synchronizes `stream` and reports AXQ_ERR_TIMEOUT if the last
+ * axq_matmul_noalloc call issued on the current device gave up a bounded wait
+ * (its output is then not valid), 0 otherwise.  The scratch is shared, so
+ * "last" means the last call on this device from any stream or thread; read
+ * it after synchronizing with the call of interest and before the next one.
+ * No reference counterpart. */
+int axq_noalloc_status(axq_stream_t stream);
 
 /* Synchronizes `stream` and reports whether a kernel that used `workspace`
  * gave up a bounded wait (AXQ_ERR_TIMEOUT) — 0 otherwise. */

@@ -128,6 +128,7 @@ def _corrupt(tmp_path, name, mutate):
     ("dtype", "unknown dtype"),
     ("quant", "unknown quant_type"),
     ("name", "name longer"),
+    ("huge", "too many elements"),
 ])
 def test_malformed_files_are_refused_with_a_message(tmp_path, case, fragment):
     import axon_b200 as ax
@@ -142,6 +143,8 @@ def test_malformed_files_are_refused_with_a_message(tmp_path, case, fragment):
         "dtype": None,
         "quant": lambda r: r.__setitem__(slice(first + 8, first + 12), struct.pack("<I", 9)),
         "name": lambda r: r.__setitem__(slice(first, first + 4), struct.pack("<I", 300)),
+        # first record's two dims (after its 16-byte header and 10-byte name): 2^40 x 2^40 overflows int64
+        "huge": lambda r: r.__setitem__(slice(first + 26, first + 42), struct.pack("<QQ", 1 << 40, 1 << 40)),
     }
     if case == "dtype":
         recs = ax.axon_records(gold("axon_checkpoint.axon"))

@@ -4,10 +4,11 @@ Callers behind Axon's KernelRegistry receive only their tensors (no
 allocator handle), and C hosts that own all device memory may forbid
 cudaMalloc, so they cannot supply axq_matmul's workspace.  This entry point
 runs the same kernels on a scratch array built into the library.  Here it is
-called through the C ABI and compared with axq_matmul (caller workspace) on
-two consecutive calls each, for a GEMV-sized and a GEMM-sized problem, and
-its size limit is checked.  This file is named so that pytest collects it
-last.
+called through the C ABI and compared with axq_matmul (caller workspace) and
+with the CPU oracle on two consecutive calls each, for a GEMV-sized and a
+GEMM-sized problem; its status word (axq_noalloc_status) reads success after
+each call, and its size limit is checked.  This file is named so that pytest
+collects it last.
 """
 import ctypes
 
@@ -41,18 +42,21 @@ def _run_both(orc, fmt, M, K, N, seed):
         out = torch.full((M, N), float("nan"), device="cuda")
         st = L.axq_matmul_noalloc(F, q.data_ptr(), b.data_ptr(), out.data_ptr(), M, K, N, 0, stream)
         assert st == 0, L.axq_last_error()
+        assert L.axq_noalloc_status(stream) == 0, L.axq_last_error()  # no bounded wait gave up
         outs.append(out)
     torch.cuda.synchronize()
-    return ref_out.cpu().numpy(), [o.cpu().numpy() for o in outs]
+    y_orc = orc.matmul(fmt, q.cpu().numpy(), b.cpu().numpy(), M, K)
+    return ref_out.cpu().numpy(), [o.cpu().numpy() for o in outs], y_orc
 
 
 @pytest.mark.parametrize("fmt", ["Q4_0", "Q4_K", "Q6_K"])
 @pytest.mark.parametrize("M,K,N", [(96, 4096, 1), (256, 2048, 64)])
 def test_noalloc_matches_workspace_entry_point(cuda, orc, fmt, M, K, N):
-    ref_out, outs = _run_both(orc, fmt, M, K, N, seed=M + N)
+    ref_out, outs, y_orc = _run_both(orc, fmt, M, K, N, seed=M + N)
     for y in outs:
         assert np.isfinite(y).all()
         assert rel_err(y, ref_out) <= TOL
+        assert rel_err(y, y_orc) <= TOL
 
 
 def test_noalloc_rejects_sizes_beyond_its_scratch(cuda):
