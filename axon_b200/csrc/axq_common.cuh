@@ -19,6 +19,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 namespace axq {
@@ -80,6 +81,16 @@ __device__ __forceinline__ float h2f_ref(uint32_t h) {
     uint32_t mant = (h & 0x3FFu) << 13;
     uint32_t u = (e == 0) ? sign : (e == 31) ? (sign | 0x7F800000u | mant) : (sign | ((e + 112u) << 23) | mant);
     return __uint_as_float(u);
+}
+
+// fp16 bits -> float with subnormals flushed to (signed) zero, as the
+// reference's decoder does (a scale that decodes to zero must give exact
+// zeros); normal, infinite and NaN values convert as the hardware does.  For
+// the matmul kernels, whose scales only need the value (dequantize, which
+// must reproduce NaN bit patterns too, uses h2f_ref).
+__device__ __forceinline__ float h2f_flush(uint32_t h) {
+    return (h & 0x7C00u) ? __half2float(__ushort_as_half(static_cast<unsigned short>(h & 0xFFFFu)))
+                         : __uint_as_float((h & 0x8000u) << 16);
 }
 
 // get_scale_min_k4 (cpu_backend.cpp:681-689): 6-bit scale/min j of a

@@ -165,14 +165,6 @@ __device__ __forceinline__ void ldg_w(const uint8_t* p, uint32_t* out) {
     }
 }
 
-// fp16 bits -> float with subnormals flushed to (signed) zero, as the
-// reference's decoder does (a scale that decodes to zero must give exact
-// zeros); normal, infinite and NaN values convert as the hardware does.
-__device__ __forceinline__ float h2f_flush(uint32_t h) {
-    return (h & 0x7C00u) ? __half2float(__ushort_as_half(static_cast<unsigned short>(h & 0xFFFFu)))
-                         : __uint_as_float((h & 0x8000u) << 16);
-}
-
 // Byte j (0..7, run time) of the little-endian pair (lo, hi).
 __device__ __forceinline__ uint32_t byte_rt(uint32_t lo, uint32_t hi, int j) {
     return prmt(lo, hi, static_cast<uint32_t>(j)) & 0xFFu;

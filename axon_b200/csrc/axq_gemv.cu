@@ -109,16 +109,20 @@ __device__ __forceinline__ float act_u(const ActCG& X, int t) {
 // so the L1 latency of the loads overlaps the dot products of earlier runs.
 // SX: also fetch the integer run sums.  Indexes are compile-time after
 // unrolling, so the arrays live in registers (only D+1 runs at a time).
-template <int NT, bool SX, int H>
+// LHM: the runs are consumed lh-major (runs 0, 2, 4, 6, then 1, 3, 5, 7:
+// the first 16 elements of each 32-element group, then the second 16), the
+// order in which the 16-element-run formats decode their packed words.
+template <int NT, bool SX, int H, int D1 = 3, bool LHM = false>
 struct ActPipe {
-    static constexpr int D = (NT == 1) ? 3 : (NT == 2 ? 2 : 1);
+    static constexpr int D = (NT == 1) ? D1 : (NT == 2 ? 2 : 1);
+    static constexpr int run_of(int k) { return LHM ? 2 * (k & 3) + (k >> 2) : k; }
     ActCG X;
     int ntok;
     Run16 r[NT][8];
     int sx[NT][8];
     __device__ __forceinline__ ActPipe(ActCG x, int nt) : X(x), ntok(nt) {
 #pragma unroll
-        for (int j = 0; j < D; ++j) load(j);
+        for (int j = 0; j < D; ++j) load(run_of(j));
     }
     __device__ __forceinline__ void load(int j) {
 #pragma unroll
@@ -129,9 +133,9 @@ struct ActPipe {
             if constexpr (SX) sx[t][j] = isx1(X, tt, 8 * H + j);
         }
     }
-    // Call at the start of run j (0..7 within the half).
-    __device__ __forceinline__ void step(int j) {
-        if (j + D < 8) load(j + D);
+    // Call at the start of the k-th run consumed (0..7 within the half).
+    __device__ __forceinline__ void step(int k) {
+        if (k + D < 8) load(run_of(k + D));
     }
 };
 
@@ -194,7 +198,9 @@ __device__ __forceinline__ void k4sm(const uint32_t* hw, int& sc, int& m) {
 // MS <= 16*15*16*32385.
 template <int H, int AL> struct RowQ2K {
     static constexpr int RL = 16;
-    uint32_t hd, scw[2], mw[2], w[8];
+    static constexpr bool LH_MAJOR = true;  // the qs words of one lh at a time
+    uint32_t hd, scw[2], mw[2], w[4];
+    const uint8_t* p;
     __device__ __forceinline__ void load(const uint8_t* cg) {
         uint32_t h[1], sc[2];
         ldw<1, AL>(cg, h);
@@ -205,18 +211,23 @@ template <int H, int AL> struct RowQ2K {
             scw[i] = sc[i] & 0x0F0F0F0Fu;
             mw[i] = (sc[i] >> 4) & 0x0F0F0F0Fu;
         }
-        ldw<8, AL>(cg + 20 + 32 * H, w);
+        p = cg;
+    }
+    // qs[32H + 16LH .. +15]: the four code words of runs 2s + LH, s = 0..3
+    template <int LH>
+    __device__ __forceinline__ void prep() {
+        ldw<4, AL>(p + 20 + 32 * H + 16 * LH, w);
     }
     template <int J>
     __device__ __forceinline__ void run(uint32_t* q, int& sc, int& m) const {
-        constexpr int s = J >> 1, lh = J & 1;
+        constexpr int s = J >> 1;
 #pragma unroll
-        for (int v = 0; v < 4; ++v) q[v] = w[4 * lh + v] & (0x03030303u << (2 * s));
+        for (int v = 0; v < 4; ++v) q[v] = w[v] & (0x03030303u << (2 * s));
         sc = static_cast<int>(__byte_perm(scw[J >> 2], 0u, 0x4440u | (J & 3))) << (6 - 2 * s);
         m = static_cast<int>(__byte_perm(mw[J >> 2], 0u, 0x4440u | (J & 3)));
     }
-    __device__ __forceinline__ float dscale() const { return h2f_ref(hd & 0xFFFFu) * (1.0f / 64.0f); }
-    __device__ __forceinline__ float mscale() const { return h2f_ref(hd >> 16); }
+    __device__ __forceinline__ float dscale() const { return h2f_flush(hd & 0xFFFFu) * (1.0f / 64.0f); }
+    __device__ __forceinline__ float mscale() const { return h2f_flush(hd >> 16); }
 };
 
 // Bit select: bits of x where m is set, bits of y elsewhere (one LOP3).
@@ -242,9 +253,11 @@ __device__ __forceinline__ int sext_byte(uint32_t w) {
 // |HS|, |LS| <= 8 * 2048 * 16*7*127 < 2.4e8; |MS| <= 8 * 128 * 16*32385.
 template <int H, int AL> struct RowQ3K {
     static constexpr int RL = 16;
-    uint32_t hd, sv[2], a[8], b[8];  // sv: 4 * (scale - 32) of the half's eight runs, one signed byte each
+    static constexpr bool LH_MAJOR = true;  // hmask and qs words of one lh at a time
+    uint32_t hd, sv[2], a[4], b[4];  // sv: 4 * (scale - 32) of the half's eight runs, one signed byte each
+    const uint8_t* p;
     __device__ __forceinline__ void load(const uint8_t* cg) {
-        uint32_t h[1], s12[3], hm[8], w[8];
+        uint32_t h[1], s12[3];
         ld_words<1>(cg + 108, h);
         hd = h[0];
         ld_words<3>(cg + 96, s12);
@@ -262,10 +275,17 @@ template <int H, int AL> struct RowQ3K {
         // to the top of its byte it is 4 * (v - 32) as a signed byte
 #pragma unroll
         for (int i = 0; i < 2; ++i) sv[i] = (s6[i] ^ 0x20202020u) << 2;
-        ld_words<8>(cg, hm);
-        ld_words<8>(cg + 32 + 32 * H, w);
+        p = cg;
+    }
+    // hmask[16LH ..] and qs[32H + 16LH ..] merged into the 3-bit codes of runs
+    // 2s + LH: a = s = 0 (bits 0-2) and s = 2 (bits 4-6), b = s = 1 and s = 3
+    template <int LH>
+    __device__ __forceinline__ void prep() {
+        uint32_t hm[4], w[4];
+        ld_words<4>(p + 16 * LH, hm);
+        ld_words<4>(p + 32 + 32 * H + 16 * LH, w);
 #pragma unroll
-        for (int v = 0; v < 8; ++v) {
+        for (int v = 0; v < 4; ++v) {
             // high bit of s = 0 / 2 (bits 4H, 4H+2 of each hmask byte) to bits 2 / 6
             a[v] = bsel(0x33333333u, w[v], bsel(0x0F0F0F0Fu, shl<2 - 4 * H>(hm[v]), shl<4 - 4 * H>(hm[v])));
             // s = 1 / 3: fields at bits 2-3 / 6-7 moved down by 2; high bits 4H+1, 4H+3
@@ -274,15 +294,15 @@ template <int H, int AL> struct RowQ3K {
     }
     template <int J>
     __device__ __forceinline__ void run(uint32_t* q, int& sc, int& m) const {
-        constexpr int s = J >> 1, lh = J & 1;
+        constexpr int s = J >> 1;
         constexpr uint32_t MASK = (s >= 2) ? 0x70707070u : 0x07070707u;
 #pragma unroll
-        for (int v = 0; v < 4; ++v) q[v] = ((s & 1) ? b[4 * lh + v] : a[4 * lh + v]) & MASK;
+        for (int v = 0; v < 4; ++v) q[v] = ((s & 1) ? b[v] : a[v]) & MASK;
         m = sext_byte<J & 3>(sv[J >> 2]);  // 4 * (scale - 32)
         sc = (s < 2) ? (m << 4) : m;
     }
-    __device__ __forceinline__ float dscale() const { return h2f_ref(hd & 0xFFFFu) * (1.0f / 64.0f); }
-    __device__ __forceinline__ float mscale() const { return h2f_ref(hd & 0xFFFFu); }
+    __device__ __forceinline__ float dscale() const { return h2f_flush(hd & 0xFFFFu) * (1.0f / 64.0f); }
+    __device__ __forceinline__ float mscale() const { return h2f_flush(hd & 0xFFFFu); }
 };
 
 // Q4_K {d, dmin, scales[12], qs[128]}: group G = 4H + J covers nibble G&1 of
@@ -290,6 +310,7 @@ template <int H, int AL> struct RowQ3K {
 // |HS| <= 8 * 63*16 * 32*15*127 < 5e8; MS <= 8*63*32*32385.
 template <int H, int AL> struct RowQ4K {
     static constexpr int RL = 32;
+    static constexpr bool LH_MAJOR = false;
     uint32_t hw[4];
     const uint8_t* p;
     __device__ __forceinline__ void load(const uint8_t* cg) {
@@ -307,14 +328,15 @@ template <int H, int AL> struct RowQ4K {
         k4sm<G>(hw, s6, m);
         sc = (G & 1) ? s6 : (s6 << 4);
     }
-    __device__ __forceinline__ float dscale() const { return h2f_ref(hw[0] & 0xFFFFu) * 0.0625f; }
-    __device__ __forceinline__ float mscale() const { return h2f_ref(hw[0] >> 16); }
+    __device__ __forceinline__ float dscale() const { return h2f_flush(hw[0] & 0xFFFFu) * 0.0625f; }
+    __device__ __forceinline__ float mscale() const { return h2f_flush(hw[0] >> 16); }
 };
 
 // Q5_K {d, dmin, scales[12], qh[32], qs[128]}: as Q4_K plus bit G of qh[l]
 // as bit 4 of the code (no in-place factor): |HS| <= 8 * 63 * 32*31*127.
 template <int H, int AL> struct RowQ5K {
     static constexpr int RL = 32;
+    static constexpr bool LH_MAJOR = false;
     uint32_t hw[4], qh[8];
     const uint8_t* p;
     __device__ __forceinline__ void load(const uint8_t* cg) {
@@ -334,8 +356,8 @@ template <int H, int AL> struct RowQ5K {
         }
         k4sm<G>(hw, sc, m);
     }
-    __device__ __forceinline__ float dscale() const { return h2f_ref(hw[0] & 0xFFFFu); }
-    __device__ __forceinline__ float mscale() const { return h2f_ref(hw[0] >> 16); }
+    __device__ __forceinline__ float dscale() const { return h2f_flush(hw[0] & 0xFFFFu); }
+    __device__ __forceinline__ float mscale() const { return h2f_flush(hw[0] >> 16); }
 };
 
 // Q6_K {ql[128], qh[64], scales[16], d}: half H; run J = 2T + lh: low 4 bits
@@ -344,6 +366,7 @@ template <int H, int AL> struct RowQ5K {
 // |HS| <= 16 * 128 * 16*63*127 < 3e8, |MS| <= 16*128*16*32385 < 1.1e9.
 template <int H, int AL> struct RowQ6K {
     static constexpr int RL = 16;
+    static constexpr bool LH_MAJOR = false;
     uint32_t hd, sc2[2];
     const uint8_t* p;
     __device__ __forceinline__ void load(const uint8_t* cg) {
@@ -366,8 +389,8 @@ template <int H, int AL> struct RowQ6K {
         }
         sc = m = static_cast<int>(static_cast<int8_t>(bt<J>(sc2)));
     }
-    __device__ __forceinline__ float dscale() const { return h2f_ref(hd & 0xFFFFu); }
-    __device__ __forceinline__ float mscale() const { return h2f_ref(hd & 0xFFFFu) * 32.0f; }
+    __device__ __forceinline__ float dscale() const { return h2f_flush(hd & 0xFFFFu); }
+    __device__ __forceinline__ float mscale() const { return h2f_flush(hd & 0xFFFFu) * 32.0f; }
 };
 
 template <int F, int H, int AL> struct RowOf;
@@ -379,26 +402,46 @@ template <int H, int AL> struct RowOf<F_Q6_K, H, AL> { using T = RowQ6K<H, AL>; 
 
 // Half CG of two rows (c0, c1) of a K-quant format: every activation run is
 // loaded once and dotted with both rows' codes; acc[i][t] += row i's part.
+// Formats whose runs are 16 elements and whose code words are shared by the
+// runs 2s + lh of one lh (Q2_K, Q3_K) decode lh-major: the words of one lh
+// are loaded (and merged) once, then its four runs follow, so only those
+// words are live.
 template <int F, int H, int AL, int NT>
 __device__ __forceinline__ void kquant_half(const uint8_t* c0, const uint8_t* c1, const ActCG& X, int ntok,
-                                            float (*acc)[NT]) {
+                                            bool valid, float (*acc)[NT]) {
     using R = typename RowOf<F, H, AL>::T;
     constexpr int RL = R::RL, NW = RL / 4, NR = 128 / RL;
+    constexpr bool LHM = R::LH_MAJOR;
+    static_assert(!LHM || RL == 16, "lh-major order is for 16-element runs");
     R r0, r1;
     r0.load(c0);
     r1.load(c1);
-    ActPipe<NT, true, H> P(X, ntok);
+    // Q6_K decodes from shared memory per run and keeps more live values: a
+    // shallower activation prefetch keeps it inside the register budget
+    ActPipe<NT, true, H, (F == F_Q6_K) ? 2 : 3, LHM> P(X, ntok);
     int hs[2][NT], ls[2][NT], ms[2][NT];
 #pragma unroll
     for (int t = 0; t < NT; ++t) hs[0][t] = hs[1][t] = ls[0][t] = ls[1][t] = ms[0][t] = ms[1][t] = 0;
-    static_for<NR>([&](auto Jc) {
-        constexpr int J = decltype(Jc)::value, j0 = J * (RL / 16);
+    static_for<NR>([&](auto Kc) {
+        constexpr int K = decltype(Kc)::value;  // position in the decode order
+        constexpr int J = LHM ? 2 * (K & 3) + (K >> 2) : K;
+        constexpr int j0 = J * (RL / 16);
+        if constexpr (LHM) {
+            if constexpr ((K & 3) == 0) {
+                r0.template prep<(K >> 2)>();
+                r1.template prep<(K >> 2)>();
+            }
+        }
         uint32_t qa[NW], qb[NW];
         int sa, ma, sb, mb;
         r0.template run<J>(qa, sa, ma);
         r1.template run<J>(qb, sb, mb);
-        P.step(j0);
-        if constexpr (RL == 32) P.step(j0 + 1);
+        if constexpr (LHM) {
+            P.step(K);
+        } else {
+            P.step(j0);
+            if constexpr (RL == 32) P.step(j0 + 1);
+        }
 #pragma unroll
         for (int t = 0; t < NT; ++t) {  // padded tokens compute on the last token's data; never written
             int ha, la, hb, lb, sx = P.sx[t][j0];
@@ -421,8 +464,10 @@ __device__ __forceinline__ void kquant_half(const uint8_t* c0, const uint8_t* c1
         const float u = act_u(X, t);
         const float dot0 = fmaf(254.0f, static_cast<float>(hs[0][t]), static_cast<float>(ls[0][t]));
         const float dot1 = fmaf(254.0f, static_cast<float>(hs[1][t]), static_cast<float>(ls[1][t]));
-        acc[0][t] = fmaf(u, fmaf(d0, dot0, -m0 * static_cast<float>(ms[0][t])), acc[0][t]);
-        acc[1][t] = fmaf(u, fmaf(d1, dot1, -m1 * static_cast<float>(ms[1][t])), acc[1][t]);
+        const float v0 = fmaf(u, fmaf(d0, dot0, -m0 * static_cast<float>(ms[0][t])), acc[0][t]);
+        const float v1 = fmaf(u, fmaf(d1, dot1, -m1 * static_cast<float>(ms[1][t])), acc[1][t]);
+        acc[0][t] = valid ? v0 : acc[0][t];
+        acc[1][t] = valid ? v1 : acc[1][t];
     }
 }
 
@@ -436,7 +481,7 @@ __device__ __forceinline__ void kquant_half(const uint8_t* c0, const uint8_t* c1
 // skipped.
 template <int F, int H, int NT>
 __device__ __forceinline__ void block32_half(const uint8_t* c0, const uint8_t* c1, int nblk_valid, const ActCG& X,
-                                             int ntok, float (*acc)[NT]) {
+                                             int ntok, bool valid, float (*acc)[NT]) {
     constexpr bool Q8 = (F == F_Q8_0);
     constexpr int BB = Q8 ? 34 : 18;
     ActPipe<NT, !Q8, H> P(X, ntok);
@@ -449,8 +494,8 @@ __device__ __forceinline__ void block32_half(const uint8_t* c0, const uint8_t* c
             uint32_t h0[1], h1[1];
             ld_words<1>(c0 + BB * B, h0);
             ld_words<1>(c1 + BB * B, h1);
-            const float da = h2f_ref(h0[0] & 0xFFFFu) * (Q8 ? 1.0f : 0.0625f);
-            const float db = h2f_ref(h1[0] & 0xFFFFu) * (Q8 ? 1.0f : 0.0625f);
+            const float da = h2f_flush(h0[0] & 0xFFFFu) * (Q8 ? 1.0f : 0.0625f);
+            const float db = h2f_flush(h1[0] & 0xFFFFu) * (Q8 ? 1.0f : 0.0625f);
             uint32_t qa[8], qb[8];
             if constexpr (Q8) {
                 ld_words<8>(c0 + BB * B + 2, qa);
@@ -493,8 +538,9 @@ __device__ __forceinline__ void block32_half(const uint8_t* c0, const uint8_t* c
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
         const float u = act_u(X, t);
-        acc[0][t] = fmaf(u, accf[0][t], acc[0][t]);
-        acc[1][t] = fmaf(u, accf[1][t], acc[1][t]);
+        const float v0 = fmaf(u, accf[0][t], acc[0][t]), v1 = fmaf(u, accf[1][t], acc[1][t]);
+        acc[0][t] = valid ? v0 : acc[0][t];
+        acc[1][t] = valid ? v1 : acc[1][t];
     }
 }
 
@@ -507,9 +553,9 @@ template <int F> struct Lane {
     static constexpr int PERM = (F == F_Q4_0) ? 1 : 0;
     template <int H, int AL, int NT>
     __device__ __forceinline__ static void half(const uint8_t* c0, const uint8_t* c1, int nblk_valid, const ActCG& X,
-                                                int ntok, float (*acc)[NT]) {
-        if constexpr (F == F_Q8_0 || F == F_Q4_0) block32_half<F, H, NT>(c0, c1, nblk_valid, X, ntok, acc);
-        else kquant_half<F, H, AL, NT>(c0, c1, X, ntok, acc);
+                                                int ntok, bool valid, float (*acc)[NT]) {
+        if constexpr (F == F_Q8_0 || F == F_Q4_0) block32_half<F, H, NT>(c0, c1, nblk_valid, X, ntok, valid, acc);
+        else kquant_half<F, H, AL, NT>(c0, c1, X, ntok, valid, acc);
     }
 };
 
@@ -641,6 +687,125 @@ __device__ __forceinline__ uintptr_t slot_base(const GemvArgs& a, int slot) {
     return reinterpret_cast<uintptr_t>((a.pair && slot >= 8) ? a.w2 : a.w);
 }
 
+// Consumer warps of one half H (warps 4H..4H+3) over every unit of this CTA:
+// wait for each stage, decode the lane's half CG of two rows, release the
+// stage; per unit, combine the partial sums across lanes and
+// warps and store the outputs (or, for peer-store calls, every rank's copy).
+template <int F, int NT, int AL, int H>
+__device__ __forceinline__ void consume(const GemvArgs& a, uint8_t* stages, float* red, uint64_t* full,
+                                        uint64_t* empty, volatile int* abort_flag, unsigned* entry_flag, int warp,
+                                        int lane) {
+    using L = Lane<F>;
+    static_assert((kStageCG * L::CGB) % 16 == 0, "a K-step must keep row segments' 16-byte phase");
+    const int cgl = 4 * (warp & 3) + (lane >> 3);  // CG slot in the stage
+    const int pr = lane & 7;                        // rows pr and pr + 8 of the unit
+    float acc[2][NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) acc[0][t] = acc[1][t] = 0.0f;
+    int s = 0, unit_par = 0;
+    uint32_t phase = 0;
+    bool entered = (a.npeers == 0);  // every rank has entered this call
+    bool aborted = false;
+    const uintptr_t base0 = slot_base(a, pr), base1 = slot_base(a, pr + 8);
+    for (int64_t u = blockIdx.x; u < a.units; u += gridDim.x, unit_par ^= 1) {
+        const int64_t row0 = slot_row(a, u, pr), row1 = slot_row(a, u, pr + 8);
+        const bool ok0 = row0 < a.rows, ok1 = row1 < a.rows;
+        // Each row segment sits in its stage row at the segment's offset
+        // modulo 16 (the bulk copy starts at the 16-byte boundary below it);
+        // K-steps advance by step_bytes, a multiple of 16, so the offset is
+        // the row start's for every K-step of the unit.
+        const int mis0 = static_cast<int>((base0 + static_cast<uintptr_t>(row0 * a.rb)) & 15);
+        const int mis1 = ok1 ? static_cast<int>((base1 + static_cast<uintptr_t>(row1 * a.rb)) & 15) : mis0;
+        const uint8_t* stage_lane0 = stages + cgl * L::CGB + pr * a.rs + mis0;
+        // a row past the end decodes row0 again; its sum is never written
+        const uint8_t* stage_lane1 = ok1 ? stages + cgl * L::CGB + (pr + 8) * a.rs + mis1 : stage_lane0;
+        const uint8_t* act = a.act + static_cast<int64_t>(cgl) * a.act_cg_stride;
+        int cg = cgl, nbv = a.nblk_row - cgl * 8;
+        for (int ks = 0; ks < a.nks; ++ks, cg += kStageCG, nbv -= kStageCG * 8, act += kStageCG * a.act_cg_stride) {
+            if (!aborted && !wait_or_abort(&full[s], phase, abort_flag)) {
+                aborted = true;
+                if (lane == 0) {
+                    *abort_flag = 1;
+                    atomicExch(a.err, 1);
+                }
+            }
+            {
+                // Every lane decodes (no divergent branch around the decode):
+                // a lane whose row is past the end or whose CG is past the row
+                // reads stale stage bytes and the last CG's activations, and
+                // its sums are dropped (valid = false).
+                const bool valid = ok0 && cg < a.ncg && !aborted;
+                const int sb = s * a.stage_bytes;
+                const uint8_t* c0 = stage_lane0 + sb;
+                const uint8_t* c1 = stage_lane1 + sb;
+                const uint8_t* xa = cg < a.ncg ? act : a.act + static_cast<int64_t>(a.ncg - 1) * a.act_cg_stride;
+                L::template half<H, AL, NT>(c0, c1, nbv, ActCG{xa}, a.ntok, valid, acc);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+            if (++s == a.nstages) {
+                s = 0;
+                phase ^= 1;
+            }
+        }
+        // combine the four CG slots of each warp, then the warps
+        float* rp = red + unit_par * (kConsumerWarps * kUnitRows * NT);
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                float v = acc[i][t];
+                v += __shfl_xor_sync(0xffffffffu, v, 8);
+                v += __shfl_xor_sync(0xffffffffu, v, 16);
+                if (lane < 8) rp[(warp * kUnitRows + pr + 8 * i) * NT + t] = v;
+                acc[i][t] = 0.0f;
+            }
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+        if (!entered && warp == 0) {
+            if (lane == 0 && ld_acquire_cta_shared_u32(entry_flag) == 0) {
+                // the producer's entry wait (normally long done); this bound
+                // outlasts the producer's own
+                const uint64_t t0 = globaltimer_ns();
+                while (ld_acquire_cta_shared_u32(entry_flag) == 0) {
+                    if (globaltimer_ns() - t0 > 2 * kPeerWaitNs) {
+                        atomicExch(a.err, 1);
+                        break;
+                    }
+                    __nanosleep(100);
+                }
+            }
+            __syncwarp();
+            entered = true;
+        }
+        const int64_t orow = a.pair ? u * 8 + lane : u * kUnitRows + lane;
+        if (warp == 0 && lane < (a.pair ? 8 : 16) && orow < a.rows) {
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                if (t < a.ntok) {
+                    float v = 0.0f;
+#pragma unroll
+                    for (int w2 = 0; w2 < kConsumerWarps; ++w2) v += rp[(w2 * kUnitRows + lane) * NT + t];
+                    if (a.pair) {  // v = gate row; combine with the same row of W_up
+                        float up = 0.0f;
+#pragma unroll
+                        for (int w2 = 0; w2 < kConsumerWarps; ++w2) up += rp[(w2 * kUnitRows + lane + 8) * NT + t];
+                        v = v / (1.0f + expf(-v)) * up;
+                    }
+                    if (a.npeers > 0) {
+                        const int64_t gi = (a.row_offset + orow) * a.out_ld + t;
+                        for (int g = 0; g < a.npeers; ++g) a.peer_out[g][gi] = v;
+                    } else if (a.out_tokmajor) {
+                        a.out[t * a.out_ld + orow] = v;
+                    } else {
+                        a.out[orow * a.out_ld + t] = v;
+                    }
+                }
+            }
+        }
+    }
+}
+
 template <int F, int NT, int AL>
 __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
     using L = Lane<F>;
@@ -750,7 +915,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
     // ---------------- consumer warps ----------------
     // Warp w decodes half h = w/4 of the stage's CGs 4(w%4)..4(w%4)+3; lane l
     // takes CG 4(w%4) + l/8 for rows l%8 and l%8 + 8 of the unit, so every
-    // activation run it loads serves two rows.
+    // activation run it loads serves two rows.  The half is a template
+    // argument: one warp-uniform branch here instead of one per K-step.
     pdl_wait();  // activation records of this call are complete
     // Peer-store calls: every earlier kernel of the stream has completed now
     // (the activation prep waited for its predecessor before finishing), so
@@ -758,102 +924,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
     // the fewest units) counts this rank as entered at every rank.
     if (a.npeers > 0 && tid == 0 && blockIdx.x == gridDim.x - 1)
         for (int g = 0; g < a.npeers; ++g) red_add_sys_u32(a.peer_entry[g], 1u);
-    const int h = warp >> 2;
-    const int cgl = 4 * (warp & 3) + (lane >> 3);  // CG slot in the stage
-    const int pr = lane & 7;                        // rows pr and pr + 8 of the unit
-    float acc[2][NT];
-#pragma unroll
-    for (int t = 0; t < NT; ++t) acc[0][t] = acc[1][t] = 0.0f;
-    int s = 0, unit_par = 0;
-    uint32_t phase = 0;
-    bool entered = (a.npeers == 0);  // every rank has entered this call
-    for (int64_t u = blockIdx.x; u < a.units; u += gridDim.x, unit_par ^= 1) {
-        const int64_t row0 = slot_row(a, u, pr), row1 = slot_row(a, u, pr + 8);
-        const uintptr_t base0 = slot_base(a, pr), base1 = slot_base(a, pr + 8);
-        const bool ok0 = row0 < a.rows, ok1 = row1 < a.rows;
-        for (int ks = 0; ks < a.nks; ++ks) {
-            if (!wait_or_abort(&full[s], phase, abort_flag)) {
-                if (lane == 0) {
-                    *abort_flag = 1;
-                    atomicExch(a.err, 1);
-                }
-            }
-            const int cg = ks * kStageCG + cgl;
-            if (ok0 && cg < a.ncg && !*abort_flag) {
-                const int64_t off = static_cast<int64_t>(ks) * step_bytes;
-                const uint8_t* st = stages + s * a.stage_bytes + cgl * L::CGB;
-                const uint8_t* c0 = st + pr * a.rs + ((base0 + static_cast<uintptr_t>(row0 * a.rb + off)) & 15);
-                // a row past the end decodes row0 again; its sum is never written
-                const uint8_t* c1 =
-                    ok1 ? st + (pr + 8) * a.rs + ((base1 + static_cast<uintptr_t>(row1 * a.rb + off)) & 15) : c0;
-                const ActCG X{a.act + static_cast<int64_t>(cg) * a.act_cg_stride};
-                const int nbv = a.nblk_row - cg * 8;
-                if (h == 0) L::template half<0, AL, NT>(c0, c1, nbv, X, a.ntok, acc);
-                else L::template half<1, AL, NT>(c0, c1, nbv, X, a.ntok, acc);
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
-            if (++s == a.nstages) {
-                s = 0;
-                phase ^= 1;
-            }
-        }
-        // combine the four CG slots of each warp, then the warps
-        float* rp = red + unit_par * (kConsumerWarps * kUnitRows * NT);
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-#pragma unroll
-            for (int t = 0; t < NT; ++t) {
-                float v = acc[i][t];
-                v += __shfl_xor_sync(0xffffffffu, v, 8);
-                v += __shfl_xor_sync(0xffffffffu, v, 16);
-                if (lane < 8) rp[(warp * kUnitRows + pr + 8 * i) * NT + t] = v;
-                acc[i][t] = 0.0f;
-            }
-        }
-        asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
-        if (!entered && warp == 0) {
-            if (lane == 0 && ld_acquire_cta_shared_u32(entry_flag) == 0) {
-                // the producer's entry wait (normally long done); this bound
-                // outlasts the producer's own
-                const uint64_t t0 = globaltimer_ns();
-                while (ld_acquire_cta_shared_u32(entry_flag) == 0) {
-                    if (globaltimer_ns() - t0 > 2 * kPeerWaitNs) {
-                        atomicExch(a.err, 1);
-                        break;
-                    }
-                    __nanosleep(100);
-                }
-            }
-            __syncwarp();
-            entered = true;
-        }
-        const int64_t orow = a.pair ? u * 8 + lane : u * kUnitRows + lane;
-        if (warp == 0 && lane < (a.pair ? 8 : 16) && orow < a.rows) {
-#pragma unroll
-            for (int t = 0; t < NT; ++t) {
-                if (t < a.ntok) {
-                    float v = 0.0f;
-#pragma unroll
-                    for (int w2 = 0; w2 < kConsumerWarps; ++w2) v += rp[(w2 * kUnitRows + lane) * NT + t];
-                    if (a.pair) {  // v = gate row; combine with the same row of W_up
-                        float up = 0.0f;
-#pragma unroll
-                        for (int w2 = 0; w2 < kConsumerWarps; ++w2) up += rp[(w2 * kUnitRows + lane + 8) * NT + t];
-                        v = v / (1.0f + expf(-v)) * up;
-                    }
-                    if (a.npeers > 0) {
-                        const int64_t gi = (a.row_offset + orow) * a.out_ld + t;
-                        for (int g = 0; g < a.npeers; ++g) a.peer_out[g][gi] = v;
-                    } else if (a.out_tokmajor) {
-                        a.out[t * a.out_ld + orow] = v;
-                    } else {
-                        a.out[orow * a.out_ld + t] = v;
-                    }
-                }
-            }
-        }
-    }
+    if (warp < 4) consume<F, NT, AL, 0>(a, stages, red, full, empty, abort_flag, entry_flag, warp, lane);
+    else consume<F, NT, AL, 1>(a, stages, red, full, empty, abort_flag, entry_flag, warp, lane);
     if (a.npeers > 0 && warp == 0) {
         // The warp's peer stores are ordered before the CTA counts itself
         // (a GPU-scope release, cumulative over the warp barrier); the last

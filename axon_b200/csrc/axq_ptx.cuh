@@ -129,9 +129,12 @@ __device__ __forceinline__ int dp4a_s8(uint32_t a, uint32_t b, int c) {
 // past the data, so shared buffers carry slack.
 template <int N>
 __device__ __forceinline__ void ld_words(const uint8_t* p, uint32_t* out) {
-    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
-    const uint32_t* base = reinterpret_cast<const uint32_t*>(a & ~static_cast<uintptr_t>(3));
-    const uint32_t sh = static_cast<uint32_t>(a & 3) * 8;
+    // The aligned base is formed by pointer arithmetic (not an integer round
+    // trip), so a pointer into shared memory stays one: the compiler then
+    // emits shared loads instead of generic ones.
+    const uint32_t mis = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(p)) & 3u;
+    const uint32_t* base = reinterpret_cast<const uint32_t*>(p - mis);
+    const uint32_t sh = mis * 8;
     uint32_t w[N + 1];
 #pragma unroll
     for (int i = 0; i <= N; ++i) w[i] = base[i];
