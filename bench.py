@@ -1,16 +1,22 @@
 """Benchmark of the quantized GEMV path on B200.
 
-Workload (the largest configuration, the one sharded across GPUs): per GPU,
-y = x . W^T for W[28672 x 8192] packed in Q2_K, Q3_K and Q5_K (one matmul
-each per step; weights ~ N(0, 0.02^2) plus 0.1% outliers ~ N(0, 0.5^2)),
-x[1 x 8192] ~ N(0,1).  One step = the three GEMVs.  With N GPUs each rank
-holds its own 28672-row shard of a [28672*N x 8192] weight (weak scaling)
-and the outputs are all-gathered over NCCL.  The three packed matrices
-(340 MB per GPU) exceed the 126 MB L2, so no flush is needed between steps.
+Workload (the large low-bit configuration): y = x . W^T for one
+W[28672 x 8192] in each of Q2_K, Q3_K and Q5_K (weights ~ N(0, 0.02^2) plus
+0.1% outliers ~ N(0, 0.5^2), packed by this library), x[1 x 8192] ~ N(0,1).
+One decode pass = the three GEMVs; one step = --passes decode passes (256 by
+default, so the timed region lasts about half a second on one GPU).  With N
+GPUs the same matrices are row-sharded (strong scaling): rank r holds rows
+[r*28672/N, (r+1)*28672/N) of each and its GEMV epilogue stores its output
+rows straight into every rank's copy of the full output over NVLink
+(symmetric buffers, no separate collective).  The three packed matrices
+(340 MB) exceed the 126 MB L2, so consecutive passes read them from HBM.
 
-Metric: packed-weight GB/s over all ranks (higher is better).
+Metric: packed-weight GB/s of the whole job (higher is better).  On one GPU
+the line also carries the batched GEMM (M = 128 tokens, TFLOP/s) and the
+pack sweep (2^30 elements, GB/s read), each with its roofline and the
+reference's CPU figure.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--passes P] [--impl reference]
 
 Under torchrun (N > 1) every rank runs; rank 0 prints one JSON line.
 """
@@ -32,13 +38,16 @@ sys.path.insert(0, ROOT)
 
 ROWS, K_DIM, M_TOK = 28672, 8192, 1
 FORMATS = ("Q2_K", "Q3_K", "Q5_K")
+PASSES = 320
+GEMM_TOKENS = 128
 METRIC = "Quant matmul weight GB/s (GEMV), TOPS (GEMM) at 1/2/4/8 B200 vs AVX2 host"
-WORKLOAD = "low-bit large GEMV: y = x.W^T, W[28672x8192] in Q2_K, Q3_K, Q5_K per GPU, x[1x8192]"
+WORKLOAD = ("low-bit large GEMV: y = x.W^T, W[28672x8192] in Q2_K, Q3_K, Q5_K, x[1x8192], rows sharded "
+            "across the GPUs")
 
 
 def packed_bytes(fmt: str, rows: int = ROWS, cols: int = K_DIM) -> int:
-    be = 256
-    bb = {"Q2_K": 84, "Q3_K": 110, "Q4_K": 144, "Q5_K": 176, "Q6_K": 210}[fmt]
+    be = 32 if fmt in ("Q8_0", "Q4_0") else 256
+    bb = {"Q8_0": 34, "Q4_0": 18, "Q2_K": 84, "Q3_K": 110, "Q4_K": 144, "Q5_K": 176, "Q6_K": 210}[fmt]
     return rows * ((cols + be - 1) // be) * bb
 
 
@@ -178,8 +187,17 @@ class CpuArm:
                 j.close()
 
 
+def bench_config(world: int) -> dict:
+    """The workload's config, identical in both arms."""
+    return {"workload": WORKLOAD, "rows": ROWS, "K": K_DIM, "M": M_TOK, "formats": list(FORMATS),
+            "parallelism": (f"row-shard x{world} ({ROWS // world} rows per GPU), outputs stored into every "
+                            "rank's copy by the GEMV epilogue over NVLink") if world > 1 else "single GPU",
+            "l2": "inputs larger than L2 (340 MB of packed weights per pass)"}
+
+
 def run_reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     if rank != 0:
         return 0
     threads = os.cpu_count() or 1
@@ -202,11 +220,11 @@ def run_reference_arm(args):
     line = {
         "impl": "reference", "metric": METRIC, "value": round(gbs, 4), "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD + " (rank 0's shard)", "rows": rows, "K": K_DIM, "M": M_TOK,
-                   "formats": list(FORMATS), "l2": "inputs larger than L2"},
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": bench_config(world),
+        "step": {"passes": 1, "what": "one decode pass (the three GEMVs over all 28672 rows) per step on the host"},
         "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": arm.kind,
-                         "sample": f"full step: {len(FORMATS)} GEMVs over {rows} rows"},
+                         "sample": f"one pass per step: {len(FORMATS)} GEMVs over all {rows} rows"},
         "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -214,6 +232,21 @@ def run_reference_arm(args):
 
 
 # ------------------------------------------------------------------ GPU arm
+
+def _graph(fn, reps):
+    """fn() captured `reps` times in one CUDA graph, or None if capture fails."""
+    import torch
+    try:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+            for _ in range(reps):
+                fn()
+        return graph
+    except Exception as exc:
+        print(f"graph capture failed, timing eagerly: {exc}", file=sys.stderr)
+        torch.cuda.synchronize()
+        return None
+
 
 def run_gpu(args):
     import torch
@@ -228,49 +261,50 @@ def run_gpu(args):
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    if ROWS % world:
+        raise SystemExit(f"{ROWS} rows do not split over {world} GPUs")
+    rows_l = ROWS // world
+    r0 = rank * rows_l
+    passes = args.passes
 
-    # Seeded synthetic weights, packed on the device by our quantize kernel.
-    g = torch.Generator(device=dev).manual_seed(1000 * rank + 9)
+    # The one matrix per format (same seed on every rank, so the shards are
+    # the rows of one weight), this rank's rows packed by our quantize kernel.
+    g = torch.Generator(device=dev).manual_seed(9)
     qs = {}
     for fmt in FORMATS:
         W = torch.randn(ROWS, K_DIM, device=dev, generator=g) * 0.02
         m = torch.rand(ROWS, K_DIM, device=dev, generator=g) < 0.001
         W[m] = torch.randn(int(m.sum().item()), device=dev, generator=g) * 0.5
-        qt = ax.QTensor.empty(ROWS, K_DIM, ax.QuantFormat[fmt], device=dev)
-        ax.quantize(qt, W, ax.QuantFormat[fmt])
-        del W, m
+        del m
+        qt = ax.QTensor.empty(rows_l, K_DIM, ax.QuantFormat[fmt], device=dev)
+        ax.quantize(qt, W[r0:r0 + rows_l].contiguous(), ax.QuantFormat[fmt])
+        del W
         qs[fmt] = qt
     torch.cuda.synchronize()
     xg = torch.Generator(device=dev).manual_seed(2)
     x = torch.randn(M_TOK, K_DIM, device=dev, generator=xg)
-    # Output of each matmul: token-major [M x rows] on one GPU; with G ranks
-    # the full row-major [G*rows x M] on every rank, this rank's rows written
-    # in place by the matmul and the rest brought by the library's in-place
-    # NCCL all-gather (axq_allgather / axq_matmul_sharded).
     comm = ax.Communicator.from_process_group() if world > 1 else None
-    # one contiguous buffer holds the three outputs, so the end-to-end step
-    # reads them back with a single copy
+    # one GPU: the three outputs in one buffer (one read-back); several: one
+    # symmetric buffer per format holding the full output on every rank
     y_all = torch.empty(len(FORMATS), M_TOK, ROWS, device=dev)
     ys = {f: y_all[i] for i, f in enumerate(FORMATS)}
-    # with several ranks each output lives in a symmetric buffer: the GEMV's
-    # epilogue stores every value into each rank's copy over NVLink
-    symm = {f: ax.SymmetricBuffer(comm, 4 * world * ROWS * M_TOK) for f in FORMATS} if world > 1 else None
+    symm = {f: ax.SymmetricBuffer(comm, 4 * ROWS * M_TOK) for f in FORMATS} if world > 1 else None
     ws = ax.Workspace()
     stream = torch.cuda.current_stream()
 
-    def run_fmt(fmt):
-        """One matmul of the step (activation prep + GEMV) and, with several
-        ranks, the all-gather of its output."""
+    def run_fmt(fmt, q=None, xin=None):
+        q = qs[fmt] if q is None else q
+        xin = x if xin is None else xin
         if world > 1:
-            ax.matmul_sharded_p2p(symm[fmt], qs[fmt], x, world * ROWS, b_tokmajor=True, workspace=ws, wait=False)
+            ax.matmul_sharded_p2p(symm[fmt], q, xin, ROWS, b_tokmajor=True, workspace=ws, wait=False)
         else:
-            ax.linear_q(x, qs[fmt], out=ys[fmt], workspace=ws)
+            ax.linear_q(xin, q, out=ys[fmt], workspace=ws)
 
     def wait_fmt(fmt):
         if world > 1:
             symm[fmt].wait()
 
-    def step():
+    def one_pass():
         # the three matmuls back to back, then their completion waits
         for fmt in FORMATS:
             run_fmt(fmt)
@@ -282,27 +316,21 @@ def run_gpu(args):
             dist.barrier()
         torch.cuda.synchronize()
 
-    def capture(fn):
-        """fn's launches captured once in a CUDA graph (the step is a handful
-        of kernels; replaying removes the host's per-call cost), or None."""
-        try:
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph, capture_error_mode="thread_local"):
-                fn()
-            return graph
-        except Exception as exc:
-            print(f"graph capture failed, timing eagerly: {exc}", file=sys.stderr)
-            torch.cuda.synchronize()
-            return None
+    # a step is `passes` decode passes: graphs of `chunk` passes, replayed
+    chunk = 16 if passes % 16 == 0 else 1
+    for _ in range(3):
+        one_pass()
+    barrier()
+    g_chunk = _graph(one_pass, chunk)
+    replay = (lambda: g_chunk.replay()) if g_chunk is not None else one_pass
+    n_replay = passes // chunk if g_chunk is not None else passes
+
+    def step():
+        for _ in range(n_replay):
+            replay()
 
     for _ in range(max(args.warmup, 3)):
         step()
-    barrier()
-    g_step = capture(step)
-    g_fmt = {f: capture(lambda f=f: (run_fmt(f), wait_fmt(f))) for f in FORMATS}
-    replay = (lambda g, fn: g.replay() if g is not None else fn())
-    for _ in range(max(args.warmup, 3)):
-        replay(g_step, step)
     barrier()
 
     sampler = ClockSampler(local) if rank == 0 else None
@@ -314,109 +342,138 @@ def run_gpu(args):
     barrier()
     t0.record(stream)
     for _ in range(args.steps):
-        replay(g_step, step)
+        step()
     t1.record(stream)
     barrier()
     ms = t0.elapsed_time(t1) / args.steps
-    # each format's matmul alone, replayed back to back (its average duration)
+    clocks = sampler.stop() if sampler else None
+
+    # Each format's matmul alone (prep + GEMV, plus the peer wait on several
+    # GPUs), 16 calls per graph over enough weight copies (> 2x L2) that no
+    # call finds its weights in L2: the per-launch duration of the roofline.
     fmt_ms = {}
     for f in FORMATS:
+        nb = packed_bytes(f, rows_l)
+        ncopy = max(2, -(-(300 << 20) // nb) + 1)
+        copies = [qs[f]] + [ax.QTensor(qs[f].data.clone(), qs[f].shape, qs[f].fmt) for _ in range(ncopy - 1)]
+        it = [0]
+
+        def one(f=f, copies=copies, it=it):
+            run_fmt(f, q=copies[it[0] % len(copies)])
+            wait_fmt(f)
+            it[0] += 1
+
+        for _ in range(3):
+            one()
+        barrier()
+        gf = _graph(one, 16)
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
+        reps = max(4, min(64, int(200.0 / max(ms / passes, 1e-3) / 16)))
         barrier()
         e0.record(stream)
-        for _ in range(args.steps):
-            replay(g_fmt[f], lambda f=f: (run_fmt(f), wait_fmt(f)))
+        for _ in range(reps):
+            if gf is not None:
+                gf.replay()
+            else:
+                for _ in range(16):
+                    one()
         e1.record(stream)
         barrier()
-        fmt_ms[f] = e0.elapsed_time(e1) / args.steps
-    clocks = sampler.stop() if sampler else None
-    del g_step, g_fmt  # graphs holding NCCL calls go before the communicator
-    if world > 1:
-        t = torch.tensor([ms] + [fmt_ms[f] for f in FORMATS], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t[0])
-        fmt_ms = {f: float(t[1 + i]) for i, f in enumerate(FORMATS)}
+        fmt_ms[f] = e0.elapsed_time(e1) / (16 * reps)
+        del gf, copies
+    torch.cuda.empty_cache()
 
-    # End to end through the public API with host buffers: pinned x -> device,
-    # the three matmuls back to back (with several ranks: issued, then waited
-    # for), then every full output -> pinned host.  Copies sit outside the
-    # chain of matmul kernels: a copy between two kernels would stop the next
-    # one from launching while the previous one drains.
+    # End to end through the public API with host buffers: every pass copies
+    # x from pinned host memory, runs the three matmuls and their waits, and
+    # copies the three full outputs back to pinned host memory; `chunk`
+    # passes are captured in one CUDA graph (the copies are graph nodes).
     xh = torch.randn(M_TOK, K_DIM).pin_memory()
-    yh = {f: torch.empty(world * M_TOK * ROWS).pin_memory() for f in FORMATS}
-    yh_all = torch.empty(len(FORMATS) * M_TOK * ROWS).pin_memory()
+    yh = torch.empty(len(FORMATS) * M_TOK * ROWS).pin_memory()
     xd = torch.empty_like(x)
 
-    def e2e_step():
+    def e2e_pass():
         xd.copy_(xh, non_blocking=True)
+        for fmt in FORMATS:
+            run_fmt(fmt, xin=xd)
+        for fmt in FORMATS:
+            wait_fmt(fmt)
         if world > 1:
-            outs = [ax.matmul_sharded_p2p(symm[f], qs[f], xd, world * ROWS, b_tokmajor=True, workspace=ws,
-                                          wait=False) for f in FORMATS]
-            for f in FORMATS:
-                symm[f].wait()
-            for f, y in zip(FORMATS, outs):
-                yh[f].copy_(y.view(-1), non_blocking=True)
+            for i, f in enumerate(FORMATS):
+                yh[i * ROWS * M_TOK:(i + 1) * ROWS * M_TOK].copy_(symm[f].tensor((ROWS * M_TOK,)), non_blocking=True)
         else:
-            for fmt in FORMATS:
-                ax.linear_q(xd, qs[fmt], out=ys[fmt], workspace=ws)
-            yh_all.copy_(y_all.view(-1), non_blocking=True)
+            yh.copy_(y_all.view(-1), non_blocking=True)
 
     for _ in range(3):
-        e2e_step()
+        e2e_pass()
+    barrier()
+    g_e2e = _graph(e2e_pass, chunk)
+    e2e_replay = (lambda: g_e2e.replay()) if g_e2e is not None else e2e_pass
+    e2e_n = passes // chunk if g_e2e is not None else passes
+    for _ in range(2):
+        for _ in range(e2e_n):
+            e2e_replay()
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
-        e2e_step()
+        for _ in range(e2e_n):
+            e2e_replay()
     e1.record(stream)
     barrier()
     e2e_ms = e0.elapsed_time(e1) / args.steps
+    del g_chunk, g_e2e  # graphs go before the communicator
     if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
+        t = torch.tensor([ms, e2e_ms] + [fmt_ms[f] for f in FORMATS], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t[0])
+        ms, e2e_ms = float(t[0]), float(t[1])
+        fmt_ms = {f: float(t[2 + i]) for i, f in enumerate(FORMATS)}
 
-    total_w = world * sum(packed_bytes(f) for f in FORMATS)
+    total_w = sum(packed_bytes(f) for f in FORMATS) * passes
     value = total_w / (ms / 1e3) / 1e9
     e2e_val = total_w / (e2e_ms / 1e3) / 1e9
     peak, peak_kind = load_peaks()
-    # Roofline of each format's matmul: algorithmic bytes (packed weights +
-    # fp32 activations read + fp32 outputs written) / its event-timed duration;
-    # the reported kernel is the one with the largest share of the step.
+    # Roofline of each format's matmul on one GPU's rows: algorithmic bytes
+    # (packed weights + fp32 activations read + fp32 outputs written) / its
+    # event-timed duration; the reported kernel has the largest share.
     by_fmt = {}
     for f in FORMATS:
-        alg = packed_bytes(f) + 4 * K_DIM * M_TOK + 4 * ROWS * M_TOK
+        alg = packed_bytes(f, rows_l) + 4 * K_DIM * M_TOK + 4 * rows_l * M_TOK
         ach = alg / (fmt_ms[f] / 1e3) / 1e9
         by_fmt[f] = {"achieved": round(ach, 1), "frac": round(ach / peak, 4), "ms_per_launch": round(fmt_ms[f], 5),
-                     "algorithmic_bytes": alg, "traffic": load_traffic(f)}
+                     "algorithmic_bytes": alg, "traffic": load_traffic(f) if world == 1 else None}
     dom = max(FORMATS, key=lambda f: fmt_ms[f])
     line = None
     if rank == 0:
+        extra = {}
+        if world == 1 and not args.no_extras:
+            extra["gemm"] = gemm_record(qs, ws, peak)
+            extra["pack"] = pack_record(peak)
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             cpu = cpu_baseline(qs, x)
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "int8-dp4a/f32-acc", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "rows_per_gpu": ROWS, "K": K_DIM, "M": M_TOK,
-                       "timing": "one step captured in a CUDA graph, replayed; e2e is eager through linear_q",
-                       "formats": list(FORMATS), "parallelism": (f"row-shard x{world}, outputs stored into every rank's copy by the GEMV epilogue "
-                                       "over NVLink (symmetric buffers)") if world > 1 else "single GPU",
-                       "l2": "inputs larger than L2 (340 MB of packed weights per GPU)"},
+            "config": bench_config(world),
+            "step": {"passes": passes, "what": "decode passes (the three GEMVs) per step; graphs of "
+                                               f"{chunk} passes replayed"},
             "roofline": {"bound": "hbm", "achieved": by_fmt[dom]["achieved"], "peak": peak, "unit": "GB/s",
                          "frac": by_fmt[dom]["frac"], "peak_source": peak_kind,
                          "kernel": f"matmul {dom} (act prep + gemv), largest share of the step",
                          "ms_per_launch": by_fmt[dom]["ms_per_launch"], "traffic": by_fmt[dom]["traffic"],
                          "by_format": by_fmt},
-            "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * K_DIM * M_TOK,
-                    "d2h_bytes_per_step": 4 * world * M_TOK * ROWS * len(FORMATS)},
+            "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * K_DIM * M_TOK * passes,
+                    "d2h_bytes_per_step": 4 * M_TOK * ROWS * len(FORMATS) * passes,
+                    "how": "public API per pass (linear_q / matmul_sharded_p2p) with the pinned-host copies, "
+                           f"{chunk} passes per CUDA graph"},
             # per matmul: activation prep + GEMV (+ the peer wait with several ranks)
-            "gpu_launches": (3 if world > 1 else 2) * len(FORMATS) * args.steps,
+            "gpu_launches": (3 if world > 1 else 2) * len(FORMATS) * passes * args.steps,
             "clocks": clocks,
         }
+        line.update(extra)
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
@@ -431,8 +488,153 @@ def run_gpu(args):
     return 0
 
 
+def gemm_record(qs, ws, peak_hbm):
+    """Batched GEMM on the same matrices: X[128 x 8192] . W^T for each format
+    (tensor-core path), 16 calls per CUDA graph over rotating weight copies;
+    TFLOP/s = 2*M*N*K / time against the measured dense bf16 peak (the MMA
+    is kind::f16 with fp16 operands, whose dense rate equals bf16's); beside
+    it the reference's CPU matmul at 128 tokens on a row sample."""
+    import torch
+    import axon_b200 as ax
+    dev = qs[FORMATS[0]].data.device
+    n = GEMM_TOKENS
+    mp = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    tpk = json.load(open(mp)).get("bf16_tflops") if os.path.exists(mp) else None
+    tkind = "measured (cuBLAS bf16, burst)" if tpk else "fallback"
+    tpk = float(tpk or 1590.0)
+    X = torch.randn(n, K_DIM, device=dev, generator=torch.Generator(device=dev).manual_seed(12))
+    Y = torch.empty(n, ROWS, device=dev)
+    by = {}
+    for f in FORMATS:
+        nb = packed_bytes(f)
+        copies = [qs[f]] + [ax.QTensor(qs[f].data.clone(), qs[f].shape, qs[f].fmt)
+                            for _ in range(max(1, -(-(300 << 20) // nb)))]
+        it = [0]
+
+        def one(copies=copies, it=it):
+            ax.linear_q(X, copies[it[0] % len(copies)], out=Y, workspace=ws)
+            it[0] += 1
+
+        for _ in range(3):
+            one()
+        torch.cuda.synchronize()
+        gr = _graph(one, 16)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(8):
+            gr.replay() if gr is not None else [one() for _ in range(16)]
+        e1.record()
+        torch.cuda.synchronize()
+        t = e0.elapsed_time(e1) / (8 * 16)
+        by[f] = {"ms": round(t, 5), "tflops": round(2.0 * n * ROWS * K_DIM / (t / 1e3) / 1e12, 1)}
+        del gr, copies
+    torch.cuda.empty_cache()
+    dom = max(FORMATS, key=lambda f: by[f]["ms"])
+    ach = by[dom]["tflops"]
+    rec = {"workload": f"batched GEMM: Y = X.W^T, W[28672x8192] in Q2_K, Q3_K, Q5_K, X[{n}x8192]",
+           "unit": "TFLOP/s", "value": round(sum(2.0 * n * ROWS * K_DIM for _ in FORMATS) /
+                                          (sum(by[f]["ms"] for f in FORMATS) / 1e3) / 1e12, 1),
+           "by_format": by,
+           "roofline": {"bound": "tensor", "achieved": ach, "peak": tpk, "unit": "TFLOP/s",
+                        "frac": round(ach / tpk, 4), "peak_source": tkind,
+                        "kernel": f"matmul {dom} (fp16 activation tiles + tcgen05 GEMM kind::f16)",
+                        "traffic": None}}
+    # the reference's CPU matmul (its kernels re-decode each weight row for
+    # every token column) on 1/64 of the rows, all host threads
+    try:
+        import oracle
+        ref = oracle.ref()
+        threads = os.cpu_count() or 1
+        rows = ROWS // 64
+        xn = X.t().contiguous().cpu().numpy()
+        flops, secs = 0.0, 0.0
+        for f in FORMATS:
+            qn = qs[f].data[: rows * packed_bytes(f, 1)].cpu().numpy()
+            if ref is not None:
+                job = oracle.MatmulJob(ref, f, qn, xn, rows, K_DIM, threads)
+                t0 = time.perf_counter()
+                job.run()
+                secs += time.perf_counter() - t0
+                job.close()
+            else:
+                t0 = time.perf_counter()
+                oracle.orc().matmul(f, qn, xn, rows, K_DIM)
+                secs += time.perf_counter() - t0
+            flops += 2.0 * n * rows * K_DIM
+        rec["cpu_baseline"] = {"value": round(flops / secs / 1e12, 6), "unit": "TFLOP/s",
+                               "cores": threads if ref is not None else 1,
+                               "kind": "reference" if ref is not None else "port",
+                               "sample": f"{rows} of {ROWS} rows x {n} tokens, each format once"}
+    except Exception as exc:  # the baseline is reported, never required
+        rec["cpu_baseline"] = {"unavailable": str(exc)[:200]}
+    return rec
+
+
+def pack_record(peak_hbm):
+    """Pack sweep at 2^30 fp32 elements ([262144 x 4096], N(0,1) with 1%
+    U(-50, 50)) into all seven formats: GB/s of fp32 read per format; the
+    roofline is the slowest format's (fp32 read + packed bytes written) /
+    time against measured HBM; beside it the reference's cpu::quantize on
+    2^24 elements per format over all host threads."""
+    import torch
+    import axon_b200 as ax
+    dev = torch.device("cuda", torch.cuda.current_device())
+    rows, cols = 1 << 18, 4096
+    n = rows * cols
+    g = torch.Generator(device=dev).manual_seed(11)
+    src = torch.randn(rows, cols, device=dev, generator=g)
+    m = torch.rand(rows, cols, device=dev, generator=g) < 0.01
+    src[m] = torch.rand(int(m.sum().item()), device=dev, generator=g) * 100 - 50
+    del m
+    fmts = ("Q8_0", "Q4_0", "Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K")
+    by = {}
+    for f in fmts:
+        F = ax.QuantFormat[f]
+        dst = torch.empty(ax.quantized_size_2d(rows, cols, F), dtype=torch.uint8, device=dev)
+        for _ in range(2):
+            ax.quantize(dst, src, F)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(5):
+            ax.quantize(dst, src, F)
+        e1.record()
+        torch.cuda.synchronize()
+        t = e0.elapsed_time(e1) / 5
+        by[f] = {"ms": round(t, 4), "read_GBps": round(4.0 * n / (t / 1e3) / 1e9, 1),
+                 "hbm_frac": round((4.0 * n + dst.numel()) / (t / 1e3) / 1e9 / peak_hbm, 4),
+                 "bytes": int(4 * n + dst.numel())}
+        del dst
+    sample = src[: (1 << 24) // cols].cpu().numpy()
+    del src
+    torch.cuda.empty_cache()
+    dom = max(fmts, key=lambda f: by[f]["ms"])
+    ach = by[dom]["bytes"] / (by[dom]["ms"] / 1e3) / 1e9
+    peak, kind = load_peaks()
+    rec = {"workload": "pack sweep: 2^30 fp32 elements (rows of 4096) into all seven formats", "unit": "GB/s",
+           "value": round(4.0 * n * len(fmts) / (sum(by[f]["ms"] for f in fmts) / 1e3) / 1e9, 1),
+           "value_is": "fp32 GB/s read over the sweep", "by_format": by,
+           "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
+                        "frac": round(ach / peak, 4), "peak_source": kind, "kernel": f"pack_kernel {dom}",
+                        "traffic": None}}
+    try:
+        threads = os.cpu_count() or 1
+        secs = 0.0
+        for f in fmts:
+            t0 = time.perf_counter()
+            cpu_pack_reference(f, sample, threads)
+            secs += time.perf_counter() - t0
+        import oracle
+        rec["cpu_baseline"] = {"value": round(4.0 * sample.size * len(fmts) / secs / 1e9, 3), "unit": "GB/s",
+                               "cores": threads, "kind": "reference" if oracle.ref() is not None else "port",
+                               "sample": "2^24 elements of the same tensor, each format once"}
+    except Exception as exc:
+        rec["cpu_baseline"] = {"unavailable": str(exc)[:200]}
+    return rec
+
+
 def cpu_baseline(qs, x):
-    """Reference CPU path (rank 0, N=1) on a bounded sample: the full step's
+    """Reference CPU path (rank 0, N=1) on a bounded sample: the pass's
     three GEMVs over 1/4 of the rows, with all host threads, ~10 s."""
     rows = ROWS // 4
     threads = os.cpu_count() or 1
@@ -452,7 +654,7 @@ def cpu_baseline(qs, x):
             break
     arm.close()
     return {"value": round(arm.bytes * n / dt / 1e9, 4), "unit": "GB/s", "cores": threads, "kind": arm.kind,
-            "sample": f"{n} steps of {len(FORMATS)} GEMVs over {rows} of {ROWS} rows"}
+            "sample": f"{n} passes of {len(FORMATS)} GEMVs over {rows} of {ROWS} rows"}
 
 
 # ------------------------------------------------------------------ suite
@@ -741,7 +943,9 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="axon_b200", choices=["axon_b200", "reference"])
+    ap.add_argument("--passes", type=int, default=PASSES, help="decode passes per step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="skip the GEMM and pack records")
     ap.add_argument("--suite", action="store_true", help="time every configuration (one JSON line each)")
     ap.add_argument("--case", default=None, help="time one matmul, FMT:ROWS:K:TOKENS")
     ap.add_argument("--axon", action="store_true", help="time loading the packed weights from an .axon file")
