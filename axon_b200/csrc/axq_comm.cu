@@ -14,6 +14,7 @@
 // GPU, so callers can test their error paths.
 #include <dlfcn.h>
 
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -118,10 +119,12 @@ int allgather_inplace(Comm* c, float* buf, size_t count, cudaStream_t s, const c
 
 // ---- symmetric buffers (CUDA IPC) and the peer-store barrier ---------------
 
-// Layout of one rank's allocation: [data: bytes, rounded to 256] then the
-// control block, one 128-byte line per counter: the completion counter and
-// the entry counter (every rank adds 1 to each per call), this rank's
-// finished-CTA counter and its call count (epoch).
+// Layout of one rank's allocation: [output: bytes, rounded to 256] then the
+// landing area, two copies of the output that the peer-store GEMVs of all
+// ranks fill alternately (call e into copy e & 1), then the control block,
+// one 128-byte line per counter: the completion counter (every rank adds 1
+// per call), this rank's finished-CTA counter, its call count (epoch) and
+// the finished-block counter of its wait kernel.
 constexpr size_t kSymmCtrlBytes = 512;
 constexpr int kMaxRanks = 64;  // the GEMV epilogue stores to every rank in turn
 
@@ -130,36 +133,53 @@ struct Symm {
     size_t bytes = 0, data_bytes = 0;
     uint8_t* local = nullptr;
     std::vector<uint8_t*> peer;       // every rank's allocation (peer[rank] = local)
-    float** d_out = nullptr;          // device: data pointer of every rank
+    float** d_land = nullptr;         // device: landing area of every rank
     unsigned** d_comp = nullptr;      // device: completion counter of every rank
-    unsigned** d_entry = nullptr;     // device: entry counter of every rank
     bool pending = false;             // a peer-store call awaits its axq_symm_wait
     int* pending_err = nullptr;       // status word of that call's workspace
+    size_t pending_floats = 0;        // M x N of that call (what the wait copies out)
+    static uint8_t* land(uint8_t* base, size_t data_bytes) { return base + data_bytes; }
     static unsigned* ctrl(uint8_t* base, size_t data_bytes, int line) {
-        return reinterpret_cast<unsigned*>(base + data_bytes + 128 * line);
+        return reinterpret_cast<unsigned*>(base + 3 * data_bytes + 128 * line);
     }
     unsigned* comp() const { return ctrl(local, data_bytes, 0); }
-    unsigned* entry() const { return ctrl(local, data_bytes, 1); }
-    unsigned* done() const { return ctrl(local, data_bytes, 2); }
-    unsigned* epoch() const { return ctrl(local, data_bytes, 3); }
+    unsigned* done() const { return ctrl(local, data_bytes, 1); }
+    unsigned* epoch() const { return ctrl(local, data_bytes, 2); }
+    unsigned* wait_blocks() const { return ctrl(local, data_bytes, 3); }
 };
 
-// Waits until every rank has signalled this rank for the next epoch (their
-// peer stores of the output are then visible here), then advances the epoch.
-// Bounded: a rank that never signals sets *err and the wait gives up.  It
-// first waits for the stream's earlier kernels, so epochs advance in call
-// order even when several buffers have calls outstanding.
-__global__ void peer_wait_kernel(const unsigned* comp, unsigned* epoch, int nranks, int* err) {
+// Waits until every rank has signalled this rank's completion counter for
+// the next call (its peer stores into this rank's landing copy are then
+// visible), copies that landing copy (n floats) into the output, and
+// advances the call count.  Every block polls; the last block to finish
+// advances the epoch, after every block has read it.  Bounded: a rank that
+// never signals sets *err, the copy proceeds, and the wait gives up.  It
+// first waits for the stream's earlier kernels, so calls complete in order
+// even when several buffers have calls outstanding.
+__global__ void peer_wait_kernel(const unsigned* comp, unsigned* epoch, unsigned* blocks_done, const float* land0,
+                                 int64_t land_stride, float* out, int64_t n, int nranks, int* err) {
     pdl_wait();  // every earlier kernel of the stream (and its epoch update) is complete
     pdl_launch_dependents();
-    if (threadIdx.x != 0) return;
     const unsigned e = *epoch + 1;
-    // every rank adds 1 per call, and no rank can signal call e + 1 before
-    // this rank's wait for call e is over, so the sum reaches e * nranks only
-    // once every rank has signalled call e
-    const unsigned target = e * static_cast<unsigned>(nranks);
-    if (!poll_counter_sys(comp, target, kPeerWaitNs)) atomicExch(err, 1);  // a rank never signalled
-    *epoch = e;
+    if (threadIdx.x == 0) {
+        // every rank adds 1 per call, and no rank can signal call e + 1 before
+        // this rank's wait for call e is over, so the sum reaches e * nranks
+        // only once every rank has signalled call e
+        if (!poll_counter_sys(comp, e * static_cast<unsigned>(nranks), kPeerWaitNs)) atomicExch(err, 1);
+    }
+    __syncthreads();
+    const float* src = land0 + static_cast<int64_t>(e & 1u) * land_stride;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    const int64_t n4 = n / 4;  // landing copies and output are 256-byte aligned
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4; i += stride)
+        reinterpret_cast<float4*>(out)[i] = reinterpret_cast<const float4*>(src)[i];
+    for (int64_t i = 4 * n4 + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
+        out[i] = src[i];
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(blocks_done, 1u) == gridDim.x - 1) {
+        *blocks_done = 0u;
+        *epoch = e;
+    }
 }
 
 }  // namespace
@@ -322,12 +342,12 @@ int axq_symm_create(void* comm, size_t bytes, void** symm_out, void** local_out)
         set_last_error(std::string(fn) + ": " + what + ": " + cudaGetErrorString(e));
         return AXQ_ERR_CUDA;
     };
-    cudaError_t e = cudaMalloc(&y->local, y->data_bytes + kSymmCtrlBytes);
+    cudaError_t e = cudaMalloc(&y->local, 3 * y->data_bytes + kSymmCtrlBytes);
     if (e != cudaSuccess) {
         delete y;
         return cuda_err(e, "cudaMalloc");
     }
-    cudaMemset(y->local + y->data_bytes, 0, kSymmCtrlBytes);
+    cudaMemset(y->local + 3 * y->data_bytes, 0, kSymmCtrlBytes);
     cudaIpcMemHandle_t h;
     e = cudaIpcGetMemHandle(&h, y->local);
     // exchange the handles: an all-gather of G x 64 bytes on the communicator
@@ -363,19 +383,16 @@ int axq_symm_create(void* comm, size_t bytes, void** symm_out, void** local_out)
         e = cudaIpcOpenMemHandle(&p, hs[g], cudaIpcMemLazyEnablePeerAccess);
         y->peer[g] = static_cast<uint8_t*>(p);
     }
-    std::vector<float*> outs(G);
-    std::vector<unsigned*> cmp(G), ent(G);
+    std::vector<float*> lands(G);
+    std::vector<unsigned*> cmp(G);
     for (int g = 0; g < G; ++g) {
-        outs[g] = reinterpret_cast<float*>(y->peer[g]);
+        lands[g] = y->peer[g] ? reinterpret_cast<float*>(Symm::land(y->peer[g], y->data_bytes)) : nullptr;
         cmp[g] = y->peer[g] ? Symm::ctrl(y->peer[g], y->data_bytes, 0) : nullptr;
-        ent[g] = y->peer[g] ? Symm::ctrl(y->peer[g], y->data_bytes, 1) : nullptr;
     }
-    if (e == cudaSuccess) e = cudaMalloc(&y->d_out, G * sizeof(float*));
+    if (e == cudaSuccess) e = cudaMalloc(&y->d_land, G * sizeof(float*));
     if (e == cudaSuccess) e = cudaMalloc(&y->d_comp, G * sizeof(unsigned*));
-    if (e == cudaSuccess) e = cudaMalloc(&y->d_entry, G * sizeof(unsigned*));
-    if (e == cudaSuccess) e = cudaMemcpy(y->d_out, outs.data(), G * sizeof(float*), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(y->d_land, lands.data(), G * sizeof(float*), cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemcpy(y->d_comp, cmp.data(), G * sizeof(unsigned*), cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = cudaMemcpy(y->d_entry, ent.data(), G * sizeof(unsigned*), cudaMemcpyHostToDevice);
     if (e != cudaSuccess) {
         axq_symm_destroy(y);
         return cuda_err(e, "peer mapping");
@@ -391,9 +408,8 @@ int axq_symm_destroy(void* symm) {
     cudaDeviceSynchronize();
     for (size_t g = 0; g < y->peer.size(); ++g)
         if (static_cast<int>(g) != y->c->rank && y->peer[g]) cudaIpcCloseMemHandle(y->peer[g]);
-    if (y->d_out) cudaFree(y->d_out);
+    if (y->d_land) cudaFree(y->d_land);
     if (y->d_comp) cudaFree(y->d_comp);
-    if (y->d_entry) cudaFree(y->d_entry);
     if (y->local) cudaFree(y->local);
     delete y;
     return AXQ_OK;
@@ -408,8 +424,13 @@ int axq_symm_wait(void* symm, axq_stream_t stream) {
     if (int e = check_comm(y->c, "axq_symm_wait")) return e;
     if (!y->pending) return AXQ_OK;  // the last call already completed in stream order
     y->pending = false;
-    cudaError_t e = launch_pdl(peer_wait_kernel, dim3(1), dim3(32), 0, reinterpret_cast<cudaStream_t>(stream),
-                               static_cast<const unsigned*>(y->comp()), y->epoch(), y->c->nranks, y->pending_err);
+    const int64_t n = static_cast<int64_t>(y->pending_floats);
+    const int blocks = static_cast<int>(std::min<int64_t>(64, std::max<int64_t>(1, (n / 4 + 255) / 256)));
+    cudaError_t e = launch_pdl(peer_wait_kernel, dim3(blocks), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream),
+                               static_cast<const unsigned*>(y->comp()), y->epoch(), y->wait_blocks(),
+                               reinterpret_cast<const float*>(Symm::land(y->local, y->data_bytes)),
+                               static_cast<int64_t>(y->data_bytes / 4), reinterpret_cast<float*>(y->local), n,
+                               y->c->nranks, y->pending_err);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) {
         set_last_error(std::string("axq_symm_wait: ") + cudaGetErrorString(e));
@@ -480,13 +501,14 @@ int axq_matmul_sharded_p2p_async(void* symm, int fmt, const void* a_q_local, con
         return AXQ_ERR_COMM;
     }
     int* err = static_cast<int*>(workspace);
-    GemvPeers peers{y->d_out, y->d_comp, y->done(), y->d_entry, y->entry(), y->epoch(),
-                    c->rank * rows,  c->nranks, c->rank};
+    GemvPeers peers{y->d_land, y->d_comp, y->done(), y->epoch(), static_cast<int64_t>(y->data_bytes / 4),
+                    c->rank * rows, c->nranks, c->rank};
     cudaError_t e = gemv_dispatch(fmt, a_q_local, nullptr, b, mine, rows, K, N, static_cast<int>(flags),
                                   static_cast<uint8_t*>(workspace) + 256, workspace_bytes - 256, err, s, &peers);
     if (e == cudaSuccess) {
         y->pending = true;
         y->pending_err = err;
+        y->pending_floats = static_cast<size_t>(M) * static_cast<size_t>(N);
     }
     if (e != cudaSuccess) {
         set_last_error(std::string(fn) + ": " + cudaGetErrorString(e));

@@ -655,22 +655,19 @@ struct GemvArgs {
     const uint8_t* w2;
     int pair;
     // peer-store epilogue (npeers > 0, row-major out only): each output value
-    // is stored at row row_offset + row of every rank's copy of the output
-    // (peer_out[g], mapped over NVLink; a.out is unused), and the grid's last
-    // CTA then adds 1 to every rank's completion counter peer_comp[g]
-    float* const* peer_out;
+    // is stored at row row_offset + row of copy (*epoch + 1) & 1 of every
+    // rank's landing area (peer_land[g], mapped over NVLink; a.out is
+    // unused), and the grid's last CTA then adds 1 to every rank's
+    // completion counter peer_comp[g].  Two copies alternate by call, so no
+    // rank waits for the others before storing: a rank starts call e + 2's
+    // stores only after its wait for call e + 1, which needs every rank's
+    // call e + 1, which each rank issues after its own wait for call e (the
+    // read of copy e & 1).
+    float* const* peer_land;
     unsigned* const* peer_comp;
     unsigned* done;  // finished-CTA count of this grid (reset by the last CTA)
-    // entry handshake: the last CTA adds 1 to every rank's entry counter
-    // peer_entry[g] once the call's inputs are ready; before its first peer store each CTA
-    // waits until every rank has entered this call (*my_entry >= (*epoch + 1)
-    // * npeers), so no rank overwrites a copy its owner may still be reading.
-    // Counters are sums over ranks: a rank enters call e + 1 only after its
-    // wait for call e, which needs every rank to have entered call e, so the
-    // sum reaches (e + 1) * npeers only once every rank has entered call e + 1.
-    unsigned* const* peer_entry;
-    const unsigned* my_entry;
     const unsigned* epoch;
+    int64_t land_stride;
     int64_t row_offset;
     int npeers, rank;
 };
@@ -693,8 +690,7 @@ __device__ __forceinline__ uintptr_t slot_base(const GemvArgs& a, int slot) {
 // warps and store the outputs (or, for peer-store calls, every rank's copy).
 template <int F, int NT, int AL, int H>
 __device__ __forceinline__ void consume(const GemvArgs& a, uint8_t* stages, float* red, uint64_t* full,
-                                        uint64_t* empty, volatile int* abort_flag, unsigned* entry_flag, int warp,
-                                        int lane) {
+                                        uint64_t* empty, volatile int* abort_flag, int warp, int lane) {
     using L = Lane<F>;
     static_assert((kStageCG * L::CGB) % 16 == 0, "a K-step must keep row segments' 16-byte phase");
     const int cgl = 4 * (warp & 3) + (lane >> 3);  // CG slot in the stage
@@ -704,7 +700,8 @@ __device__ __forceinline__ void consume(const GemvArgs& a, uint8_t* stages, floa
     for (int t = 0; t < NT; ++t) acc[0][t] = acc[1][t] = 0.0f;
     int s = 0, unit_par = 0;
     uint32_t phase = 0;
-    bool entered = (a.npeers == 0);  // every rank has entered this call
+    // peer-store calls: this call's copy of every rank's landing area
+    const int64_t land_off = a.npeers > 0 ? static_cast<int64_t>((*a.epoch + 1u) & 1u) * a.land_stride : 0;
     bool aborted = false;
     const uintptr_t base0 = slot_base(a, pr), base1 = slot_base(a, pr + 8);
     for (int64_t u = blockIdx.x; u < a.units; u += gridDim.x, unit_par ^= 1) {
@@ -762,22 +759,6 @@ __device__ __forceinline__ void consume(const GemvArgs& a, uint8_t* stages, floa
             }
         }
         asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
-        if (!entered && warp == 0) {
-            if (lane == 0 && ld_acquire_cta_shared_u32(entry_flag) == 0) {
-                // the producer's entry wait (normally long done); this bound
-                // outlasts the producer's own
-                const uint64_t t0 = globaltimer_ns();
-                while (ld_acquire_cta_shared_u32(entry_flag) == 0) {
-                    if (globaltimer_ns() - t0 > 2 * kPeerWaitNs) {
-                        atomicExch(a.err, 1);
-                        break;
-                    }
-                    __nanosleep(100);
-                }
-            }
-            __syncwarp();
-            entered = true;
-        }
         const int64_t orow = a.pair ? u * 8 + lane : u * kUnitRows + lane;
         if (warp == 0 && lane < (a.pair ? 8 : 16) && orow < a.rows) {
 #pragma unroll
@@ -793,8 +774,8 @@ __device__ __forceinline__ void consume(const GemvArgs& a, uint8_t* stages, floa
                         v = v / (1.0f + expf(-v)) * up;
                     }
                     if (a.npeers > 0) {
-                        const int64_t gi = (a.row_offset + orow) * a.out_ld + t;
-                        for (int g = 0; g < a.npeers; ++g) a.peer_out[g][gi] = v;
+                        const int64_t gi = land_off + (a.row_offset + orow) * a.out_ld + t;
+                        for (int g = 0; g < a.npeers; ++g) a.peer_land[g][gi] = v;
                     } else if (a.out_tokmajor) {
                         a.out[t * a.out_ld + orow] = v;
                     } else {
@@ -813,9 +794,6 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + kMaxStages;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kMaxStages);
-    // peer-store calls: 1 once every rank has entered this call, 2 if the
-    // producer's wait for that gave up (set by the producer warp)
-    unsigned* entry_flag = reinterpret_cast<unsigned*>(empty + kMaxStages) + 1;
     float* red = reinterpret_cast<float*>(smem + kHeaderBytes);  // [2][warps][16][NT]
     uint8_t* stages = smem + kHeaderBytes + ((2 * kConsumerWarps * kUnitRows * NT * 4 + 127) / 128) * 128;
 
@@ -829,7 +807,6 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
             mbar_init(&empty[s], kConsumerWarps);
         }
         *abort_flag = 0;
-        *entry_flag = 0;
         fence_mbar_init();
     }
     __syncthreads();
@@ -840,35 +817,17 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
         // ---------------- producer warp: lane r copies row r of each stage ----
         // The weights were complete before this call was enqueued (no kernel
         // of this library writes them), so streaming starts at once.
-        // Peer-store calls: every CTA's producer waits for the other ranks'
-        // entry before its first wait for a free slot (consumers never hold
-        // it up) and hands the result to the consumers in entry_flag.
-        bool polled = (a.npeers == 0);
-        auto poll_entry = [&]() {
-            if (lane == 0) {
-                const unsigned target = (*a.epoch + 1) * static_cast<unsigned>(a.npeers);
-                unsigned ok = 1;
-                if (!poll_counter_sys(a.my_entry, target, kPeerWaitNs)) {  // give up, report
-                    atomicExch(a.err, 1);
-                    ok = 2;
-                }
-                st_release_cta_shared_u32(entry_flag, ok);
-            }
-            __syncwarp();
-            polled = true;
-        };
         const uint64_t wpol = l2_evict_first_policy();  // weights are read once
         int s = 0, pass = 0;  // ring slot and how many times the ring was filled
         for (int64_t u = blockIdx.x; u < a.units; u += gridDim.x) {
             for (int ks = 0; ks < a.nks; ++ks) {
                 if (pass > 0) {
-                    if (!polled) poll_entry();
                     if (!wait_or_abort(&empty[s], (pass - 1) & 1, abort_flag)) {
                         if (lane == 0) {
                             *abort_flag = 1;
                             atomicExch(a.err, 1);
                         }
-                        return;  // (the entry was polled before this wait)
+                        return;
                     }
                 }
                 uint8_t* st = stages + s * a.stage_bytes;
@@ -908,7 +867,6 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
                 }
             }
         }
-        if (!polled) poll_entry();
         return;
     }
 
@@ -918,14 +876,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
     // activation run it loads serves two rows.  The half is a template
     // argument: one warp-uniform branch here instead of one per K-step.
     pdl_wait();  // activation records of this call are complete
-    // Peer-store calls: every earlier kernel of the stream has completed now
-    // (the activation prep waited for its predecessor before finishing), so
-    // this rank's reads of the old output are done: the last CTA (one with
-    // the fewest units) counts this rank as entered at every rank.
-    if (a.npeers > 0 && tid == 0 && blockIdx.x == gridDim.x - 1)
-        for (int g = 0; g < a.npeers; ++g) red_add_sys_u32(a.peer_entry[g], 1u);
-    if (warp < 4) consume<F, NT, AL, 0>(a, stages, red, full, empty, abort_flag, entry_flag, warp, lane);
-    else consume<F, NT, AL, 1>(a, stages, red, full, empty, abort_flag, entry_flag, warp, lane);
+    if (warp < 4) consume<F, NT, AL, 0>(a, stages, red, full, empty, abort_flag, warp, lane);
+    else consume<F, NT, AL, 1>(a, stages, red, full, empty, abort_flag, warp, lane);
     if (a.npeers > 0 && warp == 0) {
         // The warp's peer stores are ordered before the CTA counts itself
         // (a GPU-scope release, cumulative over the warp barrier); the last
@@ -1013,12 +965,11 @@ cudaError_t launch_gemv(const void* w, const void* w2, const float* x, float* ou
     a.nks = (a.ncg + kStageCG - 1) / kStageCG;
     if (peers) {
         if (N > kGemvMaxN || (flags & AXQ_FLAG_OUT_TOKMAJOR)) return cudaErrorInvalidValue;
-        a.peer_out = peers->out;
+        a.peer_land = peers->land;
         a.peer_comp = peers->comp;
         a.done = peers->done;
-        a.peer_entry = peers->entry;
-        a.my_entry = peers->my_entry;
         a.epoch = peers->epoch;
+        a.land_stride = peers->land_stride;
         a.row_offset = peers->row_offset;
         a.npeers = peers->n;
         a.rank = peers->rank;

@@ -38,17 +38,17 @@ size_t gemv_workspace_bytes(int64_t Kp, int64_t ntok);
 // output copies, of their completion and entry counters, this rank's
 // finished-CTA counter, entry counters and call epoch, and the global row of
 // local row 0.
-// Peer-store GEMV epilogue of a row-sharded matmul: out[g] is rank g's
-// copy of the full output (this rank's rows start at row_offset), comp[g]
-// and entry[g] its completion and entry counters; my_entry, epoch and done
-// are this rank's entry counter, call count and finished-CTA counter.
+// Peer-store GEMV epilogue of a row-sharded matmul: land[g] is rank g's
+// landing area, two copies of the full output `land_stride` floats apart;
+// call e (1-based: *epoch + 1, epoch = calls this rank has waited for)
+// stores into copy e & 1 at row row_offset + row of every rank; comp[g] is
+// rank g's completion counter and done this rank's finished-CTA counter.
 struct GemvPeers {
-    float* const* out;
+    float* const* land;
     unsigned* const* comp;
     unsigned* done;
-    unsigned* const* entry;
-    const unsigned* my_entry;
     const unsigned* epoch;
+    int64_t land_stride;
     int64_t row_offset;
     int n, rank;
 };

@@ -189,8 +189,8 @@ int axq_comm_inject_failure(void* comm, int64_t collective_index);
  * buf + r*count_per_rank; on completion every rank holds all of them. */
 int axq_allgather(void* comm, float* buf, size_t count_per_rank, axq_stream_t stream);
 
-/* Symmetric buffer: every rank allocates `bytes` of device memory (plus a
- * small signal area) and maps every other rank's allocation over NVLink
+/* Symmetric buffer: every rank allocates `bytes` of device memory (plus two
+ * landing copies of it and a small signal area) and maps every other rank's allocation over NVLink
  * (CUDA IPC).  Collective over the communicator's ranks (one process per
  * GPU).  *local_out is this rank's copy; destroy is collective too and must
  * follow the last use on every rank. */
@@ -199,9 +199,13 @@ int axq_symm_destroy(void* symm);
 
 /* As axq_matmul_sharded, with the output in a symmetric buffer (full
  * [M x N] row-major copy on every rank): for up to 4 columns the GEMV's
- * epilogue stores every output value into each rank's copy over NVLink and
- * its last CTA signals the ranks; a one-thread kernel then waits (bounded)
- * until every rank has signalled — no separate collective.  More columns run
+ * epilogue stores every output value into each rank's landing area over
+ * NVLink and its last CTA signals the ranks; a small kernel then waits
+ * (bounded) until every rank has signalled and copies the landing area into
+ * this rank's copy — no separate collective.  The landing area has two
+ * copies that alternate by call, so no rank waits for another before its
+ * stores; reads of a call's output must be ordered on the call's stream
+ * before the call after the next one on the same buffer.  More columns run
  * the tensor-core path and the in-place NCCL all-gather.  A wait that gives
  * up sets the workspace status (axq_workspace_status). */
 int axq_matmul_sharded_p2p(void* symm, int fmt, const void* a_q_local, const float* b, int64_t M, int64_t K,

@@ -112,10 +112,10 @@ def test_one_rank_peer_store_async_and_wait(orc, comm1):
 def test_one_rank_peer_waits_run_out_and_context_survives(orc, comm1):
     """Failure detection without a GPU fault: the buffer's call count is
     advanced by hand (a count no rank will ever reach), so the next call's
-    entry wait (every CTA's producer) and completion wait (peer_wait_kernel)
-    both give up on their own one-second bounds and report through the call's
-    workspace status word.  The context stays usable: a plain matmul and a
-    fresh symmetric buffer still give the oracle's result."""
+    completion wait (peer_wait_kernel) gives up on its own one-second bound
+    and reports through the call's workspace status word.  The context stays
+    usable: a plain matmul and a fresh symmetric buffer still give the
+    oracle's result."""
     import time
     import torch
     import axon_b200 as ax
@@ -131,10 +131,11 @@ def test_one_rank_peer_waits_run_out_and_context_survives(orc, comm1):
     buf = ax.SymmetricBuffer(comm1, 4 * M * N)
     try:
         assert rel_err(ax.matmul_sharded_p2p(buf, a, bd, M, workspace=ws).cpu().numpy(), y_ref) <= TOL
-        # control block after the data (rounded up to 256 bytes), one 128-byte
-        # line each: completion count, entry count, finished CTAs, call count
+        # control block after the output and its two landing copies (each
+        # rounded up to 256 bytes), one 128-byte line each: completion count,
+        # finished CTAs, call count, finished wait blocks
         data_bytes = -(-buf.nbytes // 256) * 256
-        calls = torch.as_tensor(_CudaArray(buf.ptr + data_bytes + 3 * 128, (1,), "<i4"), device="cuda")
+        calls = torch.as_tensor(_CudaArray(buf.ptr + 3 * data_bytes + 2 * 128, (1,), "<i4"), device="cuda")
         calls += 1
         torch.cuda.synchronize()
         t0 = time.time()
