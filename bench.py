@@ -809,7 +809,10 @@ def run_case(args):
     import torch
     import axon_b200 as ax
 
-    fmt, rows, K, M = args.case.split(":")
+    parts = args.case.split(":")
+    if parts[0] == "PACK":
+        return run_case_pack(args, parts[1], int(parts[2]), int(parts[3]))
+    fmt, rows, K, M = parts
     rows, K, M = int(rows), int(K), int(M)
     dev = torch.device("cuda", 0)
     if fmt == "F32":
@@ -837,6 +840,39 @@ def run_case(args):
     ms = e0.elapsed_time(e1) / max(1, args.steps)
     print(json.dumps({"case": args.case, "ms": round(ms, 5), "TOPS": round(2.0 * rows * K * M / (ms / 1e3) / 1e12, 2),
                       "weight_GBps": round(nbytes / (ms / 1e3) / 1e9, 1)}), flush=True)
+    return 0
+
+
+def run_case_pack(args, fmt, rows, cols):
+    """Pack timing (--case PACK:FMT:ROWS:COLS): an fp32 [ROWS x COLS] tensor,
+    N(0,1) with 1% U(-50, 50), packed --warmup untimed then --steps timed
+    times; prints fp32 GB/s read and the HBM fraction of read + written
+    bytes.  Small enough to run under a profiler."""
+    import torch
+    import axon_b200 as ax
+    dev = torch.device("cuda", 0)
+    F = ax.QuantFormat[fmt]
+    g = torch.Generator(device=dev).manual_seed(11)
+    src = torch.randn(rows, cols, device=dev, generator=g)
+    m = torch.rand(rows, cols, device=dev, generator=g) < 0.01
+    src[m] = torch.rand(int(m.sum().item()), device=dev, generator=g) * 100 - 50
+    del m
+    dst = torch.empty(ax.quantized_size_2d(rows, cols, F), dtype=torch.uint8, device=dev)
+    for _ in range(args.warmup):
+        ax.quantize(dst, src, F)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        ax.quantize(dst, src, F)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / max(1, args.steps)
+    peak, _ = load_peaks()
+    n = rows * cols
+    print(json.dumps({"case": args.case, "ms": round(ms, 5), "read_GBps": round(4.0 * n / (ms / 1e3) / 1e9, 1),
+                      "hbm_frac": round((4.0 * n + dst.numel()) / (ms / 1e3) / 1e9 / peak, 4),
+                      "bytes_per_launch": int(4 * n + dst.numel())}), flush=True)
     return 0
 
 
@@ -947,7 +983,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the GEMM and pack records")
     ap.add_argument("--suite", action="store_true", help="time every configuration (one JSON line each)")
-    ap.add_argument("--case", default=None, help="time one matmul, FMT:ROWS:K:TOKENS")
+    ap.add_argument("--case", default=None, help="time one matmul, FMT:ROWS:K:TOKENS (or PACK:FMT:ROWS:COLS)")
     ap.add_argument("--axon", action="store_true", help="time loading the packed weights from an .axon file")
     args = ap.parse_args()
     if args.axon:
