@@ -71,6 +71,7 @@ SIGNATURES = {
     "axq_matmul_workspace_size": (_sz, [ctypes.c_int, _i64, _i64, _i64]),
     "axq_matmul": (ctypes.c_int, [ctypes.c_int, _vp, _vp, _vp, _i64, _i64, _i64, ctypes.c_uint, _vp, _sz, _vp]),
     "axq_workspace_status": (ctypes.c_int, [_vp, _vp]),
+    "axq_linear": (ctypes.c_int, [ctypes.c_int, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, ctypes.c_size_t, _vp]),
     "axq_matmul_noalloc": (ctypes.c_int, [ctypes.c_int, _vp, _vp, _vp, _i64, _i64, _i64, ctypes.c_uint, _vp]),
     "axq_noalloc_status": (ctypes.c_int, [_vp]),
     "axq_gate_up_workspace_size": (_sz, [ctypes.c_int, _i64, _i64, _i64]),

@@ -1,6 +1,7 @@
 // C-ABI layer (include/axq.h): argument validation, status/message
 // handling in the reference's Expected<void>/Error style, and dispatch to the
 // kernels.  Nothing here allocates device memory.
+#include <algorithm>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -9,6 +10,7 @@
 
 #include "axq_common.cuh"
 #include "axq_internal.h"
+#include "axq_ptx.cuh"
 
 namespace axq {
 
@@ -38,6 +40,16 @@ const char* fmt_name(int f) {
 }
 
 bool known_fmt(int f) { return host_block_elems(f) != 0; }
+
+// y[t][m] += bias[m] for the token-major [N x M] output of a quantized
+// Linear; launched after the matmul in stream order (it waits for it).
+__global__ void bias_add_kernel(float* __restrict__ y, const float* __restrict__ bias, int64_t M, int64_t n) {
+    pdl_wait();  // the matmul's output is complete
+    pdl_launch_dependents();
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        y[i] += bias[i % M];
+}
 
 // A kernel handed a pageable host pointer or another device's memory would
 // fault; reject those here instead.
@@ -186,6 +198,31 @@ int axq_matmul(int fmt, const void* a_q, const float* b, float* out, int64_t M, 
                                         workspace_bytes - kStatusBytes, err, s);
     if (e != cudaSuccess) return cuda_fail(e, fn);
     return AXQ_OK;
+}
+
+int axq_linear(int fmt, const void* w_q, const float* x, const float* bias, float* y, int64_t out_features,
+               int64_t in_features, int64_t tokens, void* workspace, size_t workspace_bytes, axq_stream_t stream) {
+    const char* fn = "axq_linear";
+    if (bias) {
+        if (int r = check_ptr(bias, "bias", fn)) return r;
+        if (reinterpret_cast<uintptr_t>(bias) % 4) return fail(AXQ_ERR_INVALID, std::string(fn) + ": bias must be 4-byte aligned");
+    }
+    // y[tokens x out] = x[tokens x in] . W^T: W is the left operand in the
+    // reference's orientation, x and y token-major
+    int st = axq_matmul(fmt, w_q, x, y, out_features, in_features, tokens, AXQ_FLAG_B_TOKMAJOR | AXQ_FLAG_OUT_TOKMAJOR,
+                        workspace, workspace_bytes, stream);
+    if (st != AXQ_OK) {
+        std::string m = g_last_error;
+        if (m.rfind("axq_matmul", 0) == 0) m.replace(0, 10, fn);
+        return fail(st, m);
+    }
+    if (!bias || out_features == 0 || tokens == 0) return AXQ_OK;
+    const int64_t n = out_features * tokens;
+    const int blocks = static_cast<int>(std::min<int64_t>((n + 255) / 256, 4 * 148));
+    cudaError_t e = launch_pdl(bias_add_kernel, dim3(blocks), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), y,
+                               bias, out_features, n);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    return e == cudaSuccess ? AXQ_OK : cuda_fail(e, fn);
 }
 
 size_t axq_gate_up_workspace_size(int fmt, int64_t M, int64_t K, int64_t N) {

@@ -542,6 +542,47 @@ AXON_FIXED_MATMUL(matmul_q6_K, Q6_K)
 void set_stream(axq_stream_t stream) { t_stream = stream; }
 axq_stream_t current_stream() { return t_stream; }
 
+Expected<Linear> Linear::create(DeviceTensor weight, DeviceTensor bias) {
+    const char* fn = "Linear";
+    if (!weight.is_quantized()) return Error{std::string(fn) + ": the weight must be packed (quantized)"};
+    const bool has_bias = bias.data() != nullptr;
+    if (has_bias) {
+        if (bias.is_quantized() || bias.dtype() != DType::Float32 || bias.rows() * bias.cols() != weight.rows())
+            return Error{std::string(fn) + ": bias must be fp32 with out_features elements"};
+        if (bias.device_index() != weight.device_index())
+            return Error{std::string(fn) + ": weight and bias live on different devices"};
+    }
+    Linear l;
+    l.weight_ = std::move(weight);
+    l.bias_ = std::move(bias);
+    l.has_bias_ = has_bias;
+    return l;
+}
+
+Expected<DeviceTensor> Linear::forward(const DeviceTensor& x) const {
+    const char* fn = "Linear::forward";
+    if (x.is_quantized() || x.dtype() != DType::Float32) return Error{std::string(fn) + ": x must be fp32"};
+    if (x.cols() != in_features())
+        return Error{std::string(fn) + ": x has " + std::to_string(x.cols()) + " features, the layer " +
+                     std::to_string(in_features())};
+    if (auto e = check_same_device(weight_, x, fn); !e) return e.error();
+    int cur = 0;
+    cudaGetDevice(&cur);
+    if (cur != x.device_index()) return Error{std::string(fn) + ": x is not on the current device"};
+    auto y = DeviceTensor::empty(x.rows(), out_features());
+    if (!y) return y.error();
+    const int fmt = static_cast<int>(weight_.quant().format);
+    const size_t need = axq_matmul_workspace_size(fmt, out_features(), in_features(), x.rows());
+    auto ws = scratch(x.device_index(), need);
+    if (!ws) return ws.error();
+    const int st = axq_linear(fmt, weight_.data(), static_cast<const float*>(x.data()),
+                              has_bias_ ? static_cast<const float*>(bias_.data()) : nullptr,
+                              static_cast<float*>(y.value().data()), out_features(), in_features(), x.rows(),
+                              ws.value(), need, t_stream);
+    if (st != AXQ_OK) return last_error(fn);
+    return y;
+}
+
 Expected<void> synchronize() {
     if (cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(t_stream)) != cudaSuccess) {
         const char* m = cudaGetErrorString(cudaGetLastError());

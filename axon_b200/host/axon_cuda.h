@@ -226,6 +226,29 @@ Expected<void> matmul_q4_K(DeviceTensor& out, const DeviceTensor& a, const Devic
 Expected<void> matmul_q5_K(DeviceTensor& out, const DeviceTensor& a, const DeviceTensor& b);
 Expected<void> matmul_q6_K(DeviceTensor& out, const DeviceTensor& a, const DeviceTensor& b);
 
+// ---- quantized Linear (nn/linear.h, src/nn/linear.cpp:7-27) ---------------
+// The reference's Linear holds an fp32 weight [in, out] and a bias [out] and
+// computes y = rt.matmul(x, W) (+ bias through AddOp).  A packed weight sits
+// on the left of the quantized matmul, so this Linear holds W packed as
+// [out_features x in_features] (rows of whole blocks) and computes
+// y[tokens x out] = x[tokens x in] . W^T + bias through axq_linear.
+class Linear {
+public:
+    // weight: packed [out x in]; bias: fp32 [1 x out] or an undefined tensor
+    // (no bias).  Takes ownership of both.
+    static Expected<Linear> create(DeviceTensor weight, DeviceTensor bias = DeviceTensor());
+    Expected<DeviceTensor> forward(const DeviceTensor& x) const;  // x: fp32 [tokens x in]
+    const DeviceTensor& weight() const { return weight_; }
+    const DeviceTensor& bias() const { return bias_; }
+    bool has_bias() const { return has_bias_; }
+    int64_t in_features() const { return weight_.cols(); }
+    int64_t out_features() const { return weight_.rows(); }
+
+private:
+    DeviceTensor weight_, bias_;
+    bool has_bias_ = false;
+};
+
 // Stream every call of this thread is enqueued on (default: the legacy
 // default stream); calls are asynchronous, synchronize() waits for them and
 // reports any kernel that gave up a bounded wait.

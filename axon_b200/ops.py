@@ -239,16 +239,38 @@ def matmul(out: torch.Tensor, a, b: torch.Tensor, stream: Optional[torch.cuda.St
     return out
 
 
-def linear_q(x: torch.Tensor, w: QTensor, out: Optional[torch.Tensor] = None, **kw) -> torch.Tensor:
-    """Quantized Linear: y[N, M] = x[N, K] . W[M, K]^T with W packed row-wise.
+def linear_q(x: torch.Tensor, w: QTensor, out: Optional[torch.Tensor] = None, bias: Optional[torch.Tensor] = None,
+             workspace: Optional[Workspace] = None, stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """Quantized Linear: y[N, M] = x[N, K] . W[M, K]^T (+ bias[M]) with W
+    packed row-wise (C ABI axq_linear).
 
-    The reference has no quantized Linear (its Linear puts an fp32 weight on
-    the right, src/nn/linear.cpp:19); this is the glue that puts the packed
-    weight on the left: y = (W_q . x^T)^T."""
+    The reference's Linear (src/nn/linear.cpp:19-27) keeps an fp32 weight
+    [in, out] on the right of rt.matmul and adds the bias with AddOp; a
+    packed weight sits on the left, so this is y = (W_q . x^T)^T + bias."""
     M, K = w.shape
+    _req_cuda(x, "x", torch.float32)
+    _req_cuda(w.data, "w", torch.uint8)
+    if x.dim() != 2 or x.shape[1] != K:
+        raise AxqError(Status.ERR_INVALID, f"linear_q: x must be [N x {K}]")
+    N = x.shape[0]
     if out is None:
-        out = torch.empty((x.shape[0], M), dtype=torch.float32, device=x.device)
-    return matmul_q(out, w, x, b_tokmajor=True, out_tokmajor=True, **kw)
+        out = torch.empty((N, M), dtype=torch.float32, device=x.device)
+    _req_cuda(out, "out", torch.float32)
+    if tuple(out.shape) != (N, M):
+        raise AxqError(Status.ERR_INVALID, f"linear_q: out must be [{N} x {M}]")
+    if w.data.numel() < _packed_bytes(M, K, w.fmt):
+        raise AxqError(Status.ERR_INVALID, "linear_q: quantized weight is smaller than its shape")
+    bptr = None
+    if bias is not None:
+        _req_cuda(bias, "bias", torch.float32)
+        if bias.numel() != M:
+            raise AxqError(Status.ERR_INVALID, f"linear_q: bias must have {M} elements")
+        bptr = bias.data_ptr()
+    need = _ws_size(int(w.fmt), M, K, N)
+    wp, wbytes = _aligned_ptr((workspace or _default_ws).get(need + 256, out.device))
+    check(lib().axq_linear(int(w.fmt), w.data.data_ptr(), x.data_ptr(), bptr, out.data_ptr(), M, K, N, wp, wbytes,
+                           _stream_handle(stream, out.device)))
+    return out
 
 
 def gate_up_silu(x: torch.Tensor, w_gate: QTensor, w_up: QTensor, out: Optional[torch.Tensor] = None,

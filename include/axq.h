@@ -98,6 +98,17 @@ size_t axq_matmul_workspace_size(int fmt, int64_t M, int64_t K, int64_t N);
 int axq_matmul(int fmt, const void* a_q, const float* b, float* out, int64_t M, int64_t K, int64_t N,
                unsigned flags, void* workspace, size_t workspace_bytes, axq_stream_t stream);
 
+/* Quantized Linear: y[tokens x out_features] = x[tokens x in_features] . W^T
+ * (+ bias[out_features] on every row when bias is not NULL), with W packed
+ * row-wise as [out_features x in_features] (the left operand of
+ * axq_matmul).  The reference's Linear (src/nn/linear.cpp:19-27) keeps an fp32
+ * weight [in x out] and computes rt.matmul(x, W) then AddOp with the bias;
+ * a packed weight has to sit on the left, so this is that Linear for a
+ * quantized weight: y = (W_q . x^T)^T + bias.  Workspace as axq_matmul with
+ * M = out_features, N = tokens. */
+int axq_linear(int fmt, const void* w_q, const float* x, const float* bias, float* y, int64_t out_features,
+               int64_t in_features, int64_t tokens, void* workspace, size_t workspace_bytes, axq_stream_t stream);
+
 /* Fused MLP front half (the reference has no SiLU and no quantized Linear;
  * this is the composition SiLU(X W_gate^T) * (X W_up^T) of its matmul):
  *   h = silu(W_gate . B) * (W_up . B)  elementwise, silu(v) = v / (1 + e^-v),

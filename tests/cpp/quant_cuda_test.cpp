@@ -179,10 +179,67 @@ void run_axon(const std::string& dir) {
 
 }  // namespace
 
+// Quantized Linear (the reference's nn::Linear with a packed weight on the
+// left): y = x . W^T + bias against the oracle's W . x^T plus the bias,
+// for a GEMV-sized and a GEMM-sized batch; without bias too; refusals.
+void run_linear() {
+    const QuantFormat f = QuantFormat::Q4_K;
+    const int64_t M = 96, K = 1024;
+    Rng rng(99);
+    std::vector<float> w(static_cast<size_t>(M * K)), bias(static_cast<size_t>(M));
+    for (auto& v : w) v = rng.normal();
+    for (auto& v : bias) v = rng.normal();
+    std::vector<uint8_t> packed(quantized_size_2d(M, K, f));
+    CHECK(orc_quantize(static_cast<int>(f), w.data(), M, K, packed.data()) == 0);
+    // the weight packed on the device (byte-equal to the oracle's packing,
+    // which run_format checks), so the oracle's bytes describe it
+    auto wsrc = DeviceTensor::from_host(w.data(), M, K);
+    auto wq = DeviceTensor::empty(M, K, f);
+    CHECK(static_cast<bool>(wq) && static_cast<bool>(wsrc));
+    CHECK(static_cast<bool>(quantize(wq.value(), wsrc.value(), f)));
+    auto bd = DeviceTensor::from_host(bias.data(), 1, M);
+    auto lin = Linear::create(std::move(wq.value()), std::move(bd.value()));
+    CHECK_MSG(static_cast<bool>(lin), lin ? "" : lin.error().message);
+    if (!lin) return;
+    CHECK(lin.value().in_features() == K && lin.value().out_features() == M && lin.value().has_bias());
+    for (int64_t N : {int64_t(2), int64_t(33)}) {
+        std::vector<float> x(static_cast<size_t>(N * K)), xt(static_cast<size_t>(K * N)), ref(static_cast<size_t>(M * N));
+        for (auto& v : x) v = rng.normal();
+        for (int64_t t = 0; t < N; ++t)
+            for (int64_t k = 0; k < K; ++k) xt[k * N + t] = x[t * K + k];
+        CHECK(orc_matmul(static_cast<int>(f), packed.data(), xt.data(), ref.data(), M, K, N) == 0);
+        std::vector<float> want(static_cast<size_t>(N * M));
+        for (int64_t t = 0; t < N; ++t)
+            for (int64_t m = 0; m < M; ++m) want[t * M + m] = ref[m * N + t] + bias[m];
+        auto xd = DeviceTensor::from_host(x.data(), N, K);
+        auto y = lin.value().forward(xd.value());
+        CHECK_MSG(static_cast<bool>(y), y ? "" : y.error().message);
+        if (!y) continue;
+        CHECK(y.value().rows() == N && y.value().cols() == M);
+        std::vector<float> got(static_cast<size_t>(N * M));
+        CHECK(static_cast<bool>(y.value().to_host(got.data(), got.size() * 4)));
+        CHECK_MSG(rel_err(got, want) <= 1e-3, "Linear N=" + std::to_string(N) + " err " + std::to_string(rel_err(got, want)));
+    }
+    // no bias
+    auto wq2 = DeviceTensor::empty(M, K, f);
+    auto nob = Linear::create(std::move(wq2.value()));
+    CHECK(static_cast<bool>(nob) && !nob.value().has_bias());
+    // refusals: fp32 weight, wrong bias length, wrong input width
+    auto w32 = DeviceTensor::empty(M, K);
+    CHECK(!Linear::create(std::move(w32.value())));
+    auto wq3 = DeviceTensor::empty(M, K, f);
+    auto b3 = DeviceTensor::zeros(1, M - 1);
+    CHECK(!Linear::create(std::move(wq3.value()), std::move(b3.value())));
+    auto xbad = DeviceTensor::zeros(2, K + 1);
+    auto ybad = lin.value().forward(xbad.value());
+    CHECK(!ybad && ybad.error().message.find("features") != std::string::npos);
+}
+
 int main(int argc, char** argv) {
     register_cuda_kernels();
     if (argc > 1) run_axon(argv[1]);
     run_factories_and_f32();
+    run_linear();
     run_format(QuantFormat::Q8_0, "Q8_0");
     run_format(QuantFormat::Q4_0, "Q4_0");
     run_format(QuantFormat::Q2_K, "Q2_K");

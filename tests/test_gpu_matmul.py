@@ -160,3 +160,42 @@ def test_gemm_token_major_and_workload_distribution(cuda, orc, fmt):
     for bt in (False, True):
         for ot in (False, True):
             assert rel_err(gpu_matmul(fmt, q, B, M, K, bt, ot), y_ref) <= TOL, (bt, ot)
+
+
+@pytest.mark.parametrize("fmt", ["Q4_K", "Q6_K", "Q8_0", "Q2_K"])
+@pytest.mark.parametrize("N", [1, 3, 24])
+def test_linear_with_bias_matches_oracle(cuda, orc, fmt, N):
+    """Quantized Linear through the C ABI (axq_linear): y[N x M] = x W^T + bias
+    against the oracle's W . x^T transposed plus the bias, and without bias."""
+    import torch
+    import axon_b200 as ax
+    rng = np.random.default_rng(N * 13 + len(fmt))
+    M, K = 200, 2048
+    q = orc.quantize(fmt, gen(rng, (M, K), "randn"))
+    x = rng.standard_normal((N, K)).astype(np.float32)
+    bias = rng.standard_normal(M).astype(np.float32)
+    w = ax.QTensor(torch.from_numpy(q).cuda(), (M, K), ax.QuantFormat[fmt])
+    y_mm = orc.matmul(fmt, q, np.ascontiguousarray(x.T), M, K).T
+    y = ax.linear_q(torch.from_numpy(x).cuda(), w, bias=torch.from_numpy(bias).cuda()).cpu().numpy()
+    assert rel_err(y, y_mm + bias) <= TOL
+    y0 = ax.linear_q(torch.from_numpy(x).cuda(), w).cpu().numpy()
+    assert rel_err(y0, y_mm) <= TOL
+
+
+def test_linear_errors(cuda):
+    import torch
+    import axon_b200 as ax
+    w = ax.QTensor.empty(16, 256, ax.QuantFormat.Q4_K)
+    x = torch.zeros(2, 256, device="cuda")
+    with pytest.raises(ax.AxqError, match="bias must have 16"):
+        ax.linear_q(x, w, bias=torch.zeros(15, device="cuda"))
+    with pytest.raises(ax.AxqError, match=r"x must be \[N x 256\]"):
+        ax.linear_q(torch.zeros(2, 255, device="cuda"), w)
+    host = np.zeros(16, dtype=np.float32)
+    L = ax.lib()
+    y = torch.empty(2, 16, device="cuda")
+    ws = torch.empty(1 << 20, dtype=torch.uint8, device="cuda")
+    st = L.axq_linear(int(ax.QuantFormat.Q4_K), w.data.data_ptr(), x.data_ptr(), host.ctypes.data, y.data_ptr(),
+                      16, 256, 2, ws.data_ptr(), ws.numel(), None)
+    assert st == ax.Status.ERR_INVALID and b"bias" in L.axq_last_error()
+    torch.cuda.synchronize()
