@@ -49,6 +49,13 @@ template <int F> struct CG {
     static constexpr int BYTES = BLK * BB;
 };
 
+// Whether a dequant thread writes a whole K-step (both halves, one warp
+// group per K-step parity) or one half of every K-step.  Whole K-steps share
+// the packed words of the two halves (nibbles or 2-bit fields of the same
+// bytes); Q8_0's halves are separate blocks, so it keeps the split form.
+template <int F>
+constexpr bool kFullKStep = (F != F_Q8_0);
+
 struct GemmArgs {
     const uint8_t* w;
     int64_t rows, rb, K;
@@ -442,7 +449,7 @@ __global__ void __launch_bounds__(kThreadsGemm, 2) gemm_kernel(GemmArgs a) {
             mbar_init(&bars->pk_empty[i], kDqWarps);
         }
         for (int i = 0; i < kMaxAB; ++i) {
-            mbar_init(&bars->a_full[i], kDqWarps);
+            mbar_init(&bars->a_full[i], kFullKStep<F> ? kDqWarps / 2 : kDqWarps);
             mbar_init(&bars->b_full[i], 1);
             mbar_init(&bars->ab_empty[i], 1);
         }
@@ -550,63 +557,134 @@ __global__ void __launch_bounds__(kThreadsGemm, 2) gemm_kernel(GemmArgs a) {
         __syncwarp();
     } else if (warp >= 2 && warp < 2 + kDqWarps) {
         // ------------------------------------------- dequant + epilogue
-        const int q = warp & 3;          // TMEM lane quarter this warp may access
-        const int h = (warp - 2) >> 2;   // which half of each K-step this thread writes
+        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        const int h = (warp - 2) >> 2;  // K-step parity (whole K-steps) or half; epilogue column chunks
         const int r = 32 * q + lane;
         const int64_t row = row0 + r;
         const bool row_ok = row < a.rows;
-        int p = 0, s = 0, pass = 0;
-        uint32_t ppar = 0;
-        for (int i = 0; i < ncg_here; ++i) {
-            if (!gwait(&bars->pk_full[p], ppar, abort_flag, a.err)) break;
-            const int cg = cg0 + i;
-            const uintptr_t ga = wbase + static_cast<uintptr_t>(row * a.rb + static_cast<int64_t>(cg) * C::BYTES);
-            const uint8_t* rowp = pk_ring + p * a.pk_bytes + r * a.rs + (ga & 15);
-            const bool tail = (static_cast<int64_t>(cg + 1) * 256 > a.K) || ((cg + 1) * C::BLK > a.nblk_row);
-            typename Dq<F>::Hdr hdr{};
-            if (row_ok) hdr = Dq<F>::template header<AL>(rowp);
-#pragma unroll 1
-            for (int k = 0; k < kKStepsPerCG; ++k) {
-                if (pass > 0 && !gwait(&bars->ab_empty[s], (pass - 1) & 1, abort_flag, a.err)) break;
-                uint4 o[4];
-                if (row_ok) {
-                    Dq<F>::template kstep<AL>(rowp, hdr, o, h, k);
-                    if (tail) {
-                        // zero the elements past K (and blocks past the row's end)
-#pragma unroll
-                        for (int c4 = 0; c4 < 4; ++c4) {
-                            const int e = 64 * k + 8 * (4 * h + c4);
-                            const int64_t kglob = static_cast<int64_t>(cg) * 256 + e;
-                            const bool blk_ok = cg * C::BLK + e / C::BE < a.nblk_row;
-                            uint32_t* ow = reinterpret_cast<uint32_t*>(&o[c4]);
-#pragma unroll
-                            for (int u = 0; u < 8; ++u)
-                                if (!blk_ok || kglob + u >= a.K) ow[u >> 1] &= (u & 1) ? 0x0000FFFFu : 0xFFFF0000u;
+        if constexpr (kFullKStep<F>) {
+            // Warps 2..5 (group 0) dequantize the even K-steps of each column
+            // group, warps 6..9 (group 1) the odd ones; a thread writes its row's
+            // whole 64-element K-step (both halves), so the K-step's packed words
+            // are loaded once and the per-K-step waits, stores and signals are
+            // paid once per 64 elements.
+            const int grp = (warp - 2) >> 2;   // K-step parity of this warp group
+            int p = 0, s = grp, pass = 0;  // A slot of this group's next K-step, times the ring wrapped
+            while (s >= a.nab) {
+                s -= a.nab;
+                ++pass;
+            }
+            uint32_t ppar = 0;
+            for (int i = 0; i < ncg_here; ++i) {
+                if (!gwait(&bars->pk_full[p], ppar, abort_flag, a.err)) break;
+                const int cg = cg0 + i;
+                const uintptr_t ga = wbase + static_cast<uintptr_t>(row * a.rb + static_cast<int64_t>(cg) * C::BYTES);
+                const uint8_t* rowp = pk_ring + p * a.pk_bytes + r * a.rs + (ga & 15);
+                const bool tail = (static_cast<int64_t>(cg + 1) * 256 > a.K) || ((cg + 1) * C::BLK > a.nblk_row);
+                typename Dq<F>::Hdr hdr{};
+                if (row_ok) hdr = Dq<F>::template header<AL>(rowp);
+    #pragma unroll 1
+                for (int k = grp; k < kKStepsPerCG; k += 2) {
+                    if (pass > 0 && !gwait(&bars->ab_empty[s], (pass - 1) & 1, abort_flag, a.err)) break;
+                    uint4 o[8];
+                    if (row_ok) {
+                        Dq<F>::template kstep<AL>(rowp, hdr, o, 0, k);
+                        Dq<F>::template kstep<AL>(rowp, hdr, o + 4, 1, k);
+                        if (tail) {
+                            // zero the elements past K (and blocks past the row's end)
+    #pragma unroll
+                            for (int c8 = 0; c8 < 8; ++c8) {
+                                const int e = 64 * k + 8 * c8;
+                                const int64_t kglob = static_cast<int64_t>(cg) * 256 + e;
+                                const bool blk_ok = cg * C::BLK + e / C::BE < a.nblk_row;
+                                uint32_t* ow = reinterpret_cast<uint32_t*>(&o[c8]);
+    #pragma unroll
+                                for (int u = 0; u < 8; ++u)
+                                    if (!blk_ok || kglob + u >= a.K) ow[u >> 1] &= (u & 1) ? 0x0000FFFFu : 0xFFFF0000u;
+                            }
                         }
+                    } else {
+    #pragma unroll
+                        for (int c8 = 0; c8 < 8; ++c8) o[c8] = make_uint4(0, 0, 0, 0);
                     }
-                } else {
-#pragma unroll
-                    for (int c4 = 0; c4 < 4; ++c4) o[c4] = make_uint4(0, 0, 0, 0);
+                    // this row's 64 elements = the 32 TMEM columns of A slot s
+                    const uint32_t ta = tmem + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(a.BN + 32 * s);
+                    tmem_st16(ta, reinterpret_cast<const uint32_t*>(o));
+                    tmem_st16(ta + 16, reinterpret_cast<const uint32_t*>(o + 4));
+                    tmem_st_wait();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&bars->a_full[s]);
+                    s += 2;  // this group's next K-step is two slots on
+                    while (s >= a.nab) {
+                        s -= a.nab;
+                        ++pass;
+                    }
                 }
-                // this row's 32 elements = 16 TMEM columns of A slot s
-                tmem_st16(tmem + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(a.BN + 32 * s + 16 * h),
-                          reinterpret_cast<const uint32_t*>(o));
-                tmem_st_wait();
-                tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&bars->a_full[s]);
-                if (++s == a.nab) {
-                    s = 0;
-                    ++pass;
+                if (lane == 0) mbar_arrive(&bars->pk_empty[p]);
+                if (++p == a.npk) {
+                    p = 0;
+                    ppar ^= 1;
                 }
+                if (*abort_flag) break;
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->pk_empty[p]);
-            if (++p == a.npk) {
-                p = 0;
-                ppar ^= 1;
+        } else {
+            // Warps 2..5 write half 0 of every K-step, warps 6..9 half 1 (the
+            // form for Q8_0, whose two halves are separate blocks).
+            int p = 0, s = 0, pass = 0;
+            uint32_t ppar = 0;
+            for (int i = 0; i < ncg_here; ++i) {
+                if (!gwait(&bars->pk_full[p], ppar, abort_flag, a.err)) break;
+                const int cg = cg0 + i;
+                const uintptr_t ga = wbase + static_cast<uintptr_t>(row * a.rb + static_cast<int64_t>(cg) * C::BYTES);
+                const uint8_t* rowp = pk_ring + p * a.pk_bytes + r * a.rs + (ga & 15);
+                const bool tail = (static_cast<int64_t>(cg + 1) * 256 > a.K) || ((cg + 1) * C::BLK > a.nblk_row);
+                typename Dq<F>::Hdr hdr{};
+                if (row_ok) hdr = Dq<F>::template header<AL>(rowp);
+    #pragma unroll 1
+                for (int k = 0; k < kKStepsPerCG; ++k) {
+                    if (pass > 0 && !gwait(&bars->ab_empty[s], (pass - 1) & 1, abort_flag, a.err)) break;
+                    uint4 o[4];
+                    if (row_ok) {
+                        Dq<F>::template kstep<AL>(rowp, hdr, o, h, k);
+                        if (tail) {
+                            // zero the elements past K (and blocks past the row's end)
+    #pragma unroll
+                            for (int c4 = 0; c4 < 4; ++c4) {
+                                const int e = 64 * k + 8 * (4 * h + c4);
+                                const int64_t kglob = static_cast<int64_t>(cg) * 256 + e;
+                                const bool blk_ok = cg * C::BLK + e / C::BE < a.nblk_row;
+                                uint32_t* ow = reinterpret_cast<uint32_t*>(&o[c4]);
+    #pragma unroll
+                                for (int u = 0; u < 8; ++u)
+                                    if (!blk_ok || kglob + u >= a.K) ow[u >> 1] &= (u & 1) ? 0x0000FFFFu : 0xFFFF0000u;
+                            }
+                        }
+                    } else {
+    #pragma unroll
+                        for (int c4 = 0; c4 < 4; ++c4) o[c4] = make_uint4(0, 0, 0, 0);
+                    }
+                    // this row's 32 elements = 16 TMEM columns of A slot s
+                    tmem_st16(tmem + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(a.BN + 32 * s + 16 * h),
+                              reinterpret_cast<const uint32_t*>(o));
+                    tmem_st_wait();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&bars->a_full[s]);
+                    if (++s == a.nab) {
+                        s = 0;
+                        ++pass;
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars->pk_empty[p]);
+                if (++p == a.npk) {
+                    p = 0;
+                    ppar ^= 1;
+                }
+                if (*abort_flag) break;
             }
-            if (*abort_flag) break;
         }
         // epilogue: TMEM lane r holds row r, column t holds token t
         if (gwait(&bars->acc_full, 0, abort_flag, a.err)) {
