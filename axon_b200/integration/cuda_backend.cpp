@@ -134,7 +134,7 @@ Expected<void> matmul_q(KernelContext& ctx) {
                   fn);
 }
 
-// fp32 out[M,N] = a[M,K] . b[K,N] (cuBLAS SGEMM in pedantic fp32 behind the C ABI).
+// fp32 out[M,N] = a[M,K] . b[K,N] (the library's fp32 kernel behind the C ABI).
 Expected<void> matmul_f32(KernelContext& ctx) {
     constexpr const char* fn = "cuda::matmul";
     if (ctx.outputs.size() != 1 || ctx.inputs.size() != 2) return Error{"cuda::matmul: expects 1 output, 2 inputs"};

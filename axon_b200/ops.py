@@ -222,7 +222,7 @@ def matmul(out: torch.Tensor, a, b: torch.Tensor, stream: Optional[torch.cuda.St
     (src/backend/cpu_backend.cpp:116-173 with choose_gemm_strategy,
     src/backend/cpu/strategy.cpp:5-65): a packed :class:`QTensor` A goes to
     its format's quantized matmul, an fp32 A (all row-major [M x K] . [K x N])
-    to the fp32 GEMM (``axq_matmul_f32``, cuBLAS in pedantic fp32 mode)."""
+    to the fp32 GEMM (``axq_matmul_f32``, fp32 multiply-adds, no TF32)."""
     if isinstance(a, QTensor):
         return matmul_q(out, a, b, stream=stream, **kw)
     for t, name in ((a, "a"), (b, "b"), (out, "out")):

@@ -8,7 +8,7 @@
  * are asynchronous on `stream` (NULL = legacy default stream).  quantize,
  * dequantize and the matmuls allocate nothing (scratch is the caller's
  * workspace, or the built-in scratch of axq_matmul_noalloc); the
- * communicator, symmetric-buffer, fp32 (cuBLAS) and .axon entry points
+ * communicator, symmetric-buffer and .axon entry points
  * allocate as described beside them.
  *
  * Threads: any host thread may call the library, concurrently with others,
@@ -246,9 +246,8 @@ int axq_matmul_sharded(void* comm, int fmt, const void* a_q_local, const float* 
 /* ---- fp32 matmul (unquantized A) -------------------------------------------
  * Replaces cpu::matmul's fp32 path (src/backend/cpu_backend.cpp:116-173, routed
  * by choose_gemm_strategy, src/backend/cpu/strategy.cpp:35-58): row-major
- * out[M x N] = a[M x K] . b[K x N], all fp32 device buffers, as a cuBLAS SGEMM
- * in pedantic fp32 mode (no TF32).  cuBLAS is loaded at run time; without it
- * the call returns AXQ_ERR_UNSUPPORTED. */
+ * out[M x N] = a[M x K] . b[K x N], all fp32 device buffers, with fp32
+ * multiply-adds (no TF32): this library's own tiled kernel. */
 int axq_matmul_f32(const float* a, const float* b, float* out, int64_t M, int64_t K, int64_t N, axq_stream_t stream);
 
 /* ---- .axon tensor files ---------------------------------------------------

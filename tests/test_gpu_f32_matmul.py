@@ -1,5 +1,5 @@
-"""fp32 matmul for unquantized A (axq_matmul_f32, cuBLAS SGEMM in pedantic
-fp32 mode) against the reference's own cpu::matmul
+"""fp32 matmul for unquantized A (axq_matmul_f32, this library's tiled fp32
+kernel) against the reference's own cpu::matmul
 (src/backend/cpu_backend.cpp:116-173, compiled into oracle/_ref) and a
 float64 product.  The sums are the same fp32 products added in a different
 order, so the tolerance is float rounding over K terms:
@@ -13,7 +13,8 @@ pytestmark = pytest.mark.gpu
 TOL = 2e-5
 
 
-@pytest.mark.parametrize("M,K,N", [(1, 64, 1), (64, 4096, 3), (300, 1000, 257), (512, 512, 512), (7, 33, 130)])
+@pytest.mark.parametrize("M,K,N", [(1, 64, 1), (64, 4096, 3), (300, 1000, 257), (512, 512, 512), (7, 33, 130),
+                                   (129, 17, 131), (256, 2048, 384), (1000, 3, 5)])
 def test_f32_matmul_matches_reference(cuda, M, K, N):
     import oracle
     import axon_b200 as ax
