@@ -120,61 +120,64 @@ int allgather_inplace(Comm* c, float* buf, size_t count, cudaStream_t s, const c
 // ---- symmetric buffers (CUDA IPC) and the peer-store barrier ---------------
 
 // Layout of one rank's allocation: [output: bytes, rounded to 256] then the
-// landing area, two copies of the output that the peer-store GEMVs of all
-// ranks fill alternately (call e into copy e & 1), then the control block,
-// one 128-byte line per counter: the completion counter (every rank adds 1
-// per call), this rank's finished-CTA counter, its call count (epoch) and
-// the finished-block counter of its wait kernel.
-constexpr size_t kSymmCtrlBytes = 512;
+// landing area, two copies of 8-byte slots (one per output value: the value's
+// bits tagged with the call number in the high word) that the peer-store
+// GEMVs of all ranks fill alternately (call e into copy e & 1), then the
+// control block, one 128-byte line per counter: this rank's call count
+// (epoch) and the finished-block counter of its wait kernel.
+constexpr size_t kSymmCtrlBytes = 256;
 constexpr int kMaxRanks = 64;  // the GEMV epilogue stores to every rank in turn
 
 struct Symm {
     Comm* c = nullptr;
     size_t bytes = 0, data_bytes = 0;
     uint8_t* local = nullptr;
-    std::vector<uint8_t*> peer;       // every rank's allocation (peer[rank] = local)
-    float** d_land = nullptr;         // device: landing area of every rank
-    unsigned** d_comp = nullptr;      // device: completion counter of every rank
-    bool pending = false;             // a peer-store call awaits its axq_symm_wait
-    int* pending_err = nullptr;       // status word of that call's workspace
-    size_t pending_floats = 0;        // M x N of that call (what the wait copies out)
+    std::vector<uint8_t*> peer;            // every rank's allocation (peer[rank] = local)
+    unsigned long long** d_land = nullptr;  // device: landing area of every rank
+    bool pending = false;                  // a peer-store call awaits its axq_symm_wait
+    int* pending_err = nullptr;            // status word of that call's workspace
+    size_t pending_floats = 0;             // M x N of that call (what the wait copies out)
+    // one landing copy: 8 bytes per output float
+    static size_t land_bytes(size_t data_bytes) { return 2 * data_bytes; }
     static uint8_t* land(uint8_t* base, size_t data_bytes) { return base + data_bytes; }
     static unsigned* ctrl(uint8_t* base, size_t data_bytes, int line) {
-        return reinterpret_cast<unsigned*>(base + 3 * data_bytes + 128 * line);
+        return reinterpret_cast<unsigned*>(base + data_bytes + 2 * land_bytes(data_bytes) + 128 * line);
     }
-    unsigned* comp() const { return ctrl(local, data_bytes, 0); }
-    unsigned* done() const { return ctrl(local, data_bytes, 1); }
-    unsigned* epoch() const { return ctrl(local, data_bytes, 2); }
-    unsigned* wait_blocks() const { return ctrl(local, data_bytes, 3); }
+    static size_t alloc_bytes(size_t data_bytes) { return data_bytes + 2 * land_bytes(data_bytes) + kSymmCtrlBytes; }
+    unsigned* epoch() const { return ctrl(local, data_bytes, 0); }
+    unsigned* wait_blocks() const { return ctrl(local, data_bytes, 1); }
 };
 
-// Waits until every rank has signalled this rank's completion counter for
-// the next call (its peer stores into this rank's landing copy are then
-// visible), copies that landing copy (n floats) into the output, and
-// advances the call count.  Every block polls; the last block to finish
-// advances the epoch, after every block has read it.  Bounded: a rank that
-// never signals sets *err, the copy proceeds, and the wait gives up.  It
+// Waits until every value of the next call (e = epoch + 1) has landed in
+// this rank's landing copy e & 1 (its slot carries the tag e; the 8-byte
+// store that wrote it was single-copy atomic, so the value came with it) and
+// copies the n values into the output; the last block to finish advances
+// the call count, after every block has read it.  Bounded: slots still
+// missing after kPeerWaitNs set *err, and the copy takes what is there.  It
 // first waits for the stream's earlier kernels, so calls complete in order
 // even when several buffers have calls outstanding.
-__global__ void peer_wait_kernel(const unsigned* comp, unsigned* epoch, unsigned* blocks_done, const float* land0,
-                                 int64_t land_stride, float* out, int64_t n, int nranks, int* err) {
+__global__ void peer_wait_kernel(unsigned* epoch, unsigned* blocks_done, const unsigned long long* land0,
+                                 int64_t land_stride, float* out, int64_t n, int* err) {
     pdl_wait();  // every earlier kernel of the stream (and its epoch update) is complete
     pdl_launch_dependents();
     const unsigned e = *epoch + 1;
-    if (threadIdx.x == 0) {
-        // every rank adds 1 per call, and no rank can signal call e + 1 before
-        // this rank's wait for call e is over, so the sum reaches e * nranks
-        // only once every rank has signalled call e
-        if (!poll_counter_sys(comp, e * static_cast<unsigned>(nranks), kPeerWaitNs)) atomicExch(err, 1);
-    }
-    __syncthreads();
-    const float* src = land0 + static_cast<int64_t>(e & 1u) * land_stride;
+    const unsigned long long* src = land0 + static_cast<int64_t>(e & 1u) * land_stride;
     const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    const int64_t n4 = n / 4;  // landing copies and output are 256-byte aligned
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4; i += stride)
-        reinterpret_cast<float4*>(out)[i] = reinterpret_cast<const float4*>(src)[i];
-    for (int64_t i = 4 * n4 + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
-        out[i] = src[i];
+    const uint64_t t0 = globaltimer_ns();
+    bool late = false;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
+        unsigned long long v = ld_relaxed_sys_u64(src + i);
+        while (static_cast<unsigned>(v >> 32) != e && !late) {
+            if (globaltimer_ns() - t0 > kPeerWaitNs) {
+                late = true;  // a rank never stored this slot: report, copy what is there
+                atomicExch(err, 1);
+                break;
+            }
+            __nanosleep(64);
+            v = ld_relaxed_sys_u64(src + i);
+        }
+        out[i] = __uint_as_float(static_cast<unsigned>(v));
+    }
     __syncthreads();
     if (threadIdx.x == 0 && atomicAdd(blocks_done, 1u) == gridDim.x - 1) {
         *blocks_done = 0u;
@@ -342,14 +345,15 @@ int axq_symm_create(void* comm, size_t bytes, void** symm_out, void** local_out)
         set_last_error(std::string(fn) + ": " + what + ": " + cudaGetErrorString(e));
         return AXQ_ERR_CUDA;
     };
-    cudaError_t e = cudaMalloc(&y->local, 3 * y->data_bytes + kSymmCtrlBytes);
+    cudaError_t e = cudaMalloc(&y->local, Symm::alloc_bytes(y->data_bytes));
     if (e != cudaSuccess) {
         delete y;
         return cuda_err(e, "cudaMalloc");
     }
-    cudaMemset(y->local + 3 * y->data_bytes, 0, kSymmCtrlBytes);
+    // landing slots start with tag 0 (no call) and the counters at 0
+    e = cudaMemset(y->local + y->data_bytes, 0, Symm::alloc_bytes(y->data_bytes) - y->data_bytes);
     cudaIpcMemHandle_t h;
-    e = cudaIpcGetMemHandle(&h, y->local);
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, y->local);
     // exchange the handles: an all-gather of G x 64 bytes on the communicator
     uint8_t* d_h = nullptr;
     std::vector<cudaIpcMemHandle_t> hs(G);
@@ -383,16 +387,12 @@ int axq_symm_create(void* comm, size_t bytes, void** symm_out, void** local_out)
         e = cudaIpcOpenMemHandle(&p, hs[g], cudaIpcMemLazyEnablePeerAccess);
         y->peer[g] = static_cast<uint8_t*>(p);
     }
-    std::vector<float*> lands(G);
-    std::vector<unsigned*> cmp(G);
-    for (int g = 0; g < G; ++g) {
-        lands[g] = y->peer[g] ? reinterpret_cast<float*>(Symm::land(y->peer[g], y->data_bytes)) : nullptr;
-        cmp[g] = y->peer[g] ? Symm::ctrl(y->peer[g], y->data_bytes, 0) : nullptr;
-    }
-    if (e == cudaSuccess) e = cudaMalloc(&y->d_land, G * sizeof(float*));
-    if (e == cudaSuccess) e = cudaMalloc(&y->d_comp, G * sizeof(unsigned*));
-    if (e == cudaSuccess) e = cudaMemcpy(y->d_land, lands.data(), G * sizeof(float*), cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = cudaMemcpy(y->d_comp, cmp.data(), G * sizeof(unsigned*), cudaMemcpyHostToDevice);
+    std::vector<unsigned long long*> lands(G);
+    for (int g = 0; g < G; ++g)
+        lands[g] = y->peer[g] ? reinterpret_cast<unsigned long long*>(Symm::land(y->peer[g], y->data_bytes)) : nullptr;
+    if (e == cudaSuccess) e = cudaMalloc(&y->d_land, G * sizeof(unsigned long long*));
+    if (e == cudaSuccess)
+        e = cudaMemcpy(y->d_land, lands.data(), G * sizeof(unsigned long long*), cudaMemcpyHostToDevice);
     if (e != cudaSuccess) {
         axq_symm_destroy(y);
         return cuda_err(e, "peer mapping");
@@ -409,7 +409,6 @@ int axq_symm_destroy(void* symm) {
     for (size_t g = 0; g < y->peer.size(); ++g)
         if (static_cast<int>(g) != y->c->rank && y->peer[g]) cudaIpcCloseMemHandle(y->peer[g]);
     if (y->d_land) cudaFree(y->d_land);
-    if (y->d_comp) cudaFree(y->d_comp);
     if (y->local) cudaFree(y->local);
     delete y;
     return AXQ_OK;
@@ -425,12 +424,12 @@ int axq_symm_wait(void* symm, axq_stream_t stream) {
     if (!y->pending) return AXQ_OK;  // the last call already completed in stream order
     y->pending = false;
     const int64_t n = static_cast<int64_t>(y->pending_floats);
-    const int blocks = static_cast<int>(std::min<int64_t>(64, std::max<int64_t>(1, (n / 4 + 255) / 256)));
+    const int blocks = static_cast<int>(std::min<int64_t>(128, std::max<int64_t>(1, (n + 255) / 256)));
     cudaError_t e = launch_pdl(peer_wait_kernel, dim3(blocks), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream),
-                               static_cast<const unsigned*>(y->comp()), y->epoch(), y->wait_blocks(),
-                               reinterpret_cast<const float*>(Symm::land(y->local, y->data_bytes)),
-                               static_cast<int64_t>(y->data_bytes / 4), reinterpret_cast<float*>(y->local), n,
-                               y->c->nranks, y->pending_err);
+                               y->epoch(), y->wait_blocks(),
+                               reinterpret_cast<const unsigned long long*>(Symm::land(y->local, y->data_bytes)),
+                               static_cast<int64_t>(Symm::land_bytes(y->data_bytes) / 8), reinterpret_cast<float*>(y->local),
+                               n, y->pending_err);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) {
         set_last_error(std::string("axq_symm_wait: ") + cudaGetErrorString(e));
@@ -501,8 +500,8 @@ int axq_matmul_sharded_p2p_async(void* symm, int fmt, const void* a_q_local, con
         return AXQ_ERR_COMM;
     }
     int* err = static_cast<int*>(workspace);
-    GemvPeers peers{y->d_land, y->d_comp, y->done(), y->epoch(), static_cast<int64_t>(y->data_bytes / 4),
-                    c->rank * rows, c->nranks, c->rank};
+    GemvPeers peers{y->d_land, y->epoch(), static_cast<int64_t>(Symm::land_bytes(y->data_bytes) / 8), c->rank * rows,
+                    c->nranks, c->rank};
     cudaError_t e = gemv_dispatch(fmt, a_q_local, nullptr, b, mine, rows, K, N, static_cast<int>(flags),
                                   static_cast<uint8_t*>(workspace) + 256, workspace_bytes - 256, err, s, &peers);
     if (e == cudaSuccess) {

@@ -655,17 +655,16 @@ struct GemvArgs {
     const uint8_t* w2;
     int pair;
     // peer-store epilogue (npeers > 0, row-major out only): each output value
-    // is stored at row row_offset + row of copy (*epoch + 1) & 1 of every
-    // rank's landing area (peer_land[g], mapped over NVLink; a.out is
-    // unused), and the grid's last CTA then adds 1 to every rank's
-    // completion counter peer_comp[g].  Two copies alternate by call, so no
-    // rank waits for the others before storing: a rank starts call e + 2's
-    // stores only after its wait for call e + 1, which needs every rank's
-    // call e + 1, which each rank issues after its own wait for call e (the
-    // read of copy e & 1).
-    float* const* peer_land;
-    unsigned* const* peer_comp;
-    unsigned* done;  // finished-CTA count of this grid (reset by the last CTA)
+    // v of call e (= *epoch + 1) is stored as one 8-byte slot (e << 32) | bits(v)
+    // at row row_offset + row of copy e & 1 of every rank's landing area
+    // (peer_land[g], mapped over NVLink; a.out is unused).  An 8-byte store is
+    // single-copy atomic, so a reader that sees the tag e sees the value: no
+    // fence or counter is needed.  Two copies alternate by call, so no rank
+    // waits for the others before storing: a rank starts call e + 2's stores
+    // only after its wait for call e + 1, which needs every rank's call e + 1,
+    // which each rank issues after its own wait for call e (the read of copy
+    // e & 1).
+    unsigned long long* const* peer_land;
     const unsigned* epoch;
     int64_t land_stride;
     int64_t row_offset;
@@ -701,7 +700,8 @@ __device__ __forceinline__ void consume(const GemvArgs& a, uint8_t* stages, floa
     int s = 0, unit_par = 0;
     uint32_t phase = 0;
     // peer-store calls: this call's copy of every rank's landing area
-    const int64_t land_off = a.npeers > 0 ? static_cast<int64_t>((*a.epoch + 1u) & 1u) * a.land_stride : 0;
+    const unsigned call = a.npeers > 0 ? *a.epoch + 1u : 0u;
+    const int64_t land_off = static_cast<int64_t>(call & 1u) * a.land_stride;
     bool aborted = false;
     const uintptr_t base0 = slot_base(a, pr), base1 = slot_base(a, pr + 8);
     for (int64_t u = blockIdx.x; u < a.units; u += gridDim.x, unit_par ^= 1) {
@@ -775,7 +775,9 @@ __device__ __forceinline__ void consume(const GemvArgs& a, uint8_t* stages, floa
                     }
                     if (a.npeers > 0) {
                         const int64_t gi = land_off + (a.row_offset + orow) * a.out_ld + t;
-                        for (int g = 0; g < a.npeers; ++g) a.peer_land[g][gi] = v;
+                        const unsigned long long slot =
+                            (static_cast<unsigned long long>(call) << 32) | __float_as_uint(v);
+                        for (int g = 0; g < a.npeers; ++g) st_relaxed_sys_u64(a.peer_land[g] + gi, slot);
                     } else if (a.out_tokmajor) {
                         a.out[t * a.out_ld + orow] = v;
                     } else {
@@ -878,19 +880,6 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
     pdl_wait();  // activation records of this call are complete
     if (warp < 4) consume<F, NT, AL, 0>(a, stages, red, full, empty, abort_flag, warp, lane);
     else consume<F, NT, AL, 1>(a, stages, red, full, empty, abort_flag, warp, lane);
-    if (a.npeers > 0 && warp == 0) {
-        // The warp's peer stores are ordered before the CTA counts itself
-        // (a GPU-scope release, cumulative over the warp barrier); the last
-        // CTA acquires every count, and one system-scope release fence (its
-        // cumulativity covers all the stores it has observed) precedes its
-        // signal to each rank.  A system fence in every CTA costs far more.
-        __syncwarp();
-        if (lane == 0 && atom_add_acq_rel_gpu_u32(a.done, 1u) == gridDim.x - 1) {
-            *a.done = 0u;  // the next call's CTAs count only after this grid completes
-            fence_acq_rel_sys();
-            for (int g = 0; g < a.npeers; ++g) red_add_sys_u32(a.peer_comp[g], 1u);
-        }
-    }
 }
 
 struct GemvPlan {
@@ -966,8 +955,6 @@ cudaError_t launch_gemv(const void* w, const void* w2, const float* x, float* ou
     if (peers) {
         if (N > kGemvMaxN || (flags & AXQ_FLAG_OUT_TOKMAJOR)) return cudaErrorInvalidValue;
         a.peer_land = peers->land;
-        a.peer_comp = peers->comp;
-        a.done = peers->done;
         a.epoch = peers->epoch;
         a.land_stride = peers->land_stride;
         a.row_offset = peers->row_offset;

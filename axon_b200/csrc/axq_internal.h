@@ -39,14 +39,12 @@ size_t gemv_workspace_bytes(int64_t Kp, int64_t ntok);
 // finished-CTA counter, entry counters and call epoch, and the global row of
 // local row 0.
 // Peer-store GEMV epilogue of a row-sharded matmul: land[g] is rank g's
-// landing area, two copies of the full output `land_stride` floats apart;
-// call e (1-based: *epoch + 1, epoch = calls this rank has waited for)
-// stores into copy e & 1 at row row_offset + row of every rank; comp[g] is
-// rank g's completion counter and done this rank's finished-CTA counter.
+// landing area, two copies of the full output `land_stride` 8-byte slots
+// apart; call e (1-based: *epoch + 1, epoch = calls this rank has waited
+// for) stores each output value, tagged with e in the slot's high word, into
+// copy e & 1 at row row_offset + row of every rank.
 struct GemvPeers {
-    float* const* land;
-    unsigned* const* comp;
-    unsigned* done;
+    unsigned long long* const* land;
     const unsigned* epoch;
     int64_t land_stride;
     int64_t row_offset;

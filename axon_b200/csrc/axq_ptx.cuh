@@ -187,6 +187,17 @@ __device__ __forceinline__ unsigned ld_acquire_cta_shared_u32(const unsigned* p)
 
 // Polls *p (acquire, system scope) until the counter has reached `target`
 // ((int)(*p - target) >= 0, wrap-safe); false after limit_ns of global time.
+// 8-byte relaxed store / load at system scope (slots read by other GPUs;
+// single-copy atomic when 8-byte aligned).
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
 __device__ __forceinline__ bool poll_counter_sys(const unsigned* p, unsigned target, uint64_t limit_ns) {
     if (static_cast<int>(ld_acquire_sys_u32(p) - target) >= 0) return true;
     const uint64_t t0 = globaltimer_ns();

@@ -110,12 +110,12 @@ def test_one_rank_peer_store_async_and_wait(orc, comm1):
 
 
 def test_one_rank_peer_waits_run_out_and_context_survives(orc, comm1):
-    """Failure detection without a GPU fault: the buffer's call count is
-    advanced by hand (a count no rank will ever reach), so the next call's
-    completion wait (peer_wait_kernel) gives up on its own one-second bound
-    and reports through the call's workspace status word.  The context stays
-    usable: a plain matmul and a fresh symmetric buffer still give the
-    oracle's result."""
+    """Failure detection without a GPU fault: between a call and its wait the
+    buffer's call count is advanced by hand, so the wait (peer_wait_kernel)
+    looks for landing slots tagged with a call number no rank ever stores,
+    gives up on its own one-second bound and reports through the call's
+    workspace status word.  The context stays usable: a plain matmul and a
+    fresh symmetric buffer still give the oracle's result."""
     import time
     import torch
     import axon_b200 as ax
@@ -131,15 +131,17 @@ def test_one_rank_peer_waits_run_out_and_context_survives(orc, comm1):
     buf = ax.SymmetricBuffer(comm1, 4 * M * N)
     try:
         assert rel_err(ax.matmul_sharded_p2p(buf, a, bd, M, workspace=ws).cpu().numpy(), y_ref) <= TOL
-        # control block after the output and its two landing copies (each
-        # rounded up to 256 bytes), one 128-byte line each: completion count,
-        # finished CTAs, call count, finished wait blocks
+        # control block after the output (rounded up to 256 bytes) and its two
+        # landing copies (8 bytes per output value each), one 128-byte line
+        # each: call count, finished wait blocks
         data_bytes = -(-buf.nbytes // 256) * 256
-        calls = torch.as_tensor(_CudaArray(buf.ptr + 3 * data_bytes + 2 * 128, (1,), "<i4"), device="cuda")
-        calls += 1
+        calls = torch.as_tensor(_CudaArray(buf.ptr + 5 * data_bytes, (1,), "<i4"), device="cuda")
+        ax.matmul_sharded_p2p(buf, a, bd, M, workspace=ws, wait=False)  # stores call 2's tags
+        torch.cuda.synchronize()
+        calls += 1  # the wait now expects call 3
         torch.cuda.synchronize()
         t0 = time.time()
-        ax.matmul_sharded_p2p(buf, a, bd, M, workspace=ws)
+        buf.wait()
         wp = ws.get(1, bd.device).data_ptr()
         wp += (-wp) % 256
         with pytest.raises(ax.AxqError) as e:
