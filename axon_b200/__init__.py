@@ -60,6 +60,7 @@ from .shard import (  # noqa: F401
     Communicator,
     SymmetricBuffer,
     matmul_sharded_p2p,
+    wait_all,
     allgather_,
     matmul_sharded,
     row_bytes,
@@ -71,5 +72,5 @@ __all__ = [
     "AxqError", "QuantFormat", "QTensor", "Status", "Workspace", "quantize", "dequantize", "matmul_q",
     "matmul_q8_0", "matmul_q4", "matmul_q2_K", "matmul_q3_K", "matmul_q4_K", "matmul_q5_K", "matmul_q6_K",
     "linear_q", "gate_up_silu", "mlp_q", "quantized_size", "quantized_size_2d", "matmul_workspace_size", "lib", "lib_path",
-    "Communicator", "SymmetricBuffer", "matmul_sharded_p2p", "allgather_", "matmul_sharded", "row_bytes", "shard_bounds", "shard_rows",
+    "Communicator", "SymmetricBuffer", "matmul_sharded_p2p", "wait_all", "allgather_", "matmul_sharded", "row_bytes", "shard_bounds", "shard_rows",
 ]

@@ -95,6 +95,7 @@ SIGNATURES = {
                                               _vp]),
     "axq_matmul_sharded_p2p_async": (ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, _i64, _i64, _i64, ctypes.c_uint, _vp,
                                                     _sz, _vp]),
+    "axq_symm_wait_many": (ctypes.c_int, [_vp, ctypes.c_int, _vp]),
     "axq_symm_wait": (ctypes.c_int, [_vp, _vp]),
     "axq_matmul_f32": (ctypes.c_int, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "axq_axon_open": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(_vp), ctypes.POINTER(ctypes.c_uint32)]),

@@ -148,40 +148,57 @@ struct Symm {
     unsigned* wait_blocks() const { return ctrl(local, data_bytes, 1); }
 };
 
-// Waits until every value of the next call (e = epoch + 1) has landed in
-// this rank's landing copy e & 1 (its slot carries the tag e; the 8-byte
-// store that wrote it was single-copy atomic, so the value came with it) and
-// copies the n values into the output; the last block to finish advances
-// the call count, after every block has read it.  Bounded: slots still
-// missing after kPeerWaitNs set *err, and the copy takes what is there.  It
-// first waits for the stream's earlier kernels, so calls complete in order
-// even when several buffers have calls outstanding.
-__global__ void peer_wait_kernel(unsigned* epoch, unsigned* blocks_done, const unsigned long long* land0,
-                                 int64_t land_stride, float* out, int64_t n, int* err) {
+// One buffer's wait: its call count, finished-block counter, landing copies
+// (land_stride slots apart), output of n values and status word.
+struct WaitJob {
+    unsigned* epoch;
+    unsigned* blocks_done;
+    const unsigned long long* land0;
+    int64_t land_stride;
+    float* out;
+    int64_t n;
+    int* err;
+};
+constexpr int kMaxWaitJobs = 8;
+struct WaitJobs {
+    WaitJob j[kMaxWaitJobs];
+};
+
+// Block row y waits for buffer y: until every value of its next call
+// (e = epoch + 1) has landed in this rank's landing copy e & 1 (its slot
+// carries the tag e; the 8-byte store that wrote it was single-copy atomic,
+// so the value came with it), copying the n values into the output; the
+// last block of the row advances that buffer's call count, after every
+// block has read it.  Bounded: slots still missing after kPeerWaitNs set the
+// call's status word, and the copy takes what is there.  It first waits for
+// the stream's earlier kernels, so calls complete in order even when several
+// buffers have calls outstanding.
+__global__ void peer_wait_kernel(WaitJobs jobs) {
     pdl_wait();  // every earlier kernel of the stream (and its epoch update) is complete
     pdl_launch_dependents();
-    const unsigned e = *epoch + 1;
-    const unsigned long long* src = land0 + static_cast<int64_t>(e & 1u) * land_stride;
+    const WaitJob& w = jobs.j[blockIdx.y];
+    const unsigned e = *w.epoch + 1;
+    const unsigned long long* src = w.land0 + static_cast<int64_t>(e & 1u) * w.land_stride;
     const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
     const uint64_t t0 = globaltimer_ns();
     bool late = false;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < w.n; i += stride) {
         unsigned long long v = ld_relaxed_sys_u64(src + i);
         while (static_cast<unsigned>(v >> 32) != e && !late) {
             if (globaltimer_ns() - t0 > kPeerWaitNs) {
                 late = true;  // a rank never stored this slot: report, copy what is there
-                atomicExch(err, 1);
+                atomicExch(w.err, 1);
                 break;
             }
             __nanosleep(64);
             v = ld_relaxed_sys_u64(src + i);
         }
-        out[i] = __uint_as_float(static_cast<unsigned>(v));
+        w.out[i] = __uint_as_float(static_cast<unsigned>(v));
     }
     __syncthreads();
-    if (threadIdx.x == 0 && atomicAdd(blocks_done, 1u) == gridDim.x - 1) {
-        *blocks_done = 0u;
-        *epoch = e;
+    if (threadIdx.x == 0 && atomicAdd(w.blocks_done, 1u) == gridDim.x - 1) {
+        *w.blocks_done = 0u;
+        *w.epoch = e;
     }
 }
 
@@ -414,28 +431,68 @@ int axq_symm_destroy(void* symm) {
     return AXQ_OK;
 }
 
+int axq_symm_wait_many(void* const* symms, int n, axq_stream_t stream) {
+    const char* fn = "axq_symm_wait_many";
+    if (n < 0 || (n > 0 && !symms)) {
+        set_last_error(std::string(fn) + ": invalid arguments");
+        return AXQ_ERR_INVALID;
+    }
+    for (int i = 0; i < n; ++i) {
+        auto* y = static_cast<Symm*>(symms[i]);
+        if (!y) {
+            set_last_error(std::string(fn) + ": symmetric buffer is NULL");
+            return AXQ_ERR_INVALID;
+        }
+        if (int e = check_comm(y->c, fn)) return e;
+        for (int k = 0; k < i; ++k)
+            if (symms[k] == symms[i]) {
+                set_last_error(std::string(fn) + ": a buffer appears twice");
+                return AXQ_ERR_INVALID;
+            }
+    }
+    WaitJobs jobs{};
+    int nj = 0;
+    int64_t most = 1;
+    // one launch per kMaxWaitJobs outstanding buffers: block row y waits for job y
+    auto flush = [&]() -> int {
+        if (nj == 0) return AXQ_OK;
+        const int blocks = static_cast<int>(std::min<int64_t>(128, (most + 255) / 256));
+        cudaError_t e = launch_pdl(peer_wait_kernel, dim3(blocks, static_cast<unsigned>(nj)), dim3(256), 0,
+                                   reinterpret_cast<cudaStream_t>(stream), jobs);
+        if (e == cudaSuccess) e = cudaGetLastError();
+        nj = 0;
+        most = 1;
+        if (e != cudaSuccess) {
+            set_last_error(std::string(fn) + ": " + cudaGetErrorString(e));
+            return AXQ_ERR_CUDA;
+        }
+        return AXQ_OK;
+    };
+    for (int i = 0; i < n; ++i) {
+        auto* y = static_cast<Symm*>(symms[i]);
+        if (!y->pending) continue;  // its last call already completed in stream order
+        if (nj == kMaxWaitJobs)
+            if (int st = flush()) return st;
+        WaitJob& w = jobs.j[nj++];
+        w.epoch = y->epoch();
+        w.blocks_done = y->wait_blocks();
+        w.land0 = reinterpret_cast<const unsigned long long*>(Symm::land(y->local, y->data_bytes));
+        w.land_stride = static_cast<int64_t>(Symm::land_bytes(y->data_bytes) / 8);
+        w.out = reinterpret_cast<float*>(y->local);
+        w.n = static_cast<int64_t>(y->pending_floats);
+        w.err = y->pending_err;
+        most = std::max(most, w.n);
+        y->pending = false;
+    }
+    return flush();
+}
+
 int axq_symm_wait(void* symm, axq_stream_t stream) {
-    auto* y = static_cast<Symm*>(symm);
-    if (!y) {
+    if (!symm) {
         set_last_error("axq_symm_wait: symmetric buffer is NULL");
         return AXQ_ERR_INVALID;
     }
-    if (int e = check_comm(y->c, "axq_symm_wait")) return e;
-    if (!y->pending) return AXQ_OK;  // the last call already completed in stream order
-    y->pending = false;
-    const int64_t n = static_cast<int64_t>(y->pending_floats);
-    const int blocks = static_cast<int>(std::min<int64_t>(128, std::max<int64_t>(1, (n + 255) / 256)));
-    cudaError_t e = launch_pdl(peer_wait_kernel, dim3(blocks), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream),
-                               y->epoch(), y->wait_blocks(),
-                               reinterpret_cast<const unsigned long long*>(Symm::land(y->local, y->data_bytes)),
-                               static_cast<int64_t>(Symm::land_bytes(y->data_bytes) / 8), reinterpret_cast<float*>(y->local),
-                               n, y->pending_err);
-    if (e == cudaSuccess) e = cudaGetLastError();
-    if (e != cudaSuccess) {
-        set_last_error(std::string("axq_symm_wait: ") + cudaGetErrorString(e));
-        return AXQ_ERR_CUDA;
-    }
-    return AXQ_OK;
+    return axq_symm_wait_many(&symm, 1, stream);
 }
 
 int axq_matmul_sharded_p2p(void* symm, int fmt, const void* a_q_local, const float* b, int64_t M, int64_t K, int64_t N,

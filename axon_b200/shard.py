@@ -217,6 +217,17 @@ class SymmetricBuffer:
             check(lib().axq_symm_destroy(h))
 
 
+def wait_all(buffers, stream: Optional[torch.cuda.Stream] = None) -> None:
+    """Enqueue the waits of several symmetric buffers' outstanding peer-store
+    calls as one kernel (axq_symm_wait_many)."""
+    bufs = list(buffers)
+    if not bufs:
+        return
+    arr = (ctypes.c_void_p * len(bufs))(*[b.handle.value for b in bufs])
+    dev = torch.device("cuda", torch.cuda.current_device())
+    check(lib().axq_symm_wait_many(ctypes.cast(arr, ctypes.c_void_p), len(bufs), _stream_handle(stream, dev)))
+
+
 def matmul_sharded_p2p(out: SymmetricBuffer, a_local: QTensor, b: torch.Tensor, M: int, b_tokmajor: bool = False,
                        workspace: Optional[Workspace] = None, stream: Optional[torch.cuda.Stream] = None,
                        wait: bool = True) -> torch.Tensor:

@@ -304,12 +304,15 @@ def run_gpu(args):
         if world > 1:
             symm[fmt].wait()
 
+    def wait_all():
+        if world > 1:
+            ax.wait_all([symm[f] for f in FORMATS])
+
     def one_pass():
-        # the three matmuls back to back, then their completion waits
+        # the three matmuls back to back, then their completion waits (one kernel)
         for fmt in FORMATS:
             run_fmt(fmt)
-        for fmt in FORMATS:
-            wait_fmt(fmt)
+        wait_all()
 
     def barrier():
         if world > 1:
@@ -396,8 +399,7 @@ def run_gpu(args):
         xd.copy_(xh, non_blocking=True)
         for fmt in FORMATS:
             run_fmt(fmt, xin=xd)
-        for fmt in FORMATS:
-            wait_fmt(fmt)
+        wait_all()
         if world > 1:
             for i, f in enumerate(FORMATS):
                 yh[i * ROWS * M_TOK:(i + 1) * ROWS * M_TOK].copy_(symm[f].tensor((ROWS * M_TOK,)), non_blocking=True)
@@ -469,8 +471,8 @@ def run_gpu(args):
                     "d2h_bytes_per_step": 4 * M_TOK * ROWS * len(FORMATS) * passes,
                     "how": "public API per pass (linear_q / matmul_sharded_p2p) with the pinned-host copies, "
                            f"{chunk} passes per CUDA graph"},
-            # per matmul: activation prep + GEMV (+ the peer wait with several ranks)
-            "gpu_launches": (3 if world > 1 else 2) * len(FORMATS) * passes * args.steps,
+            # per matmul: activation prep + GEMV; with several ranks one wait per pass
+            "gpu_launches": (2 * len(FORMATS) + (1 if world > 1 else 0)) * passes * args.steps,
             "clocks": clocks,
         }
         line.update(extra)

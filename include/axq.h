@@ -233,6 +233,9 @@ int axq_matmul_sharded_p2p_async(void* symm, int fmt, const void* a_q_local, con
                                  int64_t N, unsigned flags, void* workspace, size_t workspace_bytes,
                                  axq_stream_t stream);
 int axq_symm_wait(void* symm, axq_stream_t stream);
+/* axq_symm_wait for several buffers (each at most once) in one kernel launch:
+ * the waits of the calls of one decode pass cost one launch instead of n. */
+int axq_symm_wait_many(void* const* symms, int n, axq_stream_t stream);
 
 /* out[M x N] (row-major, full size on every rank) = A_q . B where this rank
  * passes only its row shard a_q_local (M/G packed rows of K elements).  The

@@ -111,7 +111,7 @@ def main(outdir):
             a = ax.QTensor(torch.from_numpy(np.ascontiguousarray(ax.shard_rows(q_full, M, K, F, world, rank))).to(dev),
                            (M // world, K), F)
             ops.append((a, torch.from_numpy(b).to(dev), M, N, orc.matmul(fmt, q_full, np.ascontiguousarray(b.T), M, K)))
-        for _ in range(2):
+        for it in range(2):
             for (a, bd, M, N, _), bb in zip(ops, (buf, buf2)):
                 ax.matmul_sharded_p2p(bb, a, bd, M, b_tokmajor=True, wait=False)
             try:
@@ -119,8 +119,11 @@ def main(outdir):
                 report["p2p_refused"] = None
             except ax.AxqError as e:
                 report["p2p_refused"] = int(e.status)
-            buf.wait()
-            buf2.wait()
+            if it == 0:
+                buf.wait()
+                buf2.wait()
+            else:
+                ax.wait_all([buf, buf2])  # both waits in one launch
             torch.cuda.synchronize()
             report["p2p_async"].append([rel_err(bb.tensor((M, N)).cpu().numpy(), y_ref)
                                         for (_, _, M, N, y_ref), bb in zip(ops, (buf, buf2))])

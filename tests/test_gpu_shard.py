@@ -89,7 +89,7 @@ def test_one_rank_peer_store_async_and_wait(orc, comm1):
         cases.append((a, torch.from_numpy(b).cuda(), M, N, orc.matmul(fmt, q, b, M, K)))
     bufs = [ax.SymmetricBuffer(comm1, 4 * M * N) for _, _, M, N, _ in cases]
     try:
-        for _ in range(3):
+        for it in range(3):
             for (a, bd, M, N, _), buf in zip(cases, bufs):
                 buf.tensor((M, N)).fill_(float("nan"))
                 ax.matmul_sharded_p2p(buf, a, bd, M, wait=False)
@@ -97,8 +97,12 @@ def test_one_rank_peer_store_async_and_wait(orc, comm1):
             with pytest.raises(ax.AxqError, match="axq_symm_wait first") as e:
                 ax.matmul_sharded_p2p(bufs[0], a, bd, M, wait=False)
             assert e.value.status == ax.Status.ERR_INVALID
+            if it == 1:
+                ax.wait_all(bufs)  # both waits in one launch
+            else:
+                for buf in bufs:
+                    buf.wait()
             for buf in bufs:
-                buf.wait()
                 buf.wait()  # nothing outstanding: a no-op
             torch.cuda.synchronize()
             for (_, _, M, N, y_ref), buf in zip(cases, bufs):
