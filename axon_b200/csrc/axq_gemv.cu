@@ -400,42 +400,45 @@ template <int H, int AL> struct RowOf<F_Q4_K, H, AL> { using T = RowQ4K<H, AL>; 
 template <int H, int AL> struct RowOf<F_Q5_K, H, AL> { using T = RowQ5K<H, AL>; };
 template <int H, int AL> struct RowOf<F_Q6_K, H, AL> { using T = RowQ6K<H, AL>; };
 
-// Half CG of two rows (c0, c1) of a K-quant format: every activation run is
-// loaded once and dotted with both rows' codes; acc[i][t] += row i's part.
-// Formats whose runs are 16 elements and whose code words are shared by the
-// runs 2s + lh of one lh (Q2_K, Q3_K) decode lh-major: the words of one lh
-// are loaded (and merged) once, then its four runs follow, so only those
-// words are live.
-template <int F, int H, int AL, int NT>
+// Half CG of NR rows (c0, and c1 when NR = 2) of a K-quant format: every
+// activation run is loaded once and dotted with each row's codes;
+// acc[i][t] += row i's part.  Formats whose runs are 16 elements and whose
+// code words are shared by the runs 2s + lh of one lh (Q2_K, Q3_K) decode
+// lh-major: the words of one lh are loaded (and merged) once, then its four
+// runs follow, so only those words are live.
+template <int F, int H, int AL, int NT, int NR>
 __device__ __forceinline__ void kquant_half(const uint8_t* c0, const uint8_t* c1, const ActCG& X, int ntok,
                                             bool valid, float (*acc)[NT]) {
-    using R = typename RowOf<F, H, AL>::T;
-    constexpr int RL = R::RL, NW = RL / 4, NR = 128 / RL;
-    constexpr bool LHM = R::LH_MAJOR;
+    using Row = typename RowOf<F, H, AL>::T;
+    constexpr int RL = Row::RL, NW = RL / 4, NRUN = 128 / RL;
+    constexpr bool LHM = Row::LH_MAJOR;
     static_assert(!LHM || RL == 16, "lh-major order is for 16-element runs");
-    R r0, r1;
-    r0.load(c0);
-    r1.load(c1);
+    static_assert(NR == 1 || NR == 2, "one or two rows per lane");
+    Row r[NR];
+    r[0].load(c0);
+    if constexpr (NR == 2) r[1].load(c1);
     // Q6_K decodes from shared memory per run and keeps more live values: a
     // shallower activation prefetch keeps it inside the register budget
     ActPipe<NT, true, H, (F == F_Q6_K) ? 2 : 3, LHM> P(X, ntok);
-    int hs[2][NT], ls[2][NT], ms[2][NT];
+    int hs[NR][NT], ls[NR][NT], ms[NR][NT];
 #pragma unroll
-    for (int t = 0; t < NT; ++t) hs[0][t] = hs[1][t] = ls[0][t] = ls[1][t] = ms[0][t] = ms[1][t] = 0;
-    static_for<NR>([&](auto Kc) {
+    for (int i = 0; i < NR; ++i)
+#pragma unroll
+        for (int t = 0; t < NT; ++t) hs[i][t] = ls[i][t] = ms[i][t] = 0;
+    static_for<NRUN>([&](auto Kc) {
         constexpr int K = decltype(Kc)::value;  // position in the decode order
         constexpr int J = LHM ? 2 * (K & 3) + (K >> 2) : K;
         constexpr int j0 = J * (RL / 16);
         if constexpr (LHM) {
             if constexpr ((K & 3) == 0) {
-                r0.template prep<(K >> 2)>();
-                r1.template prep<(K >> 2)>();
+#pragma unroll
+                for (int i = 0; i < NR; ++i) r[i].template prep<(K >> 2)>();
             }
         }
-        uint32_t qa[NW], qb[NW];
-        int sa, ma, sb, mb;
-        r0.template run<J>(qa, sa, ma);
-        r1.template run<J>(qb, sb, mb);
+        uint32_t q[NR][NW];
+        int sc[NR], m[NR];
+#pragma unroll
+        for (int i = 0; i < NR; ++i) r[i].template run<J>(q[i], sc[i], m[i]);
         if constexpr (LHM) {
             P.step(K);
         } else {
@@ -444,30 +447,34 @@ __device__ __forceinline__ void kquant_half(const uint8_t* c0, const uint8_t* c1
         }
 #pragma unroll
         for (int t = 0; t < NT; ++t) {  // padded tokens compute on the last token's data; never written
-            int ha, la, hb, lb, sx = P.sx[t][j0];
-            dot16<false>(qa, P.r[t][j0], ha, la);
-            dot16<false>(qb, P.r[t][j0], hb, lb);
-            if constexpr (RL == 32) {
-                int ha2, la2, hb2, lb2;
-                dot16<false>(qa + 4, P.r[t][j0 + 1], ha2, la2);
-                dot16<false>(qb + 4, P.r[t][j0 + 1], hb2, lb2);
-                ha += ha2; la += la2; hb += hb2; lb += lb2;
-                sx += P.sx[t][j0 + 1];
+            int sx = P.sx[t][j0];
+            if constexpr (RL == 32) sx += P.sx[t][j0 + 1];
+#pragma unroll
+            for (int i = 0; i < NR; ++i) {
+                int h, l;
+                dot16<false>(q[i], P.r[t][j0], h, l);
+                if constexpr (RL == 32) {
+                    int h2, l2;
+                    dot16<false>(q[i] + 4, P.r[t][j0 + 1], h2, l2);
+                    h += h2;
+                    l += l2;
+                }
+                hs[i][t] += sc[i] * h;
+                ls[i][t] += sc[i] * l;
+                ms[i][t] += m[i] * sx;
             }
-            hs[0][t] += sa * ha; ls[0][t] += sa * la; ms[0][t] += ma * sx;
-            hs[1][t] += sb * hb; ls[1][t] += sb * lb; ms[1][t] += mb * sx;
         }
     });
-    const float d0 = r0.dscale(), m0 = r0.mscale(), d1 = r1.dscale(), m1 = r1.mscale();
 #pragma unroll
-    for (int t = 0; t < NT; ++t) {
-        const float u = act_u(X, t);
-        const float dot0 = fmaf(254.0f, static_cast<float>(hs[0][t]), static_cast<float>(ls[0][t]));
-        const float dot1 = fmaf(254.0f, static_cast<float>(hs[1][t]), static_cast<float>(ls[1][t]));
-        const float v0 = fmaf(u, fmaf(d0, dot0, -m0 * static_cast<float>(ms[0][t])), acc[0][t]);
-        const float v1 = fmaf(u, fmaf(d1, dot1, -m1 * static_cast<float>(ms[1][t])), acc[1][t]);
-        acc[0][t] = valid ? v0 : acc[0][t];
-        acc[1][t] = valid ? v1 : acc[1][t];
+    for (int i = 0; i < NR; ++i) {
+        const float d = r[i].dscale(), mn = r[i].mscale();
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            const float u = act_u(X, t);
+            const float dot = fmaf(254.0f, static_cast<float>(hs[i][t]), static_cast<float>(ls[i][t]));
+            const float v = fmaf(u, fmaf(d, dot, -mn * static_cast<float>(ms[i][t])), acc[i][t]);
+            acc[i][t] = valid ? v : acc[i][t];
+        }
     }
 }
 
@@ -551,11 +558,15 @@ template <int F> struct Lane {
     static constexpr int CGB = (F == F_Q8_0) ? 8 * 34 : (F == F_Q4_0) ? 8 * 18 : Traits<F>::BB;
     static constexpr int A = (F == F_Q2_K) ? 4 : (F == F_Q4_K || F == F_Q5_K) ? 16 : 1;
     static constexpr int PERM = (F == F_Q4_0) ? 1 : 0;
-    template <int H, int AL, int NT>
+    template <int H, int AL, int NT, int NR>
     __device__ __forceinline__ static void half(const uint8_t* c0, const uint8_t* c1, int nblk_valid, const ActCG& X,
                                                 int ntok, bool valid, float (*acc)[NT]) {
-        if constexpr (F == F_Q8_0 || F == F_Q4_0) block32_half<F, H, NT>(c0, c1, nblk_valid, X, ntok, valid, acc);
-        else kquant_half<F, H, AL, NT>(c0, c1, X, ntok, valid, acc);
+        if constexpr (F == F_Q8_0 || F == F_Q4_0) {
+            static_assert(NR == 2, "the 32-element block formats decode two rows per lane");
+            block32_half<F, H, NT>(c0, c1, nblk_valid, X, ntok, valid, acc);
+        } else {
+            kquant_half<F, H, AL, NT, NR>(c0, c1, X, ntok, valid, acc);
+        }
     }
 };
 
@@ -683,20 +694,38 @@ __device__ __forceinline__ uintptr_t slot_base(const GemvArgs& a, int slot) {
     return reinterpret_cast<uintptr_t>((a.pair && slot >= 8) ? a.w2 : a.w);
 }
 
+// Rows decoded per lane: two (each activation run a lane loads serves two
+// rows) or one, which keeps the multi-token decode's activation runs and
+// per-token sums inside the register budget where two rows spilled.  The
+// one-row cases are those measured faster at W[28672 x 8192] (Q3_K and Q5_K
+// at four tokens: 123 vs 136 and 109 vs 132 us; Q6_K at two: 77 vs 100 us);
+// elsewhere two rows won.  Host and device agree through this function.
+template <int F, int NT>
+__host__ __device__ constexpr int rows_per_lane() {
+    return ((NT == 4 && (F == F_Q3_K || F == F_Q5_K)) || (NT == 2 && F == F_Q6_K)) ? 1 : 2;
+}
+
 // Consumer warps of one half H (warps 4H..4H+3) over every unit of this CTA:
-// wait for each stage, decode the lane's half CG of two rows, release the
-// stage; per unit, combine the partial sums across lanes and
-// warps and store the outputs (or, for peer-store calls, every rank's copy).
-template <int F, int NT, int AL, int H>
+// wait for each stage, decode the lane's half CGs, release the stage; per
+// unit, combine the partial sums across lanes and warps and store the
+// outputs (or, for peer-store calls, every rank's copy).
+//  NR = 2: lane l takes CG slot 4(w%4) + l/8 of the stage for rows l%8 and
+//          l%8 + 8 of the unit.
+//  NR = 1: lane l takes CG slots 2(w%4) + l/16 and that + 8 for row l%16.
+template <int F, int NT, int AL, int H, int NR>
 __device__ __forceinline__ void consume(const GemvArgs& a, uint8_t* stages, float* red, uint64_t* full,
                                         uint64_t* empty, volatile int* abort_flag, int warp, int lane) {
     using L = Lane<F>;
     static_assert((kStageCG * L::CGB) % 16 == 0, "a K-step must keep row segments' 16-byte phase");
-    const int cgl = 4 * (warp & 3) + (lane >> 3);  // CG slot in the stage
-    const int pr = lane & 7;                        // rows pr and pr + 8 of the unit
-    float acc[2][NT];
+    constexpr int NCG = 2 / NR;  // CG slots per lane per stage
+    constexpr int kSlotStep = kStageCG / 2;
+    const int cgl = NR == 2 ? 4 * (warp & 3) + (lane >> 3) : 2 * (warp & 3) + (lane >> 4);
+    const int pr = NR == 2 ? (lane & 7) : (lane & 15);  // first stage row of the lane
+    float acc[NR][NT];
 #pragma unroll
-    for (int t = 0; t < NT; ++t) acc[0][t] = acc[1][t] = 0.0f;
+    for (int i = 0; i < NR; ++i)
+#pragma unroll
+        for (int t = 0; t < NT; ++t) acc[i][t] = 0.0f;
     int s = 0, unit_par = 0;
     uint32_t phase = 0;
     // peer-store calls: this call's copy of every rank's landing area
@@ -706,7 +735,7 @@ __device__ __forceinline__ void consume(const GemvArgs& a, uint8_t* stages, floa
     const uintptr_t base0 = slot_base(a, pr), base1 = slot_base(a, pr + 8);
     for (int64_t u = blockIdx.x; u < a.units; u += gridDim.x, unit_par ^= 1) {
         const int64_t row0 = slot_row(a, u, pr), row1 = slot_row(a, u, pr + 8);
-        const bool ok0 = row0 < a.rows, ok1 = row1 < a.rows;
+        const bool ok0 = row0 < a.rows, ok1 = NR == 2 && row1 < a.rows;
         // Each row segment sits in its stage row at the segment's offset
         // modulo 16 (the bulk copy starts at the 16-byte boundary below it);
         // K-steps advance by step_bytes, a multiple of 16, so the offset is
@@ -717,6 +746,7 @@ __device__ __forceinline__ void consume(const GemvArgs& a, uint8_t* stages, floa
         // a row past the end decodes row0 again; its sum is never written
         const uint8_t* stage_lane1 = ok1 ? stages + cgl * L::CGB + (pr + 8) * a.rs + mis1 : stage_lane0;
         const uint8_t* act = a.act + static_cast<int64_t>(cgl) * a.act_cg_stride;
+        const uint8_t* act_last = a.act + static_cast<int64_t>(a.ncg - 1) * a.act_cg_stride;
         int cg = cgl, nbv = a.nblk_row - cgl * 8;
         for (int ks = 0; ks < a.nks; ++ks, cg += kStageCG, nbv -= kStageCG * 8, act += kStageCG * a.act_cg_stride) {
             if (!aborted && !wait_or_abort(&full[s], phase, abort_flag)) {
@@ -726,17 +756,19 @@ __device__ __forceinline__ void consume(const GemvArgs& a, uint8_t* stages, floa
                     atomicExch(a.err, 1);
                 }
             }
-            {
+#pragma unroll 1
+            for (int c = 0; c < NCG; ++c) {
                 // Every lane decodes (no divergent branch around the decode):
                 // a lane whose row is past the end or whose CG is past the row
                 // reads stale stage bytes and the last CG's activations, and
                 // its sums are dropped (valid = false).
-                const bool valid = ok0 && cg < a.ncg && !aborted;
-                const int sb = s * a.stage_bytes;
+                const int cgc = cg + c * kSlotStep;
+                const bool valid = ok0 && cgc < a.ncg && !aborted;
+                const int sb = s * a.stage_bytes + c * kSlotStep * L::CGB;
                 const uint8_t* c0 = stage_lane0 + sb;
                 const uint8_t* c1 = stage_lane1 + sb;
-                const uint8_t* xa = cg < a.ncg ? act : a.act + static_cast<int64_t>(a.ncg - 1) * a.act_cg_stride;
-                L::template half<H, AL, NT>(c0, c1, nbv, ActCG{xa}, a.ntok, valid, acc);
+                const uint8_t* xa = cgc < a.ncg ? act + static_cast<int64_t>(c * kSlotStep) * a.act_cg_stride : act_last;
+                L::template half<H, AL, NT, NR>(c0, c1, nbv - c * kSlotStep * 8, ActCG{xa}, a.ntok, valid, acc);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
@@ -745,16 +777,16 @@ __device__ __forceinline__ void consume(const GemvArgs& a, uint8_t* stages, floa
                 phase ^= 1;
             }
         }
-        // combine the four CG slots of each warp, then the warps
+        // combine the CG slots of each warp, then the warps
         float* rp = red + unit_par * (kConsumerWarps * kUnitRows * NT);
 #pragma unroll
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < NR; ++i) {
 #pragma unroll
             for (int t = 0; t < NT; ++t) {
                 float v = acc[i][t];
-                v += __shfl_xor_sync(0xffffffffu, v, 8);
+                if constexpr (NR == 2) v += __shfl_xor_sync(0xffffffffu, v, 8);
                 v += __shfl_xor_sync(0xffffffffu, v, 16);
-                if (lane < 8) rp[(warp * kUnitRows + pr + 8 * i) * NT + t] = v;
+                if (lane < 16 / NR) rp[(warp * kUnitRows + pr + 8 * i) * NT + t] = v;
                 acc[i][t] = 0.0f;
             }
         }
@@ -873,13 +905,13 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
     }
 
     // ---------------- consumer warps ----------------
-    // Warp w decodes half h = w/4 of the stage's CGs 4(w%4)..4(w%4)+3; lane l
-    // takes CG 4(w%4) + l/8 for rows l%8 and l%8 + 8 of the unit, so every
-    // activation run it loads serves two rows.  The half is a template
-    // argument: one warp-uniform branch here instead of one per K-step.
+    // Warp w decodes half h = w/4 of its CG slots (mapping in consume).  The
+    // half is a template argument: one warp-uniform branch here instead of
+    // one per K-step.
     pdl_wait();  // activation records of this call are complete
-    if (warp < 4) consume<F, NT, AL, 0>(a, stages, red, full, empty, abort_flag, warp, lane);
-    else consume<F, NT, AL, 1>(a, stages, red, full, empty, abort_flag, warp, lane);
+    constexpr int NR = rows_per_lane<F, NT>();
+    if (warp < 4) consume<F, NT, AL, 0, NR>(a, stages, red, full, empty, abort_flag, warp, lane);
+    else consume<F, NT, AL, 1, NR>(a, stages, red, full, empty, abort_flag, warp, lane);
 }
 
 struct GemvPlan {
