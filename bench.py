@@ -833,14 +833,30 @@ def run_case(args):
     for i in range(args.warmup):
         ax.linear_q(x, qs[i % len(qs)], out=y, workspace=ws)
     torch.cuda.synchronize()
+    graph = None
+    if args.case_graph:
+        # the timed calls as one CUDA graph, so small shards are not timed
+        # at the host's launch rate
+        stream = torch.cuda.Stream()
+        stream.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(args.steps):
+                ax.linear_q(x, qs[i % len(qs)], out=y, workspace=ws)
+        graph.replay()
+        torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for i in range(args.steps):
-        ax.linear_q(x, qs[i % len(qs)], out=y, workspace=ws)
+    if graph is not None:
+        graph.replay()
+    else:
+        for i in range(args.steps):
+            ax.linear_q(x, qs[i % len(qs)], out=y, workspace=ws)
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / max(1, args.steps)
-    print(json.dumps({"case": args.case, "ms": round(ms, 5), "TOPS": round(2.0 * rows * K * M / (ms / 1e3) / 1e12, 2),
+    print(json.dumps({"case": args.case, "graph": bool(graph), "ms": round(ms, 5),
+                      "TOPS": round(2.0 * rows * K * M / (ms / 1e3) / 1e12, 2),
                       "weight_GBps": round(nbytes / (ms / 1e3) / 1e9, 1)}), flush=True)
     return 0
 
@@ -990,6 +1006,7 @@ def main():
     ap.add_argument("--no-extras", action="store_true", help="skip the GEMM and pack records")
     ap.add_argument("--suite", action="store_true", help="time every configuration (one JSON line each)")
     ap.add_argument("--case", default=None, help="time one matmul, FMT:ROWS:K:TOKENS (or PACK:FMT:ROWS:COLS)")
+    ap.add_argument("--case-graph", action="store_true", help="--case: time the calls as one replayed CUDA graph")
     ap.add_argument("--axon", action="store_true", help="time loading the packed weights from an .axon file")
     args = ap.parse_args()
     if args.axon:
