@@ -56,14 +56,16 @@ __device__ __forceinline__ void st_u16(uint8_t* p, uint32_t v) {
 // starting from the first element, `if (v < lo) lo = v; if (v > hi) hi = v;`.
 // Equals min/max over the non-NaN elements unless the first element is NaN,
 // in which case both stay NaN.  `width` lanes (2 or 4) share a sub-block.
-template <int WIDTH>
+// FULL: every element of the block is present (no per-element count test).
+// A NaN element is skipped by the comparisons themselves, as in the fold.
+template <int WIDTH, bool FULL>
 __device__ __forceinline__ void subblock_minmax(const float* x, int e0, int count, int lane, float& lo, float& hi) {
     lo = __int_as_float(0x7f800000);
     hi = -lo;
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
         float v = x[u];
-        if (e0 + u < count && !isnan(v)) {
+        if (FULL || e0 + u < count) {
             lo = ref_min(lo, v);
             hi = ref_max(hi, v);
         }
@@ -73,19 +75,19 @@ __device__ __forceinline__ void subblock_minmax(const float* x, int e0, int coun
         lo = ref_min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
         hi = ref_max(hi, __shfl_xor_sync(0xffffffffu, hi, o));
     }
-    int first_nan = __shfl_sync(0xffffffffu, (e0 < count && isnan(x[0])) ? 1 : 0, lane & ~(WIDTH - 1));
+    int first_nan = __shfl_sync(0xffffffffu, ((FULL || e0 < count) && isnan(x[0])) ? 1 : 0, lane & ~(WIDTH - 1));
     if (first_nan) {
         lo = __int_as_float(0x7fc00000);
         hi = lo;
     }
 }
 
-template <int WIDTH>
+template <int WIDTH, bool FULL>
 __device__ __forceinline__ float subblock_amax(const float* x, int e0, int count) {
     float a = 0.0f;
 #pragma unroll
     for (int u = 0; u < 8; ++u)
-        if (e0 + u < count) a = ref_max(a, fabsf(x[u]));
+        if (FULL || e0 + u < count) a = ref_max(a, fabsf(x[u]));
 #pragma unroll
     for (int o = 1; o < WIDTH; o <<= 1) a = ref_max(a, __shfl_xor_sync(0xffffffffu, a, o));
     return a;
@@ -97,14 +99,15 @@ template <int F> struct Pack;
 
 // quantize_block_q8_0, cpu_backend.cpp:739-752.  4 lanes per block.
 template <> struct Pack<F_Q8_0> {
+    template <bool FULL>
     __device__ static void run(const float* x, int e0, int count, int lane, uint8_t* ob, WarpScratch&) {
-        float amax = subblock_amax<4>(x, e0, count);
+        float amax = subblock_amax<4, FULL>(x, e0, count);
         float d = (amax == 0.0f) ? 1.0f : __fdiv_rn(amax, 127.0f);
         if ((lane & 3) == 0) st_u16(ob, f2h_ref(d));
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
             int q = 0;
-            if (e0 + u < count) {
+            if (FULL || e0 + u < count) {
                 float r = roundf(__fdiv_rn(x[u], d));
                 q = static_cast<int8_t>(cvt_x86(ref_max(-127.0f, ref_min(127.0f, r))));
             }
@@ -115,15 +118,16 @@ template <> struct Pack<F_Q8_0> {
 
 // quantize_block_q4_0, cpu_backend.cpp:754-773.  4 lanes per block.
 template <> struct Pack<F_Q4_0> {
+    template <bool FULL>
     __device__ static void run(const float* x, int e0, int count, int lane, uint8_t* ob, WarpScratch&) {
-        float amax = subblock_amax<4>(x, e0, count);
+        float amax = subblock_amax<4, FULL>(x, e0, count);
         float d = (amax == 0.0f) ? 1.0f : __fdiv_rn(amax, 8.0f);
         if ((lane & 3) == 0) st_u16(ob, f2h_ref(d));
 #pragma unroll
         for (int u = 0; u < 8; u += 2) {
             int lo = 0, hi = 0;
-            if (e0 + u < count) lo = imax(-8, imin(7, cvt_x86(roundf(__fdiv_rn(x[u], d)))));
-            if (e0 + u + 1 < count) hi = imax(-8, imin(7, cvt_x86(roundf(__fdiv_rn(x[u + 1], d)))));
+            if (FULL || e0 + u < count) lo = imax(-8, imin(7, cvt_x86(roundf(__fdiv_rn(x[u], d)))));
+            if (FULL || e0 + u + 1 < count) hi = imax(-8, imin(7, cvt_x86(roundf(__fdiv_rn(x[u + 1], d)))));
             ob[2 + (e0 + u) / 2] = static_cast<uint8_t>((lo + 8) | ((hi + 8) << 4));
         }
     }
@@ -131,12 +135,13 @@ template <> struct Pack<F_Q4_0> {
 
 // quantize_block_q2_K, cpu_backend.cpp:775-847.  Sub-block j = lane/2.
 template <> struct Pack<F_Q2_K> {
+    template <bool FULL>
     __device__ static void run(const float* x, int e0, int count, int lane, uint8_t* ob, WarpScratch& ws) {
         const int j = lane >> 1;
         float lo, hi;
-        subblock_minmax<2>(x, e0, count, lane, lo, hi);
+        subblock_minmax<2, FULL>(x, e0, count, lane, lo, hi);
         float scale = 0.0f, minv = 0.0f;
-        if (j * 16 < count) {
+        if (FULL || j * 16 < count) {
             float range = __fsub_rn(hi, lo);
             if (range < 1e-10f) range = 1.0f;
             scale = __fdiv_rn(range, 3.0f);
@@ -156,7 +161,7 @@ template <> struct Pack<F_Q2_K> {
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
             int l = 0;
-            if (e0 + u < count) l = imax(0, imin(3, cvt_x86(roundf(__fdiv_rn(__fadd_rn(x[u], mv), dv)))));
+            if (FULL || e0 + u < count) l = imax(0, imin(3, cvt_x86(roundf(__fdiv_rn(__fadd_rn(x[u], mv), dv)))));
             ws.codes[e0 + u] = static_cast<uint8_t>(l);
         }
         __syncwarp();
@@ -177,9 +182,10 @@ template <> struct Pack<F_Q2_K> {
 
 // quantize_block_q3_K, cpu_backend.cpp:849-932.  Sub-block j = lane/2.
 template <> struct Pack<F_Q3_K> {
+    template <bool FULL>
     __device__ static void run(const float* x, int e0, int count, int lane, uint8_t* ob, WarpScratch& ws) {
         const int j = lane >> 1;
-        float amax = subblock_amax<2>(x, e0, count);
+        float amax = subblock_amax<2, FULL>(x, e0, count);
         float sub = (amax < 1e-10f) ? 0.0f : __fdiv_rn(amax, 4.0f);
         float max_abs = warp_posmax(fabsf(sub));
         int l6 = 0;
@@ -198,7 +204,7 @@ template <> struct Pack<F_Q3_K> {
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
             int l = 0;
-            if (e0 + u < count) l = imax(-4, imin(3, cvt_x86(roundf(__fdiv_rn(x[u], d_sub)))));
+            if (FULL || e0 + u < count) l = imax(-4, imin(3, cvt_x86(roundf(__fdiv_rn(x[u], d_sub)))));
             ws.codes[e0 + u] = static_cast<uint8_t>(static_cast<int8_t>(l));
         }
         __syncwarp();
@@ -206,7 +212,7 @@ template <> struct Pack<F_Q3_K> {
         uint32_t hm = 0;
 #pragma unroll
         for (int t = 0; t < 8; ++t)
-            if (32 * t + lane < count && static_cast<int8_t>(ws.codes[32 * t + lane]) + 4 > 3) hm |= 1u << t;
+            if ((FULL || 32 * t + lane < count) && static_cast<int8_t>(ws.codes[32 * t + lane]) + 4 > 3) hm |= 1u << t;
         ob[lane] = static_cast<uint8_t>(hm);
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -232,14 +238,14 @@ template <> struct Pack<F_Q3_K> {
 // Q4_K / Q5_K shared part (cpu_backend.cpp:934-1009 / 1011-1090): group g of
 // 32 = lanes 4g..4g+3.  Produces the block header (d, dmin, 12 scale bytes)
 // and the element codes in ws.codes.
-template <int LEVELS, int MAXQ>
+template <int LEVELS, int MAXQ, bool FULL>
 __device__ __forceinline__ void pack_k45_common(const float* x, int e0, int count, int lane, uint8_t* ob,
                                                 WarpScratch& ws) {
     const int g = lane >> 2;
     float lo, hi;
-    subblock_minmax<4>(x, e0, count, lane, lo, hi);
+    subblock_minmax<4, FULL>(x, e0, count, lane, lo, hi);
     float scale = 0.0f, minv = 0.0f;
-    if (g * 32 < count) {
+    if (FULL || g * 32 < count) {
         float range = __fsub_rn(hi, lo);
         if (range < 1e-10f) range = 1.0f;
         scale = __fdiv_rn(range, static_cast<float>(LEVELS));
@@ -264,7 +270,7 @@ __device__ __forceinline__ void pack_k45_common(const float* x, int e0, int coun
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
         int l = 0;
-        if (e0 + u < count) l = imax(0, imin(MAXQ, cvt_x86(roundf(__fdiv_rn(__fadd_rn(x[u], m_eff), d_eff)))));
+        if (FULL || e0 + u < count) l = imax(0, imin(MAXQ, cvt_x86(roundf(__fdiv_rn(__fadd_rn(x[u], m_eff), d_eff)))));
         ws.codes[e0 + u] = static_cast<uint8_t>(l);
     }
     __syncwarp();
@@ -282,8 +288,9 @@ __device__ __forceinline__ void pack_k45_common(const float* x, int e0, int coun
 }
 
 template <> struct Pack<F_Q4_K> {
+    template <bool FULL>
     __device__ static void run(const float* x, int e0, int count, int lane, uint8_t* ob, WarpScratch& ws) {
-        pack_k45_common<15, 15>(x, e0, count, lane, ob, ws);
+        pack_k45_common<15, 15, FULL>(x, e0, count, lane, ob, ws);
 #pragma unroll
         for (int c = 0; c < 4; ++c)
             ob[16 + 32 * c + lane] = static_cast<uint8_t>(ws.codes[64 * c + lane] | (ws.codes[64 * c + 32 + lane] << 4));
@@ -291,8 +298,9 @@ template <> struct Pack<F_Q4_K> {
 };
 
 template <> struct Pack<F_Q5_K> {
+    template <bool FULL>
     __device__ static void run(const float* x, int e0, int count, int lane, uint8_t* ob, WarpScratch& ws) {
-        pack_k45_common<31, 31>(x, e0, count, lane, ob, ws);
+        pack_k45_common<31, 31, FULL>(x, e0, count, lane, ob, ws);
         uint32_t qh = 0;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -307,9 +315,10 @@ template <> struct Pack<F_Q5_K> {
 
 // quantize_block_q6_K, cpu_backend.cpp:1092-1156.  Sub-block j = lane/2.
 template <> struct Pack<F_Q6_K> {
+    template <bool FULL>
     __device__ static void run(const float* x, int e0, int count, int lane, uint8_t* ob, WarpScratch& ws) {
         const int j = lane >> 1;
-        float amax = subblock_amax<2>(x, e0, count);
+        float amax = subblock_amax<2, FULL>(x, e0, count);
         float sub = (amax < 1e-10f) ? 0.0f : __fdiv_rn(amax, 32.0f);
         float max_abs = warp_posmax(fabsf(sub));
         if (max_abs < 1e-10f) {  // all-zero block, d = fp16(0)
@@ -324,7 +333,7 @@ template <> struct Pack<F_Q6_K> {
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
             int l = 0;
-            if (e0 + u < count) l = imax(-32, imin(31, cvt_x86(roundf(__fdiv_rn(x[u], d_sub)))));
+            if (FULL || e0 + u < count) l = imax(-32, imin(31, cvt_x86(roundf(__fdiv_rn(x[u], d_sub)))));
             ws.codes[e0 + u] = static_cast<uint8_t>(static_cast<int8_t>(l));
         }
         __syncwarp();
@@ -385,7 +394,13 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const float* __restr
         // K-quants; for 32-element formats the lanes of such blocks write
         // bytes that are never stored).
         const bool warp_live = (Traits<F>::BE == 32) ? (b0 + warp * 8 < total_blocks) : (gb < total_blocks);
-        if (warp_live) Pack<F>::run(x, e0, count, lane, obuf + bic * C::BB, ws[warp]);
+        // every block of the warp is complete (the common case): the packers
+        // skip their per-element count tests
+        const bool full = __all_sync(0xffffffffu, count == C::BE) != 0;
+        if (warp_live) {
+            if (full) Pack<F>::template run<true>(x, e0, count, lane, obuf + bic * C::BB, ws[warp]);
+            else Pack<F>::template run<false>(x, e0, count, lane, obuf + bic * C::BB, ws[warp]);
+        }
         __syncthreads();
         const int nbytes = static_cast<int>(min64(C::kBlocksPerCta, total_blocks - b0)) * C::BB;
         uint8_t* out = dst + b0 * C::BB;
