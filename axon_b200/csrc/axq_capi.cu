@@ -156,7 +156,7 @@ int axq_dequantize(int fmt, const void* src, float* dst, int64_t rows, int64_t c
 size_t axq_matmul_workspace_size(int fmt, int64_t M, int64_t K, int64_t N) {
     int be = host_block_elems(fmt);
     if (!be || K < 0 || N < 0 || M < 0) return 0;
-    if (N > kGemvMaxN) return kStatusBytes + gemm_workspace_bytes(fmt, M, K, N);
+    if (N > gemv_max_n(fmt)) return kStatusBytes + gemm_workspace_bytes(fmt, M, K, N);
     const int64_t Kp = (K + be - 1) / be * be;
     return kStatusBytes + gemv_workspace_bytes(Kp, N);
 }
@@ -191,7 +191,7 @@ int axq_matmul(int fmt, const void* a_q, const float* b, float* out, int64_t M, 
         return fail(AXQ_ERR_INVALID, std::string(fn) + ": workspace must be 256-byte aligned");
     auto* ws = static_cast<uint8_t*>(workspace);
     int* err = reinterpret_cast<int*>(ws);  // zeroed by the first kernel of the call
-    cudaError_t e = (N > kGemvMaxN)
+    cudaError_t e = (N > gemv_max_n(fmt))
                         ? gemm_dispatch(fmt, a_q, b, out, M, K, N, static_cast<int>(flags), ws + kStatusBytes,
                                         workspace_bytes - kStatusBytes, err, s)
                         : gemv_dispatch(fmt, a_q, nullptr, b, out, M, K, N, static_cast<int>(flags), ws + kStatusBytes,
@@ -228,7 +228,7 @@ int axq_linear(int fmt, const void* w_q, const float* x, const float* bias, floa
 size_t axq_gate_up_workspace_size(int fmt, int64_t M, int64_t K, int64_t N) {
     int be = host_block_elems(fmt);
     if (!be || K < 0 || N < 0 || M < 0) return 0;
-    if (N <= kGemvMaxN) return axq_matmul_workspace_size(fmt, M, K, N);
+    if (N <= gemv_max_n(fmt)) return axq_matmul_workspace_size(fmt, M, K, N);
     const size_t tmp = (static_cast<size_t>(M) * static_cast<size_t>(N) * 4 + 255) / 256 * 256;
     return axq_matmul_workspace_size(fmt, M, K, N) + 2 * tmp;
 }
@@ -264,7 +264,7 @@ int axq_gate_up_silu(int fmt, const void* w_gate, const void* w_up, const float*
     auto* ws = static_cast<uint8_t*>(workspace);
     int* err = reinterpret_cast<int*>(ws);
     cudaError_t e;
-    if (N <= kGemvMaxN) {
+    if (N <= gemv_max_n(fmt)) {
         // one pass: every unit decodes 8 rows of W_gate and the same 8 of W_up
         e = gemv_dispatch(fmt, w_gate, w_up, x, h, M, K, N, static_cast<int>(flags), ws + kStatusBytes,
                           workspace_bytes - kStatusBytes, err, s);

@@ -694,6 +694,346 @@ __device__ __forceinline__ uintptr_t slot_base(const GemvArgs& a, int slot) {
     return reinterpret_cast<uintptr_t>((a.pair && slot >= 8) ? a.w2 : a.w);
 }
 
+// End of a unit: after every consumer warp has written its partial sums
+// of the unit's 16 stage rows to rp ([warp][row][NT]), warp 0 adds them up
+// and stores the outputs (or, for peer-store calls, every rank's copy).
+template <int NT>
+__device__ __forceinline__ void store_unit(const GemvArgs& a, const float* rp, int64_t u, int warp, int lane,
+                                           unsigned call, int64_t land_off) {
+    asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+    const int64_t orow = a.pair ? u * 8 + lane : u * kUnitRows + lane;
+    if (warp == 0 && lane < (a.pair ? 8 : 16) && orow < a.rows) {
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            if (t < a.ntok) {
+                float v = 0.0f;
+#pragma unroll
+                for (int w2 = 0; w2 < kConsumerWarps; ++w2) v += rp[(w2 * kUnitRows + lane) * NT + t];
+                if (a.pair) {  // v = gate row; combine with the same row of W_up
+                    float up = 0.0f;
+#pragma unroll
+                    for (int w2 = 0; w2 < kConsumerWarps; ++w2) up += rp[(w2 * kUnitRows + lane + 8) * NT + t];
+                    v = v / (1.0f + expf(-v)) * up;
+                }
+                if (a.npeers > 0) {
+                    const int64_t gi = land_off + (a.row_offset + orow) * a.out_ld + t;
+                    const unsigned long long slot =
+                        (static_cast<unsigned long long>(call) << 32) | __float_as_uint(v);
+                    for (int g = 0; g < a.npeers; ++g) st_relaxed_sys_u64(a.peer_land[g] + gi, slot);
+                } else if (a.out_tokmajor) {
+                    a.out[t * a.out_ld + orow] = v;
+                } else {
+                    a.out[orow * a.out_ld + t] = v;
+                }
+            }
+        }
+    }
+}
+
+// ---- Small batches (2..8 tokens) of a K-quant format on the tensor cores ----
+//
+// A warp multiplies one column group of all 16 rows of the unit with
+// mma.sync.m16n8k16 (u8 codes x s8 activations -> s32).  A fragment: 16 rows
+// x one 16-element run of codes; lane 4g + i holds rows g and g + 8,
+// elements 4i..4i+3, i.e. word i of the run's code words, decoded as the
+// one-token path decodes them.  B fragment: the run's 16 activations x 8
+// columns, column 2t the hi and 2t + 1 the lo term of token t, so one MMA
+// takes the dot products of four tokens (a second one tokens 4..7).  Each
+// run's int32 result is scaled by the run's integer sub-block scale into the
+// same HS, LS and MS sums as the one-token path (the same int32 bounds hold)
+// and converted to fp32 once per half CG.  The per-token dp4a chains this
+// replaces made the 2..4-token GEMV cost about one-token time per token.
+
+__device__ __forceinline__ void mma16816(uint32_t a0, uint32_t a1, uint32_t b, int (&d)[4]) {
+    asm("mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5}, {%6}, {%7, %7, %7, %7};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(b), "r"(0));
+}
+
+// One 32-bit word at p with static alignment AL (4: aligned; else any).
+template <int AL>
+__device__ __forceinline__ uint32_t ld1(const uint8_t* p) {
+    uint32_t w[1];
+    if constexpr (AL >= 4) w[0] = *reinterpret_cast<const uint32_t*>(p);
+    else ld_words<1>(p, w);
+    return w[0];
+}
+
+// MmaRow<F, H, AL>: half H of one row's K-quant block for lane word i:
+// load(cg, i) reads the block header, run<J>(q, sc, m) gives word i of the
+// 16-element run J (elements 128H + 16J + 4i..+3) with the run's integer
+// scale and offset weight, in the conventions of the Row decoders above.
+template <int H, int AL> struct MmaQ2K {
+    static constexpr bool LH_MAJOR = true;
+    uint32_t hd, scw[2], mw[2], w;
+    const uint8_t* p;
+    __device__ __forceinline__ void load(const uint8_t* cg, int i) {
+        uint32_t h[1], sc[2];
+        ldw<1, AL>(cg, h);
+        ldw<2, AL>(cg + 4 + 8 * H, sc);
+        hd = h[0];
+#pragma unroll
+        for (int v = 0; v < 2; ++v) {
+            scw[v] = sc[v] & 0x0F0F0F0Fu;
+            mw[v] = (sc[v] >> 4) & 0x0F0F0F0Fu;
+        }
+        p = cg + 4 * i;
+    }
+    template <int LH>
+    __device__ __forceinline__ void prep() { w = ld1<AL>(p + 20 + 32 * H + 16 * LH); }
+    template <int J>
+    __device__ __forceinline__ void run(uint32_t& q, int& sc, int& m) const {
+        constexpr int s = J >> 1;
+        q = w & (0x03030303u << (2 * s));
+        sc = static_cast<int>(__byte_perm(scw[J >> 2], 0u, 0x4440u | (J & 3))) << (6 - 2 * s);
+        m = static_cast<int>(__byte_perm(mw[J >> 2], 0u, 0x4440u | (J & 3)));
+    }
+    __device__ __forceinline__ float dscale() const { return h2f_flush(hd & 0xFFFFu) * (1.0f / 64.0f); }
+    __device__ __forceinline__ float mscale() const { return h2f_flush(hd >> 16); }
+};
+
+template <int H, int AL> struct MmaQ3K {
+    static constexpr bool LH_MAJOR = true;
+    uint32_t hd, sv[2], wa, wb;
+    const uint8_t* p;
+    __device__ __forceinline__ void load(const uint8_t* cg, int i) {
+        uint32_t h[1], s12[3];
+        ld_words<1>(cg + 108, h);
+        hd = h[0];
+        ld_words<3>(cg + 96, s12);
+        uint32_t s6[2];
+        if constexpr (H == 0) {
+            s6[0] = (s12[0] & 0x0F0F0F0Fu) | ((s12[2] << 4) & 0x30303030u);
+            s6[1] = (s12[1] & 0x0F0F0F0Fu) | ((s12[2] << 2) & 0x30303030u);
+        } else {
+            s6[0] = ((s12[0] >> 4) & 0x0F0F0F0Fu) | (s12[2] & 0x30303030u);
+            s6[1] = ((s12[1] >> 4) & 0x0F0F0F0Fu) | ((s12[2] >> 2) & 0x30303030u);
+        }
+#pragma unroll
+        for (int v = 0; v < 2; ++v) sv[v] = (s6[v] ^ 0x20202020u) << 2;
+        p = cg + 4 * i;
+    }
+    template <int LH>
+    __device__ __forceinline__ void prep() {
+        const uint32_t hm = ld1<1>(p + 16 * LH);
+        const uint32_t w = ld1<1>(p + 32 + 32 * H + 16 * LH);
+        wa = bsel(0x33333333u, w, bsel(0x0F0F0F0Fu, shl<2 - 4 * H>(hm), shl<4 - 4 * H>(hm)));
+        wb = bsel(0x33333333u, w >> 2, bsel(0x0F0F0F0Fu, shl<1 - 4 * H>(hm), shl<3 - 4 * H>(hm)));
+    }
+    template <int J>
+    __device__ __forceinline__ void run(uint32_t& q, int& sc, int& m) const {
+        constexpr int s = J >> 1;
+        constexpr uint32_t MASK = (s >= 2) ? 0x70707070u : 0x07070707u;
+        q = ((s & 1) ? wb : wa) & MASK;
+        m = sext_byte<J & 3>(sv[J >> 2]);
+        sc = (s < 2) ? (m << 4) : m;
+    }
+    __device__ __forceinline__ float dscale() const { return h2f_flush(hd & 0xFFFFu) * (1.0f / 64.0f); }
+    __device__ __forceinline__ float mscale() const { return h2f_flush(hd & 0xFFFFu); }
+};
+
+// Q4_K / Q5_K: 16-element run J = 2(G - 4H) + sub is half `sub` of group G.
+template <int H, int AL> struct MmaQ4K {
+    static constexpr bool LH_MAJOR = false;
+    uint32_t hw[4];
+    const uint8_t* p;
+    __device__ __forceinline__ void load(const uint8_t* cg, int i) {
+        ldw<4, AL>(cg, hw);
+        p = cg + 4 * i;
+    }
+    template <int J>
+    __device__ __forceinline__ void run(uint32_t& q, int& sc, int& m) const {
+        constexpr int G = 4 * H + (J >> 1), sub = J & 1;
+        const uint32_t w = ld1<AL>(p + 16 + 32 * (G >> 1) + 16 * sub);
+        q = w & ((G & 1) ? 0xF0F0F0F0u : 0x0F0F0F0Fu);
+        int s6;
+        k4sm<G>(hw, s6, m);
+        sc = (G & 1) ? s6 : (s6 << 4);
+    }
+    __device__ __forceinline__ float dscale() const { return h2f_flush(hw[0] & 0xFFFFu) * 0.0625f; }
+    __device__ __forceinline__ float mscale() const { return h2f_flush(hw[0] >> 16); }
+};
+
+template <int H, int AL> struct MmaQ5K {
+    static constexpr bool LH_MAJOR = false;
+    uint32_t hw[4];
+    const uint8_t* p;
+    __device__ __forceinline__ void load(const uint8_t* cg, int i) {
+        ldw<4, AL>(cg, hw);
+        p = cg + 4 * i;
+    }
+    template <int J>
+    __device__ __forceinline__ void run(uint32_t& q, int& sc, int& m) const {
+        constexpr int G = 4 * H + (J >> 1), sub = J & 1;
+        const uint32_t qh = ld1<AL>(p + 16 + 16 * sub);
+        const uint32_t w = ld1<AL>(p + 48 + 32 * (G >> 1) + 16 * sub);
+        const uint32_t nib = (G & 1) ? (w >> 4) : w;
+        q = (nib & 0x0F0F0F0Fu) | (shl<4 - G>(qh) & 0x10101010u);
+        k4sm<G>(hw, sc, m);
+    }
+    __device__ __forceinline__ float dscale() const { return h2f_flush(hw[0] & 0xFFFFu); }
+    __device__ __forceinline__ float mscale() const { return h2f_flush(hw[0] >> 16); }
+};
+
+template <int H, int AL> struct MmaQ6K {
+    static constexpr bool LH_MAJOR = false;
+    uint32_t hd, sc2[2];
+    const uint8_t* p;
+    __device__ __forceinline__ void load(const uint8_t* cg, int i) {
+        uint32_t h[1];
+        ld_words<1>(cg + 208, h);
+        hd = h[0];
+        ld_words<2>(cg + 192 + 8 * H, sc2);
+        p = cg + 4 * i;
+    }
+    template <int J>
+    __device__ __forceinline__ void run(uint32_t& q, int& sc, int& m) const {
+        constexpr int T = J >> 1, lh = J & 1;
+        const uint32_t src = ld1<1>(p + 64 * H + 32 * (T & 1) + 16 * lh);
+        const uint32_t hb = ld1<1>(p + 128 + 32 * H + 16 * lh);
+        const uint32_t nib = (T & 2) ? (src >> 4) : src;
+        q = (nib & 0x0F0F0F0Fu) | (shl<4 - 2 * T>(hb) & 0x30303030u);
+        sc = m = static_cast<int>(static_cast<int8_t>(bt<J>(sc2)));
+    }
+    __device__ __forceinline__ float dscale() const { return h2f_flush(hd & 0xFFFFu); }
+    __device__ __forceinline__ float mscale() const { return h2f_flush(hd & 0xFFFFu) * 32.0f; }
+};
+
+template <int F, int H, int AL> struct MmaRowOf;
+template <int H, int AL> struct MmaRowOf<F_Q2_K, H, AL> { using T = MmaQ2K<H, AL>; };
+template <int H, int AL> struct MmaRowOf<F_Q3_K, H, AL> { using T = MmaQ3K<H, AL>; };
+template <int H, int AL> struct MmaRowOf<F_Q4_K, H, AL> { using T = MmaQ4K<H, AL>; };
+template <int H, int AL> struct MmaRowOf<F_Q5_K, H, AL> { using T = MmaQ5K<H, AL>; };
+template <int H, int AL> struct MmaRowOf<F_Q6_K, H, AL> { using T = MmaQ6K<H, AL>; };
+
+// Half H of one CG for rows g (c0) and g + 8 (c1) of the unit and NG groups
+// of four tokens.  X: records of this CG; bofs[grp] = offset of this lane's
+// B-fragment bytes (token (g >> 1) + 4grp, term g & 1, elements 4i..);
+// tofs[grp] = record of token i + 4grp (the lane's D columns).
+template <int F, int H, int AL, int NG>
+__device__ __forceinline__ void mma_half(const uint8_t* c0, const uint8_t* c1, const uint8_t* X, const int* bofs,
+                                         const int* tofs, int i, float (*acc)[NG]) {
+    using R = typename MmaRowOf<F, H, AL>::T;
+    constexpr bool LHM = R::LH_MAJOR;
+    R r0, r1;
+    r0.load(c0, i);
+    r1.load(c1, i);
+    int hs[2][NG], ls[2][NG], ms[2][NG];
+#pragma unroll
+    for (int grp = 0; grp < NG; ++grp) hs[0][grp] = hs[1][grp] = ls[0][grp] = ls[1][grp] = ms[0][grp] = ms[1][grp] = 0;
+    static_for<8>([&](auto Kc) {
+        constexpr int K = decltype(Kc)::value;
+        constexpr int J = LHM ? 2 * (K & 3) + (K >> 2) : K;
+        constexpr int jj = 8 * H + J;  // 16-element run of the CG
+        if constexpr (LHM) {
+            if constexpr ((K & 3) == 0) {
+                r0.template prep<(K >> 2)>();
+                r1.template prep<(K >> 2)>();
+            }
+        }
+        uint32_t q0, q1;
+        int sc0, m0, sc1, m1;
+        r0.template run<J>(q0, sc0, m0);
+        r1.template run<J>(q1, sc1, m1);
+#pragma unroll
+        for (int grp = 0; grp < NG; ++grp) {
+            const uint32_t b = __ldg(reinterpret_cast<const uint32_t*>(X + bofs[grp] + 16 * jj));
+            const int sx = __ldg(reinterpret_cast<const int*>(X + tofs[grp] + 512) + jj);
+            int d[4];
+            mma16816(q0, q1, b, d);
+            hs[0][grp] += sc0 * d[0];
+            ls[0][grp] += sc0 * d[1];
+            ms[0][grp] += m0 * sx;
+            hs[1][grp] += sc1 * d[2];
+            ls[1][grp] += sc1 * d[3];
+            ms[1][grp] += m1 * sx;
+        }
+    });
+    const float d0 = r0.dscale(), n0 = r0.mscale(), d1 = r1.dscale(), n1 = r1.mscale();
+#pragma unroll
+    for (int grp = 0; grp < NG; ++grp) {
+        const float u = __ldg(reinterpret_cast<const float*>(X + tofs[grp] + 576));
+        const float dot0 = fmaf(254.0f, static_cast<float>(hs[0][grp]), static_cast<float>(ls[0][grp]));
+        const float dot1 = fmaf(254.0f, static_cast<float>(hs[1][grp]), static_cast<float>(ls[1][grp]));
+        acc[0][grp] = fmaf(u, fmaf(d0, dot0, -n0 * static_cast<float>(ms[0][grp])), acc[0][grp]);
+        acc[1][grp] = fmaf(u, fmaf(d1, dot1, -n1 * static_cast<float>(ms[1][grp])), acc[1][grp]);
+    }
+}
+
+// Consumer warps of the small-batch path: warp w takes CG slots 2w and
+// 2w + 1 of each stage, all 16 rows; lane 4g + i accumulates rows g and
+// g + 8 for tokens i + 4grp.  A CG past the row's end is skipped (one branch
+// per warp: the whole warp shares the CG).
+template <int F, int NG, int AL>
+__device__ __forceinline__ void consume_mma(const GemvArgs& a, uint8_t* stages, float* red, uint64_t* full,
+                                            uint64_t* empty, volatile int* abort_flag, int warp, int lane) {
+    using L = Lane<F>;
+    constexpr int NT = 4 * NG;
+    const int g = lane >> 2, i = lane & 3;
+    int bofs[NG], tofs[NG];
+#pragma unroll
+    for (int grp = 0; grp < NG; ++grp) {
+        // token slots past ntok read the last token's records; never written
+        const int tb = min((g >> 1) + 4 * grp, a.ntok - 1), td = min(i + 4 * grp, a.ntok - 1);
+        bofs[grp] = kActRec * tb + 256 * (g & 1) + 4 * i;
+        tofs[grp] = kActRec * td;
+    }
+    float acc[2][NG];
+#pragma unroll
+    for (int grp = 0; grp < NG; ++grp) acc[0][grp] = acc[1][grp] = 0.0f;
+    int s = 0, unit_par = 0;
+    uint32_t phase = 0;
+    const unsigned call = a.npeers > 0 ? *a.epoch + 1u : 0u;
+    const int64_t land_off = static_cast<int64_t>(call & 1u) * a.land_stride;
+    bool aborted = false;
+    const uintptr_t base0 = slot_base(a, g), base1 = slot_base(a, g + 8);
+    for (int64_t u = blockIdx.x; u < a.units; u += gridDim.x, unit_par ^= 1) {
+        const int64_t row0 = slot_row(a, u, g), row1 = slot_row(a, u, g + 8);
+        // each row's 16-byte phase in the stage is fixed per unit (see consume)
+        const int mis0 = static_cast<int>((base0 + static_cast<uintptr_t>(row0 * a.rb)) & 15);
+        const int mis1 = static_cast<int>((base1 + static_cast<uintptr_t>(row1 * a.rb)) & 15);
+        // rows past the end decode stale stage bytes; their sums are never written
+        const uint8_t* srow0 = stages + g * a.rs + (row0 < a.rows ? mis0 : 0);
+        const uint8_t* srow1 = stages + (g + 8) * a.rs + (row1 < a.rows ? mis1 : 0);
+        for (int ks = 0; ks < a.nks; ++ks) {
+            if (!aborted && !wait_or_abort(&full[s], phase, abort_flag)) {
+                aborted = true;
+                if (lane == 0) {
+                    *abort_flag = 1;
+                    atomicExch(a.err, 1);
+                }
+            }
+            // the MMAs need the whole warp: a wait that ran out on any lane
+            // stops the warp's decoding
+            aborted = __any_sync(0xffffffffu, aborted) != 0;
+#pragma unroll 1
+            for (int c = 0; c < 2; ++c) {
+                const int slot = 2 * warp + c, cg = ks * kStageCG + slot;
+                if (cg < a.ncg && !aborted) {
+                    const int off = s * a.stage_bytes + slot * L::CGB;
+                    const uint8_t* X = a.act + static_cast<int64_t>(cg) * a.act_cg_stride;
+                    mma_half<F, 0, AL, NG>(srow0 + off, srow1 + off, X, bofs, tofs, i, acc);
+                    mma_half<F, 1, AL, NG>(srow0 + off, srow1 + off, X, bofs, tofs, i, acc);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+            if (++s == a.nstages) {
+                s = 0;
+                phase ^= 1;
+            }
+        }
+        float* rp = red + unit_par * (kConsumerWarps * kUnitRows * NT);
+#pragma unroll
+        for (int grp = 0; grp < NG; ++grp) {
+            rp[(warp * kUnitRows + g) * NT + i + 4 * grp] = acc[0][grp];
+            rp[(warp * kUnitRows + g + 8) * NT + i + 4 * grp] = acc[1][grp];
+            acc[0][grp] = acc[1][grp] = 0.0f;
+        }
+        store_unit<NT>(a, rp, u, warp, lane, call, land_off);
+    }
+}
+
 // Rows decoded per lane: two (each activation run a lane loads serves two
 // rows) or one, which keeps the multi-token decode's activation runs and
 // per-token sums inside the register budget where two rows spilled.  The
@@ -790,38 +1130,11 @@ __device__ __forceinline__ void consume(const GemvArgs& a, uint8_t* stages, floa
                 acc[i][t] = 0.0f;
             }
         }
-        asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
-        const int64_t orow = a.pair ? u * 8 + lane : u * kUnitRows + lane;
-        if (warp == 0 && lane < (a.pair ? 8 : 16) && orow < a.rows) {
-#pragma unroll
-            for (int t = 0; t < NT; ++t) {
-                if (t < a.ntok) {
-                    float v = 0.0f;
-#pragma unroll
-                    for (int w2 = 0; w2 < kConsumerWarps; ++w2) v += rp[(w2 * kUnitRows + lane) * NT + t];
-                    if (a.pair) {  // v = gate row; combine with the same row of W_up
-                        float up = 0.0f;
-#pragma unroll
-                        for (int w2 = 0; w2 < kConsumerWarps; ++w2) up += rp[(w2 * kUnitRows + lane + 8) * NT + t];
-                        v = v / (1.0f + expf(-v)) * up;
-                    }
-                    if (a.npeers > 0) {
-                        const int64_t gi = land_off + (a.row_offset + orow) * a.out_ld + t;
-                        const unsigned long long slot =
-                            (static_cast<unsigned long long>(call) << 32) | __float_as_uint(v);
-                        for (int g = 0; g < a.npeers; ++g) st_relaxed_sys_u64(a.peer_land[g] + gi, slot);
-                    } else if (a.out_tokmajor) {
-                        a.out[t * a.out_ld + orow] = v;
-                    } else {
-                        a.out[orow * a.out_ld + t] = v;
-                    }
-                }
-            }
-        }
+        store_unit<NT>(a, rp, u, warp, lane, call, land_off);
     }
 }
 
-template <int F, int NT, int AL>
+template <int F, int NT, int AL, bool MMA>
 __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
     using L = Lane<F>;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -909,9 +1222,13 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
     // half is a template argument: one warp-uniform branch here instead of
     // one per K-step.
     pdl_wait();  // activation records of this call are complete
-    constexpr int NR = rows_per_lane<F, NT>();
-    if (warp < 4) consume<F, NT, AL, 0, NR>(a, stages, red, full, empty, abort_flag, warp, lane);
-    else consume<F, NT, AL, 1, NR>(a, stages, red, full, empty, abort_flag, warp, lane);
+    if constexpr (MMA) {
+        consume_mma<F, NT / 4, AL>(a, stages, red, full, empty, abort_flag, warp, lane);
+    } else {
+        constexpr int NR = rows_per_lane<F, NT>();
+        if (warp < 4) consume<F, NT, AL, 0, NR>(a, stages, red, full, empty, abort_flag, warp, lane);
+        else consume<F, NT, AL, 1, NR>(a, stages, red, full, empty, abort_flag, warp, lane);
+    }
 }
 
 struct GemvPlan {
@@ -941,21 +1258,28 @@ GemvPlan plan_gemv(int nt) {
     return p;
 }
 
-template <int F, int NT, int AL>
+template <int F, int NT, int AL, bool MMA>
 cudaError_t launch_nt(const GemvPlan& p, const GemvArgs& a, cudaStream_t s) {
-    auto kern = gemv_kernel<F, NT, AL>;
+    auto kern = gemv_kernel<F, NT, AL, MMA>;
     static std::atomic<int> configured[64];
     if (cudaError_t e = ensure_dyn_smem(kern, p.smem, configured); e != cudaSuccess) return e;
     cudaError_t e = launch_pdl(kern, dim3(p.grid), dim3(kThreads), p.smem, s, a);
     return e != cudaSuccess ? e : cudaGetLastError();
 }
 
+// Formats with the small-batch MMA path (the K-quants).
+template <int F>
+constexpr bool kHasMma = (F != F_Q8_0 && F != F_Q4_0);
+
 template <int F, int AL>
-cudaError_t launch_al(const GemvPlan& p, const GemvArgs& a, int nt, cudaStream_t s) {
+cudaError_t launch_al(const GemvPlan& p, const GemvArgs& a, int nt, bool mma, cudaStream_t s) {
+    if constexpr (kHasMma<F>) {
+        if (mma) return nt <= 4 ? launch_nt<F, 4, AL, true>(p, a, s) : launch_nt<F, 8, AL, true>(p, a, s);
+    }
     switch (nt) {
-        case 1: return launch_nt<F, 1, AL>(p, a, s);
-        case 2: return launch_nt<F, 2, AL>(p, a, s);
-        default: return launch_nt<F, 4, AL>(p, a, s);
+        case 1: return launch_nt<F, 1, AL, false>(p, a, s);
+        case 2: return launch_nt<F, 2, AL, false>(p, a, s);
+        default: return launch_nt<F, 4, AL, false>(p, a, s);
     }
 }
 
@@ -1005,9 +1329,16 @@ cudaError_t launch_gemv(const void* w, const void* w2, const float* x, float* ou
     const bool aligned = (reinterpret_cast<uintptr_t>(w) % 16 == 0) && (a.rb % 16 == 0) &&
                          (reinterpret_cast<uintptr_t>(w2) % 16 == 0);
     const int sms = device_sm_count();
-    for (int64_t t0 = 0; t0 < N; t0 += kGemvMaxN) {
-        const int nt_run = static_cast<int>(std::min<int64_t>(kGemvMaxN, N - t0));
-        const int nt = nt_run == 1 ? 1 : nt_run == 2 ? 2 : 4;
+    // one token: the dp4a kernel; 2..8 tokens of a K-quant format: the MMA
+    // kernel (4 or 8 token slots), except two tokens of Q2_K and Q4_K, where
+    // the dp4a kernel measured faster (32 vs 37 and 34 vs 38 us at
+    // W[28672 x 8192]; three or four tokens: the MMA kernel 2.1-2.7x
+    // faster); Q8_0 / Q4_0: the dp4a kernel, 4 tokens at a time
+    const bool mma = kHasMma<F> && N >= 2 && !(N == 2 && (F == F_Q2_K || F == F_Q4_K));
+    const int64_t per_launch = mma ? kGemvMmaMaxN : kGemvMaxN;
+    for (int64_t t0 = 0; t0 < N; t0 += per_launch) {
+        const int nt_run = static_cast<int>(std::min<int64_t>(per_launch, N - t0));
+        const int nt = mma ? (nt_run <= 4 ? 4 : 8) : (nt_run == 1 ? 1 : nt_run == 2 ? 2 : 4);
         GemvPlan p = plan_gemv<F>(nt);
         p.grid = static_cast<int>(std::min<int64_t>(a.units, static_cast<int64_t>(sms) * p.ctas_per_sm));
         a.rs = p.rs;
@@ -1016,7 +1347,7 @@ cudaError_t launch_gemv(const void* w, const void* w2, const float* x, float* ou
         a.act = rec + t0 * kActRec;
         a.ntok = nt_run;
         a.out = a.out_tokmajor ? out + t0 * M : out + t0;
-        cudaError_t e = (aligned && L::A > 1) ? launch_al<F, L::A>(p, a, nt, s) : launch_al<F, 1>(p, a, nt, s);
+        cudaError_t e = (aligned && L::A > 1) ? launch_al<F, L::A>(p, a, nt, mma, s) : launch_al<F, 1>(p, a, nt, mma, s);
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;

@@ -278,8 +278,9 @@ def gate_up_silu(x: torch.Tensor, w_gate: QTensor, w_up: QTensor, out: Optional[
     """Fused front half of a gated MLP: h[N, M] = silu(x . W_gate^T) * (x . W_up^T),
     silu(v) = v / (1 + e^-v).  The reference has neither SiLU nor a quantized
     Linear (its Linear, src/nn/linear.cpp:19-27, is fp32); this composes its
-    quantized matmul.  Up to 4 rows of x run as a single GEMV pass over both
-    packed matrices (one activation prep, SiLU and product in the epilogue)."""
+    quantized matmul.  Up to 8 rows of x (4 for Q8_0 / Q4_0) run as a single
+    GEMV pass over both packed matrices (one activation prep, SiLU and product
+    in the epilogue)."""
     if w_gate.fmt != w_up.fmt or tuple(w_gate.shape) != tuple(w_up.shape):
         raise AxqError(Status.ERR_INVALID, "gate_up_silu: W_gate and W_up must have the same shape and format")
     M, K = w_gate.shape

@@ -31,7 +31,7 @@ def test_matmul_matches_golden(cuda, fmt):
 
 
 @pytest.mark.parametrize("fmt", FORMATS)
-@pytest.mark.parametrize("N", [1, 2, 3, 8, 17])
+@pytest.mark.parametrize("N", [1, 2, 3, 4, 5, 8, 17])
 def test_matmul_matches_oracle(cuda, orc, fmt, N):
     rng = np.random.default_rng(100 + N)
     for (M, K, kind) in ((64, 4096, "w002"), (37, 1000, "randn"), (16, 11008, "randn"), (9, 300, "outlier"),
@@ -45,9 +45,10 @@ def test_matmul_matches_oracle(cuda, orc, fmt, N):
 
 
 @pytest.mark.parametrize("fmt", FORMATS)
-def test_matmul_token_major_layouts(cuda, orc, fmt):
-    rng = np.random.default_rng(9)
-    M, K, N = 48, 2048, 4
+@pytest.mark.parametrize("N", [4, 6])
+def test_matmul_token_major_layouts(cuda, orc, fmt, N):
+    rng = np.random.default_rng(9 + N)
+    M, K = 48, 2048
     q = orc.quantize(fmt, gen(rng, (M, K), "randn"))
     B = rng.standard_normal((K, N)).astype(np.float32)
     y_ref = orc.matmul(fmt, q, B, M, K)
