@@ -750,6 +750,16 @@ __device__ __forceinline__ void mma16816(uint32_t a0, uint32_t a1, uint32_t b, i
         : "r"(a0), "r"(a1), "r"(b), "r"(0));
 }
 
+// k = 32: a0/a1 rows g/g+8 at elements 4i..4i+3, a2/a3 the same rows at
+// 16 + 4i..; b0/b1 the activations at 4i.. and 16 + 4i.. (one scale per 32).
+__device__ __forceinline__ void mma16832(uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1, int (&d)[4]) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%10, %10, %10, %10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
 // One 32-bit word at p with static alignment AL (4: aligned; else any).
 template <int AL>
 __device__ __forceinline__ uint32_t ld1(const uint8_t* p) {
@@ -764,6 +774,7 @@ __device__ __forceinline__ uint32_t ld1(const uint8_t* p) {
 // 16-element run J (elements 128H + 16J + 4i..+3) with the run's integer
 // scale and offset weight, in the conventions of the Row decoders above.
 template <int H, int AL> struct MmaQ2K {
+    static constexpr int RL = 16;
     static constexpr bool LH_MAJOR = true;
     uint32_t hd, scw[2], mw[2], w;
     const uint8_t* p;
@@ -793,6 +804,7 @@ template <int H, int AL> struct MmaQ2K {
 };
 
 template <int H, int AL> struct MmaQ3K {
+    static constexpr int RL = 16;
     static constexpr bool LH_MAJOR = true;
     uint32_t hd, sv[2], wa, wb;
     const uint8_t* p;
@@ -834,6 +846,7 @@ template <int H, int AL> struct MmaQ3K {
 
 // Q4_K / Q5_K: 16-element run J = 2(G - 4H) + sub is half `sub` of group G.
 template <int H, int AL> struct MmaQ4K {
+    static constexpr int RL = 32;
     static constexpr bool LH_MAJOR = false;
     uint32_t hw[4];
     const uint8_t* p;
@@ -855,6 +868,7 @@ template <int H, int AL> struct MmaQ4K {
 };
 
 template <int H, int AL> struct MmaQ5K {
+    static constexpr int RL = 32;
     static constexpr bool LH_MAJOR = false;
     uint32_t hw[4];
     const uint8_t* p;
@@ -876,6 +890,7 @@ template <int H, int AL> struct MmaQ5K {
 };
 
 template <int H, int AL> struct MmaQ6K {
+    static constexpr int RL = 16;
     static constexpr bool LH_MAJOR = false;
     uint32_t hd, sc2[2];
     const uint8_t* p;
@@ -909,38 +924,62 @@ template <int H, int AL> struct MmaRowOf<F_Q6_K, H, AL> { using T = MmaQ6K<H, AL
 // Half H of one CG for rows g (c0) and g + 8 (c1) of the unit and NG groups
 // of four tokens.  X: records of this CG; bofs[grp] = offset of this lane's
 // B-fragment bytes (token (g >> 1) + 4grp, term g & 1, elements 4i..);
-// tofs[grp] = record of token i + 4grp (the lane's D columns).
+// tofs[grp] = record of token i + 4grp (the lane's D columns).  The half's
+// activation fragments and run sums are loaded before any decode, so their
+// latency overlaps the MMAs.  32-element runs (Q4_K, Q5_K) take one k = 32
+// MMA each; 16-element runs one k = 16 MMA.
 template <int F, int H, int AL, int NG>
 __device__ __forceinline__ void mma_half(const uint8_t* c0, const uint8_t* c1, const uint8_t* X, const int* bofs,
                                          const int* tofs, int i, float (*acc)[NG]) {
     using R = typename MmaRowOf<F, H, AL>::T;
     constexpr bool LHM = R::LH_MAJOR;
+    constexpr int NRUN = 128 / R::RL;
+    uint32_t bv[8][NG];
+    int sxv[NRUN][NG];
+    float uv[NG];
+#pragma unroll
+    for (int grp = 0; grp < NG; ++grp) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) bv[j][grp] = __ldg(reinterpret_cast<const uint32_t*>(X + bofs[grp] + 16 * (8 * H + j)));
+#pragma unroll
+        for (int j = 0; j < NRUN; ++j) {
+            const int* sp = reinterpret_cast<const int*>(X + tofs[grp] + 512) + 8 * H;
+            sxv[j][grp] = (R::RL == 32) ? __ldg(sp + 2 * j) + __ldg(sp + 2 * j + 1) : __ldg(sp + j);
+        }
+        uv[grp] = __ldg(reinterpret_cast<const float*>(X + tofs[grp] + 576));
+    }
     R r0, r1;
     r0.load(c0, i);
     r1.load(c1, i);
     int hs[2][NG], ls[2][NG], ms[2][NG];
 #pragma unroll
     for (int grp = 0; grp < NG; ++grp) hs[0][grp] = hs[1][grp] = ls[0][grp] = ls[1][grp] = ms[0][grp] = ms[1][grp] = 0;
-    static_for<8>([&](auto Kc) {
+    static_for<NRUN>([&](auto Kc) {
         constexpr int K = decltype(Kc)::value;
-        constexpr int J = LHM ? 2 * (K & 3) + (K >> 2) : K;
-        constexpr int jj = 8 * H + J;  // 16-element run of the CG
+        constexpr int J = LHM ? 2 * (K & 3) + (K >> 2) : K;  // run of the half (16 or 32 elements)
         if constexpr (LHM) {
             if constexpr ((K & 3) == 0) {
                 r0.template prep<(K >> 2)>();
                 r1.template prep<(K >> 2)>();
             }
         }
-        uint32_t q0, q1;
         int sc0, m0, sc1, m1;
-        r0.template run<J>(q0, sc0, m0);
-        r1.template run<J>(q1, sc1, m1);
+        uint32_t q0, q1, q2 = 0, q3 = 0;
+        if constexpr (R::RL == 32) {
+            r0.template run<2 * J>(q0, sc0, m0);
+            r1.template run<2 * J>(q1, sc1, m1);
+            r0.template run<2 * J + 1>(q2, sc0, m0);
+            r1.template run<2 * J + 1>(q3, sc1, m1);
+        } else {
+            r0.template run<J>(q0, sc0, m0);
+            r1.template run<J>(q1, sc1, m1);
+        }
 #pragma unroll
         for (int grp = 0; grp < NG; ++grp) {
-            const uint32_t b = __ldg(reinterpret_cast<const uint32_t*>(X + bofs[grp] + 16 * jj));
-            const int sx = __ldg(reinterpret_cast<const int*>(X + tofs[grp] + 512) + jj);
             int d[4];
-            mma16816(q0, q1, b, d);
+            if constexpr (R::RL == 32) mma16832(q0, q1, q2, q3, bv[2 * J][grp], bv[2 * J + 1][grp], d);
+            else mma16816(q0, q1, bv[J][grp], d);
+            const int sx = sxv[J][grp];
             hs[0][grp] += sc0 * d[0];
             ls[0][grp] += sc0 * d[1];
             ms[0][grp] += m0 * sx;
@@ -952,7 +991,7 @@ __device__ __forceinline__ void mma_half(const uint8_t* c0, const uint8_t* c1, c
     const float d0 = r0.dscale(), n0 = r0.mscale(), d1 = r1.dscale(), n1 = r1.mscale();
 #pragma unroll
     for (int grp = 0; grp < NG; ++grp) {
-        const float u = __ldg(reinterpret_cast<const float*>(X + tofs[grp] + 576));
+        const float u = uv[grp];
         const float dot0 = fmaf(254.0f, static_cast<float>(hs[0][grp]), static_cast<float>(ls[0][grp]));
         const float dot1 = fmaf(254.0f, static_cast<float>(hs[1][grp]), static_cast<float>(ls[1][grp]));
         acc[0][grp] = fmaf(u, fmaf(d0, dot0, -n0 * static_cast<float>(ms[0][grp])), acc[0][grp]);

@@ -110,8 +110,8 @@ cudaError_t silu_mul_dispatch(const float* g, const float* u, float* h, int64_t 
 // The dp4a GEMV takes up to 4 tokens per launch; the K-quant formats' 2..8
 // token path (int8 MMAs, four tokens per MMA) up to 8.  Per format, the
 // GEMV serves the batches where it measured faster than the GEMM at
-// W[28672 x 8192]: up to 8 tokens for Q3_K, Q4_K and Q6_K (8 tokens: 88 vs
-// 106, 76 vs 89, 119 vs 121 us), up to 4 for the others (Q2_K and Q5_K at
+// W[28672 x 8192]: up to 8 tokens for Q3_K, Q4_K and Q6_K (8 tokens: 86 vs
+// 106, 70 vs 89, 116 vs 121 us), up to 4 for the others (Q2_K and Q5_K at
 // 8 tokens: 101 vs 97 and 105 vs 102 us).
 constexpr int64_t kGemvMaxN = 4;
 constexpr int64_t kGemvMmaMaxN = 8;
