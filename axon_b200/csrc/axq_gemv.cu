@@ -255,12 +255,26 @@ template <int H, int AL> struct RowQ3K {
     static constexpr int RL = 16;
     static constexpr bool LH_MAJOR = true;  // hmask and qs words of one lh at a time
     uint32_t hd, sv[2], a[4], b[4];  // sv: 4 * (scale - 32) of the half's eight runs, one signed byte each
-    const uint8_t* p;
+    const uint32_t* base;  // the block's first aligned word at or below it
+    uint32_t sh;           // bit offset of the block in that word
+    // n words at byte offset OFF (a multiple of 4) of the block
+    template <int N, int OFF>
+    __device__ __forceinline__ void words(uint32_t* out) const {
+        uint32_t w[N + 1];
+#pragma unroll
+        for (int i = 0; i <= N; ++i) w[i] = base[OFF / 4 + i];
+#pragma unroll
+        for (int i = 0; i < N; ++i) out[i] = __funnelshift_r(w[i], w[i + 1], sh);
+    }
     __device__ __forceinline__ void load(const uint8_t* cg) {
+        // the aligned base by pointer arithmetic keeps a shared pointer shared
+        const uint32_t mis = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(cg)) & 3u;
+        base = reinterpret_cast<const uint32_t*>(cg - mis);
+        sh = mis * 8;
         uint32_t h[1], s12[3];
-        ld_words<1>(cg + 108, h);
+        words<1, 108>(h);
         hd = h[0];
-        ld_words<3>(cg + 96, s12);
+        words<3, 96>(s12);
         // scale IS = 8H + J: low 4 bits from nibble H of byte (IS & 7) of the
         // first 8 scale bytes, high 2 bits from bits 2*(IS >> 2) of byte 8 + (IS & 3)
         uint32_t s6[2];
@@ -275,21 +289,29 @@ template <int H, int AL> struct RowQ3K {
         // to the top of its byte it is 4 * (v - 32) as a signed byte
 #pragma unroll
         for (int i = 0; i < 2; ++i) sv[i] = (s6[i] ^ 0x20202020u) << 2;
-        p = cg;
     }
     // hmask[16LH ..] and qs[32H + 16LH ..] merged into the 3-bit codes of runs
     // 2s + LH: a = s = 0 (bits 0-2) and s = 2 (bits 4-6), b = s = 1 and s = 3
     template <int LH>
     __device__ __forceinline__ void prep() {
         uint32_t hm[4], w[4];
-        ld_words<4>(p + 16 * LH, hm);
-        ld_words<4>(p + 32 + 32 * H + 16 * LH, w);
+        words<4, 16 * LH>(hm);
+        words<4, 32 + 32 * H + 16 * LH>(w);
 #pragma unroll
         for (int v = 0; v < 4; ++v) {
-            // high bit of s = 0 / 2 (bits 4H, 4H+2 of each hmask byte) to bits 2 / 6
-            a[v] = bsel(0x33333333u, w[v], bsel(0x0F0F0F0Fu, shl<2 - 4 * H>(hm[v]), shl<4 - 4 * H>(hm[v])));
-            // s = 1 / 3: fields at bits 2-3 / 6-7 moved down by 2; high bits 4H+1, 4H+3
-            b[v] = bsel(0x33333333u, w[v] >> 2, bsel(0x0F0F0F0Fu, shl<1 - 4 * H>(hm[v]), shl<3 - 4 * H>(hm[v])));
+            if constexpr (H == 0) {
+                // high bits 0 / 2 to bits 2 / 6 in one multiply: x * 20 puts bit 0
+                // at bits 2 and 4 and bit 2 at bits 4 and 6; bits 4-5 (the sum of
+                // the two, never carrying into bit 6) are taken from w
+                a[v] = bsel(0x33333333u, w[v], (hm[v] & 0x05050505u) * 20u);
+                // high bits 1 / 3 to bits 2 / 6: x * 10 for bits 1 and 3
+                b[v] = bsel(0x33333333u, w[v] >> 2, (hm[v] & 0x0A0A0A0Au) * 10u);
+            } else {
+                // high bits 4 / 6 to bits 2 / 6
+                a[v] = bsel(0x33333333u, w[v], bsel(0x0F0F0F0Fu, hm[v] >> 2, hm[v]));
+                // s = 1 / 3: fields at bits 2-3 / 6-7 moved down by 2; high bits 5 / 7
+                b[v] = bsel(0x33333333u, w[v] >> 2, bsel(0x0F0F0F0Fu, hm[v] >> 3, hm[v] >> 1));
+            }
         }
     }
     template <int J>
@@ -964,7 +986,8 @@ __device__ __forceinline__ void mma_half(const uint8_t* c0, const uint8_t* c1, c
             }
         }
         int sc0, m0, sc1, m1;
-        uint32_t q0, q1, q2 = 0, q3 = 0;
+        uint32_t q0, q1;
+        [[maybe_unused]] uint32_t q2 = 0, q3 = 0;  // second half of a 32-element run
         if constexpr (R::RL == 32) {
             r0.template run<2 * J>(q0, sc0, m0);
             r1.template run<2 * J>(q1, sc1, m1);
