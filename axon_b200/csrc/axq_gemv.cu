@@ -390,20 +390,33 @@ template <int H, int AL> struct RowQ6K {
     static constexpr int RL = 16;
     static constexpr bool LH_MAJOR = false;
     uint32_t hd, sc2[2];
-    const uint8_t* p;
+    const uint32_t* base;  // the block's first aligned word at or below it
+    uint32_t sh;           // bit offset of the block in that word
+    // n words at byte offset OFF (a multiple of 4) of the block
+    template <int N, int OFF>
+    __device__ __forceinline__ void words(uint32_t* out) const {
+        uint32_t w[N + 1];
+#pragma unroll
+        for (int i = 0; i <= N; ++i) w[i] = base[OFF / 4 + i];
+#pragma unroll
+        for (int i = 0; i < N; ++i) out[i] = __funnelshift_r(w[i], w[i + 1], sh);
+    }
     __device__ __forceinline__ void load(const uint8_t* cg) {
+        // the aligned base by pointer arithmetic keeps a shared pointer shared
+        const uint32_t mis = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(cg)) & 3u;
+        base = reinterpret_cast<const uint32_t*>(cg - mis);
+        sh = mis * 8;
         uint32_t h[1];
-        ld_words<1>(cg + 208, h);
+        words<1, 208>(h);
         hd = h[0];
-        ld_words<2>(cg + 192 + 8 * H, sc2);
-        p = cg;
+        words<2, 192 + 8 * H>(sc2);
     }
     template <int J>
     __device__ __forceinline__ void run(uint32_t* q, int& sc, int& m) const {
         constexpr int T = J >> 1, lh = J & 1;
         uint32_t src[4], hb[4];
-        ld_words<4>(p + 64 * H + 32 * (T & 1) + 16 * lh, src);
-        ld_words<4>(p + 128 + 32 * H + 16 * lh, hb);
+        words<4, 64 * H + 32 * (T & 1) + 16 * lh>(src);
+        words<4, 128 + 32 * H + 16 * lh>(hb);
 #pragma unroll
         for (int v = 0; v < 4; ++v) {
             const uint32_t nib = (T & 2) ? (src[v] >> 4) : src[v];
