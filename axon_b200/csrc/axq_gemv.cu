@@ -435,23 +435,23 @@ template <int H, int AL> struct RowOf<F_Q4_K, H, AL> { using T = RowQ4K<H, AL>; 
 template <int H, int AL> struct RowOf<F_Q5_K, H, AL> { using T = RowQ5K<H, AL>; };
 template <int H, int AL> struct RowOf<F_Q6_K, H, AL> { using T = RowQ6K<H, AL>; };
 
-// Half CG of NR rows (c0, and c1 when NR = 2) of a K-quant format: every
-// activation run is loaded once and dotted with each row's codes;
+// Half CG of two rows (c0, c1) of a K-quant format: every activation run is
+// loaded once and dotted with both rows' codes;
 // acc[i][t] += row i's part.  Formats whose runs are 16 elements and whose
 // code words are shared by the runs 2s + lh of one lh (Q2_K, Q3_K) decode
 // lh-major: the words of one lh are loaded (and merged) once, then its four
 // runs follow, so only those words are live.
-template <int F, int H, int AL, int NT, int NR>
+template <int F, int H, int AL, int NT>
 __device__ __forceinline__ void kquant_half(const uint8_t* c0, const uint8_t* c1, const ActCG& X, int ntok,
                                             bool valid, float (*acc)[NT]) {
     using Row = typename RowOf<F, H, AL>::T;
     constexpr int RL = Row::RL, NW = RL / 4, NRUN = 128 / RL;
     constexpr bool LHM = Row::LH_MAJOR;
     static_assert(!LHM || RL == 16, "lh-major order is for 16-element runs");
-    static_assert(NR == 1 || NR == 2, "one or two rows per lane");
+    constexpr int NR = 2;  // rows per lane
     Row r[NR];
     r[0].load(c0);
-    if constexpr (NR == 2) r[1].load(c1);
+    r[1].load(c1);
     // Q6_K decodes from shared memory per run and keeps more live values: a
     // shallower activation prefetch keeps it inside the register budget
     ActPipe<NT, true, H, (F == F_Q6_K) ? 2 : 3, LHM> P(X, ntok);
@@ -593,15 +593,11 @@ template <int F> struct Lane {
     static constexpr int CGB = (F == F_Q8_0) ? 8 * 34 : (F == F_Q4_0) ? 8 * 18 : Traits<F>::BB;
     static constexpr int A = (F == F_Q2_K) ? 4 : (F == F_Q4_K || F == F_Q5_K) ? 16 : 1;
     static constexpr int PERM = (F == F_Q4_0) ? 1 : 0;
-    template <int H, int AL, int NT, int NR>
+    template <int H, int AL, int NT>
     __device__ __forceinline__ static void half(const uint8_t* c0, const uint8_t* c1, int nblk_valid, const ActCG& X,
                                                 int ntok, bool valid, float (*acc)[NT]) {
-        if constexpr (F == F_Q8_0 || F == F_Q4_0) {
-            static_assert(NR == 2, "the 32-element block formats decode two rows per lane");
-            block32_half<F, H, NT>(c0, c1, nblk_valid, X, ntok, valid, acc);
-        } else {
-            kquant_half<F, H, AL, NT, NR>(c0, c1, X, ntok, valid, acc);
-        }
+        if constexpr (F == F_Q8_0 || F == F_Q4_0) block32_half<F, H, NT>(c0, c1, nblk_valid, X, ntok, valid, acc);
+        else kquant_half<F, H, AL, NT>(c0, c1, X, ntok, valid, acc);
     }
 };
 
@@ -1109,38 +1105,22 @@ __device__ __forceinline__ void consume_mma(const GemvArgs& a, uint8_t* stages, 
     }
 }
 
-// Rows decoded per lane: two (each activation run a lane loads serves two
-// rows) or one, which keeps the multi-token decode's activation runs and
-// per-token sums inside the register budget where two rows spilled.  The
-// one-row cases are those measured faster at W[28672 x 8192] (Q3_K and Q5_K
-// at four tokens: 123 vs 136 and 109 vs 132 us; Q6_K at two: 77 vs 100 us);
-// elsewhere two rows won.  Host and device agree through this function.
-template <int F, int NT>
-__host__ __device__ constexpr int rows_per_lane() {
-    return ((NT == 4 && (F == F_Q3_K || F == F_Q5_K)) || (NT == 2 && F == F_Q6_K)) ? 1 : 2;
-}
-
 // Consumer warps of one half H (warps 4H..4H+3) over every unit of this CTA:
-// wait for each stage, decode the lane's half CGs, release the stage; per
+// wait for each stage, decode the lane's half CG, release the stage; per
 // unit, combine the partial sums across lanes and warps and store the
-// outputs (or, for peer-store calls, every rank's copy).
-//  NR = 2: lane l takes CG slot 4(w%4) + l/8 of the stage for rows l%8 and
-//          l%8 + 8 of the unit.
-//  NR = 1: lane l takes CG slots 2(w%4) + l/16 and that + 8 for row l%16.
-template <int F, int NT, int AL, int H, int NR>
+// outputs (or, for peer-store calls, every rank's copy).  Lane l takes CG
+// slot 4(w%4) + l/8 of the stage for rows l%8 and l%8 + 8 of the unit, so
+// each activation run it loads serves two rows.
+template <int F, int NT, int AL, int H>
 __device__ __forceinline__ void consume(const GemvArgs& a, uint8_t* stages, float* red, uint64_t* full,
                                         uint64_t* empty, volatile int* abort_flag, int warp, int lane) {
     using L = Lane<F>;
     static_assert((kStageCG * L::CGB) % 16 == 0, "a K-step must keep row segments' 16-byte phase");
-    constexpr int NCG = 2 / NR;  // CG slots per lane per stage
-    constexpr int kSlotStep = kStageCG / 2;
-    const int cgl = NR == 2 ? 4 * (warp & 3) + (lane >> 3) : 2 * (warp & 3) + (lane >> 4);
-    const int pr = NR == 2 ? (lane & 7) : (lane & 15);  // first stage row of the lane
-    float acc[NR][NT];
+    const int cgl = 4 * (warp & 3) + (lane >> 3);  // CG slot in the stage
+    const int pr = lane & 7;                        // rows pr and pr + 8 of the unit
+    float acc[2][NT];
 #pragma unroll
-    for (int i = 0; i < NR; ++i)
-#pragma unroll
-        for (int t = 0; t < NT; ++t) acc[i][t] = 0.0f;
+    for (int t = 0; t < NT; ++t) acc[0][t] = acc[1][t] = 0.0f;
     int s = 0, unit_par = 0;
     uint32_t phase = 0;
     // peer-store calls: this call's copy of every rank's landing area
@@ -1150,7 +1130,7 @@ __device__ __forceinline__ void consume(const GemvArgs& a, uint8_t* stages, floa
     const uintptr_t base0 = slot_base(a, pr), base1 = slot_base(a, pr + 8);
     for (int64_t u = blockIdx.x; u < a.units; u += gridDim.x, unit_par ^= 1) {
         const int64_t row0 = slot_row(a, u, pr), row1 = slot_row(a, u, pr + 8);
-        const bool ok0 = row0 < a.rows, ok1 = NR == 2 && row1 < a.rows;
+        const bool ok0 = row0 < a.rows, ok1 = row1 < a.rows;
         // Each row segment sits in its stage row at the segment's offset
         // modulo 16 (the bulk copy starts at the 16-byte boundary below it);
         // K-steps advance by step_bytes, a multiple of 16, so the offset is
@@ -1161,7 +1141,6 @@ __device__ __forceinline__ void consume(const GemvArgs& a, uint8_t* stages, floa
         // a row past the end decodes row0 again; its sum is never written
         const uint8_t* stage_lane1 = ok1 ? stages + cgl * L::CGB + (pr + 8) * a.rs + mis1 : stage_lane0;
         const uint8_t* act = a.act + static_cast<int64_t>(cgl) * a.act_cg_stride;
-        const uint8_t* act_last = a.act + static_cast<int64_t>(a.ncg - 1) * a.act_cg_stride;
         int cg = cgl, nbv = a.nblk_row - cgl * 8;
         for (int ks = 0; ks < a.nks; ++ks, cg += kStageCG, nbv -= kStageCG * 8, act += kStageCG * a.act_cg_stride) {
             if (!aborted && !wait_or_abort(&full[s], phase, abort_flag)) {
@@ -1171,19 +1150,17 @@ __device__ __forceinline__ void consume(const GemvArgs& a, uint8_t* stages, floa
                     atomicExch(a.err, 1);
                 }
             }
-#pragma unroll 1
-            for (int c = 0; c < NCG; ++c) {
+            {
                 // Every lane decodes (no divergent branch around the decode):
                 // a lane whose row is past the end or whose CG is past the row
                 // reads stale stage bytes and the last CG's activations, and
                 // its sums are dropped (valid = false).
-                const int cgc = cg + c * kSlotStep;
-                const bool valid = ok0 && cgc < a.ncg && !aborted;
-                const int sb = s * a.stage_bytes + c * kSlotStep * L::CGB;
+                const bool valid = ok0 && cg < a.ncg && !aborted;
+                const int sb = s * a.stage_bytes;
                 const uint8_t* c0 = stage_lane0 + sb;
                 const uint8_t* c1 = stage_lane1 + sb;
-                const uint8_t* xa = cgc < a.ncg ? act + static_cast<int64_t>(c * kSlotStep) * a.act_cg_stride : act_last;
-                L::template half<H, AL, NT, NR>(c0, c1, nbv - c * kSlotStep * 8, ActCG{xa}, a.ntok, valid, acc);
+                const uint8_t* xa = cg < a.ncg ? act : a.act + static_cast<int64_t>(a.ncg - 1) * a.act_cg_stride;
+                L::template half<H, AL, NT>(c0, c1, nbv, ActCG{xa}, a.ntok, valid, acc);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
@@ -1192,16 +1169,16 @@ __device__ __forceinline__ void consume(const GemvArgs& a, uint8_t* stages, floa
                 phase ^= 1;
             }
         }
-        // combine the CG slots of each warp, then the warps
+        // combine the four CG slots of each warp, then the warps
         float* rp = red + unit_par * (kConsumerWarps * kUnitRows * NT);
 #pragma unroll
-        for (int i = 0; i < NR; ++i) {
+        for (int i = 0; i < 2; ++i) {
 #pragma unroll
             for (int t = 0; t < NT; ++t) {
                 float v = acc[i][t];
-                if constexpr (NR == 2) v += __shfl_xor_sync(0xffffffffu, v, 8);
+                v += __shfl_xor_sync(0xffffffffu, v, 8);
                 v += __shfl_xor_sync(0xffffffffu, v, 16);
-                if (lane < 16 / NR) rp[(warp * kUnitRows + pr + 8 * i) * NT + t] = v;
+                if (lane < 8) rp[(warp * kUnitRows + pr + 8 * i) * NT + t] = v;
                 acc[i][t] = 0.0f;
             }
         }
@@ -1300,9 +1277,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
     if constexpr (MMA) {
         consume_mma<F, NT / 4, AL>(a, stages, red, full, empty, abort_flag, warp, lane);
     } else {
-        constexpr int NR = rows_per_lane<F, NT>();
-        if (warp < 4) consume<F, NT, AL, 0, NR>(a, stages, red, full, empty, abort_flag, warp, lane);
-        else consume<F, NT, AL, 1, NR>(a, stages, red, full, empty, abort_flag, warp, lane);
+        if (warp < 4) consume<F, NT, AL, 0>(a, stages, red, full, empty, abort_flag, warp, lane);
+        else consume<F, NT, AL, 1>(a, stages, red, full, empty, abort_flag, warp, lane);
     }
 }
 
@@ -1346,15 +1322,31 @@ cudaError_t launch_nt(const GemvPlan& p, const GemvArgs& a, cudaStream_t s) {
 template <int F>
 constexpr bool kHasMma = (F != F_Q8_0 && F != F_Q4_0);
 
+// Whether N tokens of format F take the MMA kernel: 2..8 tokens of a K-quant
+// format, except two tokens of Q2_K and Q4_K, where the dp4a kernel measured
+// faster (32 vs 37 and 34 vs 38 us at W[28672 x 8192]; three or four tokens:
+// the MMA kernel 2.1-2.7x faster).  Q8_0 / Q4_0 take the dp4a kernel, four
+// tokens at a time.
+template <int F>
+bool use_mma(int64_t N) {
+    return kHasMma<F> && N >= 2 && !(N == 2 && (F == F_Q2_K || F == F_Q4_K));
+}
+
+// Only the (token count, kernel) pairs use_mma can select are instantiated.
 template <int F, int AL>
 cudaError_t launch_al(const GemvPlan& p, const GemvArgs& a, int nt, bool mma, cudaStream_t s) {
     if constexpr (kHasMma<F>) {
         if (mma) return nt <= 4 ? launch_nt<F, 4, AL, true>(p, a, s) : launch_nt<F, 8, AL, true>(p, a, s);
-    }
-    switch (nt) {
-        case 1: return launch_nt<F, 1, AL, false>(p, a, s);
-        case 2: return launch_nt<F, 2, AL, false>(p, a, s);
-        default: return launch_nt<F, 4, AL, false>(p, a, s);
+        if constexpr (F == F_Q2_K || F == F_Q4_K) {
+            if (nt == 2) return launch_nt<F, 2, AL, false>(p, a, s);
+        }
+        return nt == 1 ? launch_nt<F, 1, AL, false>(p, a, s) : cudaErrorInvalidValue;
+    } else {
+        switch (nt) {
+            case 1: return launch_nt<F, 1, AL, false>(p, a, s);
+            case 2: return launch_nt<F, 2, AL, false>(p, a, s);
+            default: return launch_nt<F, 4, AL, false>(p, a, s);
+        }
     }
 }
 
@@ -1404,12 +1396,8 @@ cudaError_t launch_gemv(const void* w, const void* w2, const float* x, float* ou
     const bool aligned = (reinterpret_cast<uintptr_t>(w) % 16 == 0) && (a.rb % 16 == 0) &&
                          (reinterpret_cast<uintptr_t>(w2) % 16 == 0);
     const int sms = device_sm_count();
-    // one token: the dp4a kernel; 2..8 tokens of a K-quant format: the MMA
-    // kernel (4 or 8 token slots), except two tokens of Q2_K and Q4_K, where
-    // the dp4a kernel measured faster (32 vs 37 and 34 vs 38 us at
-    // W[28672 x 8192]; three or four tokens: the MMA kernel 2.1-2.7x
-    // faster); Q8_0 / Q4_0: the dp4a kernel, 4 tokens at a time
-    const bool mma = kHasMma<F> && N >= 2 && !(N == 2 && (F == F_Q2_K || F == F_Q4_K));
+    // one token: the dp4a kernel; more: see use_mma (4 or 8 token slots)
+    const bool mma = use_mma<F>(N);
     const int64_t per_launch = mma ? kGemvMmaMaxN : kGemvMaxN;
     for (int64_t t0 = 0; t0 < N; t0 += per_launch) {
         const int nt_run = static_cast<int>(std::min<int64_t>(per_launch, N - t0));
