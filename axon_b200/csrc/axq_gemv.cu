@@ -800,83 +800,82 @@ __device__ __forceinline__ uint32_t ld1(const uint8_t* p) {
     return w[0];
 }
 
-// MmaRow<F, H, AL>: half H of one row's K-quant block for lane word i:
-// load(cg, i) reads the block header, run<J>(q, sc, m) gives word i of the
-// 16-element run J (elements 128H + 16J + 4i..+3) with the run's integer
-// scale and offset weight, in the conventions of the Row decoders above.
-template <int H, int AL> struct MmaQ2K {
+// MmaRow<F, AL>: one row's K-quant block for lane word i: load(cg, i)
+// decodes the block header (scales, d, dmin) once per column group;
+// run<H, J>(q, sc, m) gives word i of the 16-element run J of half H
+// (elements 128H + 16J + 4i..+3) with the run's integer scale and offset
+// weight, in the conventions of the Row decoders above.
+template <int AL> struct MmaQ2K {
     static constexpr int RL = 16;
     static constexpr bool LH_MAJOR = true;
-    uint32_t hd, scw[2], mw[2], w;
+    uint32_t hd, scw[4], mw[4], w;
     const uint8_t* p;
     __device__ __forceinline__ void load(const uint8_t* cg, int i) {
-        uint32_t h[1], sc[2];
+        uint32_t h[1], sc[4];
         ldw<1, AL>(cg, h);
-        ldw<2, AL>(cg + 4 + 8 * H, sc);
+        ldw<4, AL>(cg + 4, sc);
         hd = h[0];
 #pragma unroll
-        for (int v = 0; v < 2; ++v) {
+        for (int v = 0; v < 4; ++v) {
             scw[v] = sc[v] & 0x0F0F0F0Fu;
             mw[v] = (sc[v] >> 4) & 0x0F0F0F0Fu;
         }
         p = cg + 4 * i;
     }
-    template <int LH>
+    template <int H, int LH>
     __device__ __forceinline__ void prep() { w = ld1<AL>(p + 20 + 32 * H + 16 * LH); }
-    template <int J>
+    template <int H, int J>
     __device__ __forceinline__ void run(uint32_t& q, int& sc, int& m) const {
-        constexpr int s = J >> 1;
+        constexpr int s = J >> 1, B = 8 * H + J;  // B: scale byte of the run
         q = w & (0x03030303u << (2 * s));
-        sc = static_cast<int>(__byte_perm(scw[J >> 2], 0u, 0x4440u | (J & 3))) << (6 - 2 * s);
-        m = static_cast<int>(__byte_perm(mw[J >> 2], 0u, 0x4440u | (J & 3)));
+        sc = static_cast<int>(__byte_perm(scw[B >> 2], 0u, 0x4440u | (B & 3))) << (6 - 2 * s);
+        m = static_cast<int>(__byte_perm(mw[B >> 2], 0u, 0x4440u | (B & 3)));
     }
     __device__ __forceinline__ float dscale() const { return h2f_flush(hd & 0xFFFFu) * (1.0f / 64.0f); }
     __device__ __forceinline__ float mscale() const { return h2f_flush(hd >> 16); }
 };
 
-template <int H, int AL> struct MmaQ3K {
+template <int AL> struct MmaQ3K {
     static constexpr int RL = 16;
     static constexpr bool LH_MAJOR = true;
-    uint32_t hd, sv[2], wa, wb;
+    uint32_t hd, sv[4], wa, wb;  // sv[2H..2H+1]: 4 * (scale - 32) of half H's eight runs
     const uint8_t* p;
     __device__ __forceinline__ void load(const uint8_t* cg, int i) {
         uint32_t h[1], s12[3];
         ld_words<1>(cg + 108, h);
         hd = h[0];
         ld_words<3>(cg + 96, s12);
-        uint32_t s6[2];
-        if constexpr (H == 0) {
-            s6[0] = (s12[0] & 0x0F0F0F0Fu) | ((s12[2] << 4) & 0x30303030u);
-            s6[1] = (s12[1] & 0x0F0F0F0Fu) | ((s12[2] << 2) & 0x30303030u);
-        } else {
-            s6[0] = ((s12[0] >> 4) & 0x0F0F0F0Fu) | (s12[2] & 0x30303030u);
-            s6[1] = ((s12[1] >> 4) & 0x0F0F0F0Fu) | ((s12[2] >> 2) & 0x30303030u);
-        }
+        uint32_t s6[4];
+        s6[0] = (s12[0] & 0x0F0F0F0Fu) | ((s12[2] << 4) & 0x30303030u);
+        s6[1] = (s12[1] & 0x0F0F0F0Fu) | ((s12[2] << 2) & 0x30303030u);
+        s6[2] = ((s12[0] >> 4) & 0x0F0F0F0Fu) | (s12[2] & 0x30303030u);
+        s6[3] = ((s12[1] >> 4) & 0x0F0F0F0Fu) | ((s12[2] >> 2) & 0x30303030u);
 #pragma unroll
-        for (int v = 0; v < 2; ++v) sv[v] = (s6[v] ^ 0x20202020u) << 2;
+        for (int v = 0; v < 4; ++v) sv[v] = (s6[v] ^ 0x20202020u) << 2;
         p = cg + 4 * i;
     }
-    template <int LH>
+    template <int H, int LH>
     __device__ __forceinline__ void prep() {
         const uint32_t hm = ld1<1>(p + 16 * LH);
         const uint32_t w = ld1<1>(p + 32 + 32 * H + 16 * LH);
         wa = bsel(0x33333333u, w, bsel(0x0F0F0F0Fu, shl<2 - 4 * H>(hm), shl<4 - 4 * H>(hm)));
         wb = bsel(0x33333333u, w >> 2, bsel(0x0F0F0F0Fu, shl<1 - 4 * H>(hm), shl<3 - 4 * H>(hm)));
     }
-    template <int J>
+    template <int H, int J>
     __device__ __forceinline__ void run(uint32_t& q, int& sc, int& m) const {
         constexpr int s = J >> 1;
         constexpr uint32_t MASK = (s >= 2) ? 0x70707070u : 0x07070707u;
         q = ((s & 1) ? wb : wa) & MASK;
-        m = sext_byte<J & 3>(sv[J >> 2]);
+        m = sext_byte<J & 3>(sv[2 * H + (J >> 2)]);
         sc = (s < 2) ? (m << 4) : m;
     }
     __device__ __forceinline__ float dscale() const { return h2f_flush(hd & 0xFFFFu) * (1.0f / 64.0f); }
     __device__ __forceinline__ float mscale() const { return h2f_flush(hd & 0xFFFFu); }
 };
 
-// Q4_K / Q5_K: 16-element run J = 2(G - 4H) + sub is half `sub` of group G.
-template <int H, int AL> struct MmaQ4K {
+// Q4_K / Q5_K: 16-element run J of half H is half `sub` = J & 1 of group
+// G = 4H + J / 2.
+template <int AL> struct MmaQ4K {
     static constexpr int RL = 32;
     static constexpr bool LH_MAJOR = false;
     uint32_t hw[4];
@@ -885,7 +884,7 @@ template <int H, int AL> struct MmaQ4K {
         ldw<4, AL>(cg, hw);
         p = cg + 4 * i;
     }
-    template <int J>
+    template <int H, int J>
     __device__ __forceinline__ void run(uint32_t& q, int& sc, int& m) const {
         constexpr int G = 4 * H + (J >> 1), sub = J & 1;
         const uint32_t w = ld1<AL>(p + 16 + 32 * (G >> 1) + 16 * sub);
@@ -898,7 +897,7 @@ template <int H, int AL> struct MmaQ4K {
     __device__ __forceinline__ float mscale() const { return h2f_flush(hw[0] >> 16); }
 };
 
-template <int H, int AL> struct MmaQ5K {
+template <int AL> struct MmaQ5K {
     static constexpr int RL = 32;
     static constexpr bool LH_MAJOR = false;
     uint32_t hw[4];
@@ -907,7 +906,7 @@ template <int H, int AL> struct MmaQ5K {
         ldw<4, AL>(cg, hw);
         p = cg + 4 * i;
     }
-    template <int J>
+    template <int H, int J>
     __device__ __forceinline__ void run(uint32_t& q, int& sc, int& m) const {
         constexpr int G = 4 * H + (J >> 1), sub = J & 1;
         const uint32_t qh = ld1<AL>(p + 16 + 16 * sub);
@@ -920,115 +919,121 @@ template <int H, int AL> struct MmaQ5K {
     __device__ __forceinline__ float mscale() const { return h2f_flush(hw[0] >> 16); }
 };
 
-template <int H, int AL> struct MmaQ6K {
+template <int AL> struct MmaQ6K {
     static constexpr int RL = 16;
     static constexpr bool LH_MAJOR = false;
-    uint32_t hd, sc2[2];
+    uint32_t hd, sc4[4];
     const uint8_t* p;
     __device__ __forceinline__ void load(const uint8_t* cg, int i) {
         uint32_t h[1];
         ld_words<1>(cg + 208, h);
         hd = h[0];
-        ld_words<2>(cg + 192 + 8 * H, sc2);
+        ld_words<4>(cg + 192, sc4);
         p = cg + 4 * i;
     }
-    template <int J>
+    template <int H, int J>
     __device__ __forceinline__ void run(uint32_t& q, int& sc, int& m) const {
         constexpr int T = J >> 1, lh = J & 1;
         const uint32_t src = ld1<1>(p + 64 * H + 32 * (T & 1) + 16 * lh);
         const uint32_t hb = ld1<1>(p + 128 + 32 * H + 16 * lh);
         const uint32_t nib = (T & 2) ? (src >> 4) : src;
         q = (nib & 0x0F0F0F0Fu) | (shl<4 - 2 * T>(hb) & 0x30303030u);
-        sc = m = static_cast<int>(static_cast<int8_t>(bt<J>(sc2)));
+        sc = m = static_cast<int>(static_cast<int8_t>(bt<8 * H + J>(sc4)));
     }
     __device__ __forceinline__ float dscale() const { return h2f_flush(hd & 0xFFFFu); }
     __device__ __forceinline__ float mscale() const { return h2f_flush(hd & 0xFFFFu) * 32.0f; }
 };
 
-template <int F, int H, int AL> struct MmaRowOf;
-template <int H, int AL> struct MmaRowOf<F_Q2_K, H, AL> { using T = MmaQ2K<H, AL>; };
-template <int H, int AL> struct MmaRowOf<F_Q3_K, H, AL> { using T = MmaQ3K<H, AL>; };
-template <int H, int AL> struct MmaRowOf<F_Q4_K, H, AL> { using T = MmaQ4K<H, AL>; };
-template <int H, int AL> struct MmaRowOf<F_Q5_K, H, AL> { using T = MmaQ5K<H, AL>; };
-template <int H, int AL> struct MmaRowOf<F_Q6_K, H, AL> { using T = MmaQ6K<H, AL>; };
+template <int F, int AL> struct MmaRowOf;
+template <int AL> struct MmaRowOf<F_Q2_K, AL> { using T = MmaQ2K<AL>; };
+template <int AL> struct MmaRowOf<F_Q3_K, AL> { using T = MmaQ3K<AL>; };
+template <int AL> struct MmaRowOf<F_Q4_K, AL> { using T = MmaQ4K<AL>; };
+template <int AL> struct MmaRowOf<F_Q5_K, AL> { using T = MmaQ5K<AL>; };
+template <int AL> struct MmaRowOf<F_Q6_K, AL> { using T = MmaQ6K<AL>; };
 
-// Half H of one CG for rows g (c0) and g + 8 (c1) of the unit and NG groups
-// of four tokens.  X: records of this CG; bofs[grp] = offset of this lane's
-// B-fragment bytes (token (g >> 1) + 4grp, term g & 1, elements 4i..);
-// tofs[grp] = record of token i + 4grp (the lane's D columns).  The half's
-// activation fragments and run sums are loaded before any decode, so their
-// latency overlaps the MMAs.  32-element runs (Q4_K, Q5_K) take one k = 32
-// MMA each; 16-element runs one k = 16 MMA.
-template <int F, int H, int AL, int NG>
-__device__ __forceinline__ void mma_half(const uint8_t* c0, const uint8_t* c1, const uint8_t* X, const int* bofs,
-                                         const int* tofs, int i, float (*acc)[NG]) {
-    using R = typename MmaRowOf<F, H, AL>::T;
+// One CG for rows g (c0) and g + 8 (c1) of the unit and NG groups of four
+// tokens: the rows' block headers are decoded once, then each half in turn.
+// X: records of this CG; bofs[grp] = offset of this lane's B-fragment bytes
+// (token (g >> 1) + 4grp, term g & 1, elements 4i..); tofs[grp] = record of
+// token i + 4grp (the lane's D columns).  A half's activation fragments and
+// run sums are loaded before its decode, so their latency overlaps the
+// MMAs.  32-element runs (Q4_K, Q5_K) take one k = 32 MMA each; 16-element
+// runs one k = 16 MMA.  Integer sums are converted to fp32 once per half.
+template <int F, int AL, int NG>
+__device__ __forceinline__ void mma_cg(const uint8_t* c0, const uint8_t* c1, const uint8_t* X, const int* bofs,
+                                       const int* tofs, int i, float (*acc)[NG]) {
+    using R = typename MmaRowOf<F, AL>::T;
     constexpr bool LHM = R::LH_MAJOR;
     constexpr int NRUN = 128 / R::RL;
-    uint32_t bv[8][NG];
-    int sxv[NRUN][NG];
-    float uv[NG];
-#pragma unroll
-    for (int grp = 0; grp < NG; ++grp) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) bv[j][grp] = __ldg(reinterpret_cast<const uint32_t*>(X + bofs[grp] + 16 * (8 * H + j)));
-#pragma unroll
-        for (int j = 0; j < NRUN; ++j) {
-            const int* sp = reinterpret_cast<const int*>(X + tofs[grp] + 512) + 8 * H;
-            sxv[j][grp] = (R::RL == 32) ? __ldg(sp + 2 * j) + __ldg(sp + 2 * j + 1) : __ldg(sp + j);
-        }
-        uv[grp] = __ldg(reinterpret_cast<const float*>(X + tofs[grp] + 576));
-    }
     R r0, r1;
     r0.load(c0, i);
     r1.load(c1, i);
-    int hs[2][NG], ls[2][NG], ms[2][NG];
-#pragma unroll
-    for (int grp = 0; grp < NG; ++grp) hs[0][grp] = hs[1][grp] = ls[0][grp] = ls[1][grp] = ms[0][grp] = ms[1][grp] = 0;
-    static_for<NRUN>([&](auto Kc) {
-        constexpr int K = decltype(Kc)::value;
-        constexpr int J = LHM ? 2 * (K & 3) + (K >> 2) : K;  // run of the half (16 or 32 elements)
-        if constexpr (LHM) {
-            if constexpr ((K & 3) == 0) {
-                r0.template prep<(K >> 2)>();
-                r1.template prep<(K >> 2)>();
-            }
-        }
-        int sc0, m0, sc1, m1;
-        uint32_t q0, q1;
-        [[maybe_unused]] uint32_t q2 = 0, q3 = 0;  // second half of a 32-element run
-        if constexpr (R::RL == 32) {
-            r0.template run<2 * J>(q0, sc0, m0);
-            r1.template run<2 * J>(q1, sc1, m1);
-            r0.template run<2 * J + 1>(q2, sc0, m0);
-            r1.template run<2 * J + 1>(q3, sc1, m1);
-        } else {
-            r0.template run<J>(q0, sc0, m0);
-            r1.template run<J>(q1, sc1, m1);
-        }
+    const float d0 = r0.dscale(), n0 = r0.mscale(), d1 = r1.dscale(), n1 = r1.mscale();
+    static_for<2>([&](auto Hc) {
+        constexpr int H = decltype(Hc)::value;
+        uint32_t bv[8][NG];
+        int sxv[NRUN][NG];
+        float uv[NG];
 #pragma unroll
         for (int grp = 0; grp < NG; ++grp) {
-            int d[4];
-            if constexpr (R::RL == 32) mma16832(q0, q1, q2, q3, bv[2 * J][grp], bv[2 * J + 1][grp], d);
-            else mma16816(q0, q1, bv[J][grp], d);
-            const int sx = sxv[J][grp];
-            hs[0][grp] += sc0 * d[0];
-            ls[0][grp] += sc0 * d[1];
-            ms[0][grp] += m0 * sx;
-            hs[1][grp] += sc1 * d[2];
-            ls[1][grp] += sc1 * d[3];
-            ms[1][grp] += m1 * sx;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                bv[j][grp] = __ldg(reinterpret_cast<const uint32_t*>(X + bofs[grp] + 16 * (8 * H + j)));
+#pragma unroll
+            for (int j = 0; j < NRUN; ++j) {
+                const int* sp = reinterpret_cast<const int*>(X + tofs[grp] + 512) + 8 * H;
+                sxv[j][grp] = (R::RL == 32) ? __ldg(sp + 2 * j) + __ldg(sp + 2 * j + 1) : __ldg(sp + j);
+            }
+            uv[grp] = __ldg(reinterpret_cast<const float*>(X + tofs[grp] + 576));
+        }
+        int hs[2][NG], ls[2][NG], ms[2][NG];
+#pragma unroll
+        for (int grp = 0; grp < NG; ++grp)
+            hs[0][grp] = hs[1][grp] = ls[0][grp] = ls[1][grp] = ms[0][grp] = ms[1][grp] = 0;
+        static_for<NRUN>([&](auto Kc) {
+            constexpr int K = decltype(Kc)::value;
+            constexpr int J = LHM ? 2 * (K & 3) + (K >> 2) : K;  // run of the half (16 or 32 elements)
+            if constexpr (LHM) {
+                if constexpr ((K & 3) == 0) {
+                    r0.template prep<H, (K >> 2)>();
+                    r1.template prep<H, (K >> 2)>();
+                }
+            }
+            int sc0, m0, sc1, m1;
+            uint32_t q0, q1;
+            [[maybe_unused]] uint32_t q2 = 0, q3 = 0;  // second half of a 32-element run
+            if constexpr (R::RL == 32) {
+                r0.template run<H, 2 * J>(q0, sc0, m0);
+                r1.template run<H, 2 * J>(q1, sc1, m1);
+                r0.template run<H, 2 * J + 1>(q2, sc0, m0);
+                r1.template run<H, 2 * J + 1>(q3, sc1, m1);
+            } else {
+                r0.template run<H, J>(q0, sc0, m0);
+                r1.template run<H, J>(q1, sc1, m1);
+            }
+#pragma unroll
+            for (int grp = 0; grp < NG; ++grp) {
+                int d[4];
+                if constexpr (R::RL == 32) mma16832(q0, q1, q2, q3, bv[2 * J][grp], bv[2 * J + 1][grp], d);
+                else mma16816(q0, q1, bv[J][grp], d);
+                const int sx = sxv[J][grp];
+                hs[0][grp] += sc0 * d[0];
+                ls[0][grp] += sc0 * d[1];
+                ms[0][grp] += m0 * sx;
+                hs[1][grp] += sc1 * d[2];
+                ls[1][grp] += sc1 * d[3];
+                ms[1][grp] += m1 * sx;
+            }
+        });
+#pragma unroll
+        for (int grp = 0; grp < NG; ++grp) {
+            const float u = uv[grp];
+            const float dot0 = fmaf(254.0f, static_cast<float>(hs[0][grp]), static_cast<float>(ls[0][grp]));
+            const float dot1 = fmaf(254.0f, static_cast<float>(hs[1][grp]), static_cast<float>(ls[1][grp]));
+            acc[0][grp] = fmaf(u, fmaf(d0, dot0, -n0 * static_cast<float>(ms[0][grp])), acc[0][grp]);
+            acc[1][grp] = fmaf(u, fmaf(d1, dot1, -n1 * static_cast<float>(ms[1][grp])), acc[1][grp]);
         }
     });
-    const float d0 = r0.dscale(), n0 = r0.mscale(), d1 = r1.dscale(), n1 = r1.mscale();
-#pragma unroll
-    for (int grp = 0; grp < NG; ++grp) {
-        const float u = uv[grp];
-        const float dot0 = fmaf(254.0f, static_cast<float>(hs[0][grp]), static_cast<float>(ls[0][grp]));
-        const float dot1 = fmaf(254.0f, static_cast<float>(hs[1][grp]), static_cast<float>(ls[1][grp]));
-        acc[0][grp] = fmaf(u, fmaf(d0, dot0, -n0 * static_cast<float>(ms[0][grp])), acc[0][grp]);
-        acc[1][grp] = fmaf(u, fmaf(d1, dot1, -n1 * static_cast<float>(ms[1][grp])), acc[1][grp]);
-    }
 }
 
 // Consumer warps of the small-batch path: warp w takes CG slots 2w and
@@ -1083,8 +1088,7 @@ __device__ __forceinline__ void consume_mma(const GemvArgs& a, uint8_t* stages, 
                 if (cg < a.ncg && !aborted) {
                     const int off = s * a.stage_bytes + slot * L::CGB;
                     const uint8_t* X = a.act + static_cast<int64_t>(cg) * a.act_cg_stride;
-                    mma_half<F, 0, AL, NG>(srow0 + off, srow1 + off, X, bofs, tofs, i, acc);
-                    mma_half<F, 1, AL, NG>(srow0 + off, srow1 + off, X, bofs, tofs, i, acc);
+                    mma_cg<F, AL, NG>(srow0 + off, srow1 + off, X, bofs, tofs, i, acc);
                 }
             }
             __syncwarp();

@@ -107,16 +107,13 @@ cudaError_t silu_mul_dispatch(const float* g, const float* u, float* h, int64_t 
 
 // Largest N served by the GEMV kernel; larger batches use the GEMM (whose
 // cost barely depends on N below 128, while the GEMV's per-token work grows).
-// The dp4a GEMV takes up to 4 tokens per launch; the K-quant formats' 2..8
-// token path (int8 MMAs, four tokens per MMA) up to 8.  Per format, the
-// GEMV serves the batches where it measured faster than the GEMM at
-// W[28672 x 8192]: up to 8 tokens for Q3_K, Q4_K and Q6_K (8 tokens: 86 vs
-// 106, 70 vs 89, 116 vs 121 us), up to 4 for the others (Q2_K and Q5_K at
-// 8 tokens: 101 vs 97 and 105 vs 102 us).
+// The dp4a GEMV takes up to 4 tokens per launch (Q8_0, Q4_0); the K-quant
+// formats' 2..8 token path (int8 MMAs, four tokens per MMA) up to 8, where
+// it measured faster than the GEMM at W[28672 x 8192] for every K-quant
+// format (8 tokens: Q2_K 86 vs 97, Q3_K 79 vs 106, Q4_K 72 vs 89, Q5_K 84 vs
+// 102, Q6_K 119 vs 121 us).
 constexpr int64_t kGemvMaxN = 4;
 constexpr int64_t kGemvMmaMaxN = 8;
-inline int64_t gemv_max_n(int fmt) {
-    return (fmt == AXQ_Q3_K || fmt == AXQ_Q4_K || fmt == AXQ_Q6_K) ? kGemvMmaMaxN : kGemvMaxN;
-}
+inline int64_t gemv_max_n(int fmt) { return (fmt == AXQ_Q8_0 || fmt == AXQ_Q4_0) ? kGemvMaxN : kGemvMmaMaxN; }
 
 }  // namespace axq
