@@ -1,6 +1,6 @@
 // Quantized GEMV / small-batch matmul: out[M x N] = W_q[M x K] . X[K x N]
-// for N (activation columns, "tokens") of 1..4, HBM-bound on the packed
-// weights.
+// for N (activation columns, "tokens") of 1..8 (1..4 for Q8_0 / Q4_0),
+// HBM-bound on the packed weights.
 //
 // Design (B200-first):
 //  * Warp specialisation: one producer warp streams weight tiles into a ring
@@ -8,10 +8,13 @@
 //    cp.async.bulk + mbarrier complete_tx); eight consumer warps decode and
 //    multiply.  full/empty mbarriers pace the ring; every wait is bounded.
 //  * A stage holds 16 weight rows x 16 column groups (CG = 256 elements: one
-//    K-quant block or eight Q8_0/Q4_0 blocks).  Consumer warp w takes CGs 2w
-//    and 2w+1 of the stage; lane l handles row l%16 of CG 2w + l/16 in full,
-//    so every group/shift index of the decode is a compile-time constant.
-//    Per-row partials are combined across warps once per 16-row unit.
+//    K-quant block or eight Q8_0/Q4_0 blocks).  One token (dp4a path):
+//    consumer warp w takes half w/4 of CGs 4(w%4)..4(w%4)+3 and lane l CG
+//    4(w%4) + l/8 for rows l%8 and l%8 + 8, so every group/shift index of
+//    the decode is a compile-time constant.  Two to eight tokens of a K-quant
+//    format (MMA path): warp w takes CGs 2w and 2w+1 for all 16 rows with
+//    int8 mma.sync, four tokens per MMA.  Per-row partials are combined
+//    across warps once per 16-row unit.
 //  * Packed rows keep the reference's layout and any byte alignment: each
 //    row segment is copied from its 16-byte-rounded range (bytes of the
 //    neighbouring segments ride along), except where that range would leave

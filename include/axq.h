@@ -113,9 +113,10 @@ int axq_linear(int fmt, const void* w_q, const float* x, const float* bias, floa
  * this is the composition SiLU(X W_gate^T) * (X W_up^T) of its matmul):
  *   h = silu(W_gate . B) * (W_up . B)  elementwise, silu(v) = v / (1 + e^-v),
  * W_gate and W_up packed [M x K] in the same format, layouts and flags as
- * axq_matmul (h is [M x N], or [N x M] with AXQ_FLAG_OUT_TOKMAJOR).  Up to 4
- * columns run as one GEMV pass over both matrices; more use two tensor-core
- * GEMMs and an elementwise kernel (scratch included in the workspace). */
+ * axq_matmul (h is [M x N], or [N x M] with AXQ_FLAG_OUT_TOKMAJOR).  Up to 8
+ * columns (4 for Q8_0 and Q4_0) run as one GEMV pass over both matrices; more
+ * use two tensor-core GEMMs and an elementwise kernel (scratch included in
+ * the workspace). */
 size_t axq_gate_up_workspace_size(int fmt, int64_t M, int64_t K, int64_t N);
 int axq_gate_up_silu(int fmt, const void* w_gate, const void* w_up, const float* b, float* h, int64_t M, int64_t K,
                      int64_t N, unsigned flags, void* workspace, size_t workspace_bytes, axq_stream_t stream);
@@ -211,9 +212,10 @@ int axq_symm_destroy(void* symm);
 /* As axq_matmul_sharded, with the output in a symmetric buffer (full
  * [M x N] row-major copy on every rank): for up to 4 columns the GEMV's
  * epilogue stores every output value into each rank's landing area over
- * NVLink and its last CTA signals the ranks; a small kernel then waits
- * (bounded) until every rank has signalled and copies the landing area into
- * this rank's copy — no separate collective.  The landing area has two
+ * NVLink as one 8-byte slot tagged with the call's number (a single-copy
+ * atomic store, so no fence or counter is needed); a small kernel then waits
+ * (bounded) until every slot of the call is tagged and copies the values
+ * into this rank's copy — no separate collective.  The landing area has two
  * copies that alternate by call, so no rank waits for another before its
  * stores; reads of a call's output must be ordered on the call's stream
  * before the call after the next one on the same buffer.  More columns run
