@@ -232,8 +232,8 @@ def matmul_sharded_p2p(out: SymmetricBuffer, a_local: QTensor, b: torch.Tensor, 
                        workspace: Optional[Workspace] = None, stream: Optional[torch.cuda.Stream] = None,
                        wait: bool = True) -> torch.Tensor:
     """As matmul_sharded, into a symmetric buffer: up to 4 columns store every
-    output value straight into each rank's copy from the GEMV epilogue (no
-    separate collective).  Returns this rank's full [M x N] copy.  wait=False
+    output value into each rank's landing copy from the GEMV epilogue, as a
+    slot tagged with the call's number (no separate collective).  Returns this rank's full [M x N] copy.  wait=False
     leaves the completion wait to `out.wait()`, so calls on several buffers
     can be issued back to back."""
     _req_cuda(a_local.data, "a_local.data", torch.uint8)
