@@ -70,3 +70,24 @@ def test_workspace_size_grows_with_tokens():
     b = axon_b200.matmul_workspace_size(F, 4096, 4096, 8)
     assert 0 < a < b
     assert a % 256 == 0 and b % 256 == 0
+
+
+def test_workspace_size_follows_the_gemv_token_range():
+    """Up to 8 tokens of a K-quant format (4 of Q8_0 / Q4_0) take the GEMV,
+    whose workspace is the 256-byte status block plus one 592-byte activation
+    record per 256 elements and token (rounded to 256 bytes); beyond that the
+    GEMM's larger workspace applies."""
+    import axon_b200
+    Q = axon_b200.QuantFormat
+    M, K = 4096, 4096
+
+    def gemv_bytes(n):
+        return 256 + -(-(K // 256) * n * 592 // 256) * 256
+
+    for f in (Q.Q2_K, Q.Q3_K, Q.Q4_K, Q.Q5_K, Q.Q6_K):
+        for n in (1, 2, 5, 8):
+            assert axon_b200.matmul_workspace_size(f, M, K, n) == gemv_bytes(n), (f, n)
+        assert axon_b200.matmul_workspace_size(f, M, K, 9) != gemv_bytes(9), f
+    for f in (Q.Q8_0, Q.Q4_0):
+        assert axon_b200.matmul_workspace_size(f, M, K, 4) == gemv_bytes(4), f
+        assert axon_b200.matmul_workspace_size(f, M, K, 5) != gemv_bytes(5), f
